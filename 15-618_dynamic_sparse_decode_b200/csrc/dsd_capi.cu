@@ -1,0 +1,1024 @@
+// dsd_capi.cu -- the C ABI (include/dsd_b200.h) over the sm_100a kernels.
+//
+// A context is one GPU's share of the decode service: its page pool, the
+// per-step scratch (sized once at creation; a step allocates nothing), one
+// stream, pinned staging for the packed per-step H2D/D2H copies, the device
+// request page tables and a host mirror of those tables.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <map>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "dsd_b200.h"
+#include "dsd_kernels.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+struct DsdError {
+  int code;
+  std::string msg;
+};
+
+[[noreturn]] void Fail(int code, const std::string& msg) { throw DsdError{code, msg}; }
+
+void Check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    Fail(DSD_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  }
+}
+
+template <typename F>
+int Guard(F&& f) {
+  try {
+    f();
+    return DSD_OK;
+  } catch (const DsdError& e) {
+    g_last_error = e.msg;
+    return e.code;
+  } catch (const std::bad_alloc&) {
+    g_last_error = "host allocation failed";
+    return DSD_ENOMEM;
+  } catch (const std::exception& e) {
+    g_last_error = e.what();
+    return DSD_EINVAL;
+  }
+}
+
+constexpr size_t kLargeCopyBytes = size_t(1) << 20;  // DeviceTransferStats "large" threshold
+
+template <typename T>
+T* DeviceAlloc(size_t count, const char* what) {
+  void* p = nullptr;
+  const size_t bytes = std::max<size_t>(1, count) * sizeof(T);
+  const cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    Fail(DSD_ENOMEM, std::string("cudaMalloc failed for ") + what + " (" +
+                         std::to_string(bytes) + " bytes): " + cudaGetErrorString(e));
+  }
+  return static_cast<T*>(p);
+}
+
+template <typename T>
+T* PinnedAlloc(size_t count, const char* what) {
+  void* p = nullptr;
+  const cudaError_t e = cudaMallocHost(&p, std::max<size_t>(1, count) * sizeof(T));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    Fail(DSD_ENOMEM, std::string("cudaMallocHost failed for ") + what);
+  }
+  return static_cast<T*>(p);
+}
+
+size_t AlignUp(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace
+
+struct dsd_ctx {
+  int device = 0;
+  dsd_model_config cfg{};
+  dsd_ctx_options opt{};
+  int ept = 0;
+  int num_sms = 0;
+  int slots_tmpl = 1;  // attention register slots (E/4/256 rounded up to 1,2,4,8)
+  int tps = 1;         // tokens per attention stage
+  size_t attn_smem = 0;
+  float scale = 0.f;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev[6] = {};
+
+  // pool
+  float* k_pool = nullptr;
+  float* v_pool = nullptr;
+  float* summaries = nullptr;
+  int* token_counts = nullptr;
+  uint8_t* live = nullptr;
+  std::vector<int> host_counts;  // mirror of token_counts for validation
+
+  // request page tables
+  int* table = nullptr;
+  int* table_n = nullptr;
+  std::unordered_map<int, int> slot_of;
+  std::vector<int> free_slots;
+  std::vector<std::vector<int>> slot_pages;
+
+  // per-step buffers.  step_in = [hdr 4 ints][req max_batch+1 ints][pad][queries][cand ids]
+  size_t in_req_off = 0, in_q_off = 0, in_ids_off = 0, in_bytes = 0;
+  unsigned char* d_in = nullptr;
+  unsigned char* h_in = nullptr;  // pinned
+  float* d_scores = nullptr;
+  int* d_selected = nullptr;
+  float* d_outputs = nullptr;
+  float* d_part_acc = nullptr;
+  float* d_part_ml = nullptr;
+  int* d_planbuf = nullptr;
+  int* d_status = nullptr;
+  dsdk::StepPlan plan{};
+  float* h_outputs = nullptr;   // pinned D2H staging
+  float* h_scores = nullptr;
+  int* h_selected = nullptr;
+  int* h_status = nullptr;
+
+  // staging for uploads / appends (grow only, admission time)
+  unsigned char* d_stage = nullptr;
+  size_t d_stage_bytes = 0;
+
+  // bound (device-resident) steps
+  int bound_batch = -1;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t graph_exec = nullptr;
+  const float* graph_q = nullptr;
+  float* graph_out = nullptr;
+
+  dsd_transfer_stats stats{};
+};
+
+namespace {
+
+void CountH2D(dsd_ctx* c, size_t bytes) {
+  c->stats.h2d_bytes += bytes;
+  c->stats.h2d_calls += 1;
+  if (bytes >= kLargeCopyBytes) c->stats.h2d_large_calls += 1;
+}
+void CountD2H(dsd_ctx* c, size_t bytes) {
+  c->stats.d2h_bytes += bytes;
+  c->stats.d2h_calls += 1;
+  if (bytes >= kLargeCopyBytes) c->stats.d2h_large_calls += 1;
+}
+
+void H2D(dsd_ctx* c, void* dst, const void* src, size_t bytes) {
+  if (bytes == 0) return;
+  Check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, c->stream), "H2D copy");
+  CountH2D(c, bytes);
+}
+void D2H(dsd_ctx* c, void* dst, const void* src, size_t bytes) {
+  if (bytes == 0) return;
+  Check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, c->stream), "D2H copy");
+  CountD2H(c, bytes);
+}
+
+void Sync(dsd_ctx* c) { Check(cudaStreamSynchronize(c->stream), "stream synchronize"); }
+
+void SetDevice(dsd_ctx* c) { Check(cudaSetDevice(c->device), "cudaSetDevice"); }
+
+void EnsureStage(dsd_ctx* c, size_t bytes) {
+  if (bytes <= c->d_stage_bytes) return;
+  Sync(c);
+  if (c->d_stage) cudaFree(c->d_stage);
+  c->d_stage = nullptr;
+  c->d_stage_bytes = 0;
+  c->d_stage = DeviceAlloc<unsigned char>(bytes, "staging buffer");
+  c->d_stage_bytes = bytes;
+}
+
+void ValidatePage(const dsd_ctx* c, int page) {
+  if (page < 0 || page >= c->opt.capacity_pages) Fail(DSD_ERANGE, "invalid page id");
+}
+
+// Reads the kernel status word after a synchronisation and clears it.
+void CheckStatus(dsd_ctx* c) {
+  Check(cudaMemcpyAsync(c->h_status, c->d_status, sizeof(int), cudaMemcpyDeviceToHost, c->stream),
+        "status read");
+  Sync(c);
+  const int s = *c->h_status;
+  if (s != 0) {
+    Check(cudaMemsetAsync(c->d_status, 0, sizeof(int), c->stream), "status clear");
+    Sync(c);
+    if (s & dsdk::kStatusTimeout) Fail(DSD_ETIMEOUT, "a device-side wait exceeded its budget");
+    Fail(DSD_EINVAL, "device kernels rejected the step input (status " + std::to_string(s) + ")");
+  }
+}
+
+// ------------------------------------------------------------------ step
+
+void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed) {
+  const dsdk::StepPlan& plan = c->plan;
+  const int target_units = 8 * c->num_sms;
+  if (timed) Check(cudaEventRecord(c->ev[0], c->stream), "event");
+  dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, c->stream>>>(plan, c->cfg.top_k_pages,
+                                                             target_units);
+  dsdk::score_kernel<<<2 * c->num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, c->stream>>>(
+      plan, d_q, c->summaries, c->ept, c->scale, c->d_scores);
+  if (timed) Check(cudaEventRecord(c->ev[1], c->stream), "event");
+  const int sel_grid = std::max(1, std::min(c->opt.max_batch, 2 * c->num_sms));
+  dsdk::select_kernel<<<sel_grid, dsdk::kSelectThreads, 0, c->stream>>>(plan, c->d_scores,
+                                                                         c->d_selected);
+  if (timed) Check(cudaEventRecord(c->ev[2], c->stream), "event");
+  const int H = c->cfg.num_heads, D = c->cfg.head_dim, P = c->cfg.page_size;
+#define DSD_ATTN(S)                                                                              \
+  dsdk::attn_kernel<S><<<c->num_sms, dsdk::kAttnThreads, c->attn_smem, c->stream>>>(            \
+      plan, d_q, c->k_pool, c->v_pool, c->token_counts, c->d_selected, c->d_part_acc,             \
+      c->d_part_ml, H, D, P, c->tps, c->scale)
+  switch (c->slots_tmpl) {
+    case 1: DSD_ATTN(1); break;
+    case 2: DSD_ATTN(2); break;
+    case 4: DSD_ATTN(4); break;
+    default: DSD_ATTN(8); break;
+  }
+#undef DSD_ATTN
+  const int pairs = c->opt.max_batch * H;
+  const int comb_grid = std::max(1, std::min((pairs + 7) / 8, 8 * c->num_sms));
+  dsdk::combine_kernel<<<comb_grid, 256, 0, c->stream>>>(plan, c->d_part_acc, c->d_part_ml, H, D,
+                                                         d_out);
+  Check(cudaGetLastError(), "kernel launch");
+  if (timed) Check(cudaEventRecord(c->ev[3], c->stream), "event");
+}
+
+void ReadTiming(dsd_ctx* c, dsd_step_timing* t) {
+  if (!t) return;
+  Check(cudaEventSynchronize(c->ev[3]), "event sync");
+  Check(cudaEventElapsedTime(&t->score_ms, c->ev[0], c->ev[1]), "event time");
+  Check(cudaEventElapsedTime(&t->topk_ms, c->ev[1], c->ev[2]), "event time");
+  Check(cudaEventElapsedTime(&t->attention_ms, c->ev[2], c->ev[3]), "event time");
+  Check(cudaEventElapsedTime(&t->total_ms, c->ev[0], c->ev[3]), "event time");
+}
+
+int* HdrPtr(dsd_ctx* c) { return reinterpret_cast<int*>(c->h_in); }
+int* ReqPtr(dsd_ctx* c) { return reinterpret_cast<int*>(c->h_in + c->in_req_off); }
+float* QPtr(dsd_ctx* c) { return reinterpret_cast<float*>(c->h_in + c->in_q_off); }
+int* IdsPtr(dsd_ctx* c) { return reinterpret_cast<int*>(c->h_in + c->in_ids_off); }
+
+// Common tail of a host-facing step: launch, copy results back, unpack.
+void RunHostStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int output_mode,
+                 int timing, float* outputs, float* scores, int32_t* selected,
+                 dsd_step_timing* out_timing) {
+  LaunchStep(c, reinterpret_cast<const float*>(c->d_in + c->in_q_off), c->d_outputs, timing != 0);
+  const size_t out_bytes = size_t(batch) * c->ept * sizeof(float);
+  if (output_mode != DSD_OUTPUT_NONE && outputs) D2H(c, c->h_outputs, c->d_outputs, out_bytes);
+  if (output_mode == DSD_OUTPUT_DEBUG) {
+    if (scores && total_cand > 0)
+      D2H(c, c->h_scores, c->d_scores, size_t(total_cand) * sizeof(float));
+    if (selected && total_sel > 0)
+      D2H(c, c->h_selected, c->d_selected, size_t(total_sel) * sizeof(int));
+  }
+  CheckStatus(c);  // synchronises the stream
+  if (timing) ReadTiming(c, out_timing);
+  if (output_mode != DSD_OUTPUT_NONE && outputs) std::memcpy(outputs, c->h_outputs, out_bytes);
+  if (output_mode == DSD_OUTPUT_DEBUG) {
+    if (scores && total_cand > 0)
+      std::memcpy(scores, c->h_scores, size_t(total_cand) * sizeof(float));
+    if (selected && total_sel > 0)
+      std::memcpy(selected, c->h_selected, size_t(total_sel) * sizeof(int));
+  }
+}
+
+int SlotOf(dsd_ctx* c, int request_id, bool create) {
+  auto it = c->slot_of.find(request_id);
+  if (it != c->slot_of.end()) return it->second;
+  if (!create) Fail(DSD_EINVAL, "unknown request id " + std::to_string(request_id));
+  if (c->free_slots.empty()) Fail(DSD_ENOMEM, "no free request page-table slot");
+  const int slot = c->free_slots.back();
+  c->free_slots.pop_back();
+  c->slot_of[request_id] = slot;
+  c->slot_pages[slot].clear();
+  return slot;
+}
+
+void RequireTables(dsd_ctx* c) {
+  if (c->opt.max_requests <= 0 || c->table == nullptr)
+    Fail(DSD_EINVAL, "context was created without request page tables");
+}
+
+// Writes (slot, position, page) triples plus explicit counts to the device tables.
+void UploadTableEntries(dsd_ctx* c, const std::vector<int>& triples,
+                        const std::vector<int>& count_pairs) {
+  const size_t nt = triples.size() / 3, nc = count_pairs.size() / 2;
+  const size_t bytes = (triples.size() + count_pairs.size()) * sizeof(int);
+  if (bytes == 0) return;
+  EnsureStage(c, bytes);
+  std::vector<int> packed(triples);
+  packed.insert(packed.end(), count_pairs.begin(), count_pairs.end());
+  Check(cudaMemcpyAsync(c->d_stage, packed.data(), bytes, cudaMemcpyHostToDevice, c->stream),
+        "table upload");
+  CountH2D(c, bytes);
+  int* d = reinterpret_cast<int*>(c->d_stage);
+  if (nc) dsdk::table_set_count_kernel<<<(unsigned)((nc + 255) / 256), 256, 0, c->stream>>>(
+      d + triples.size(), (int)nc, c->table_n);
+  if (nt) dsdk::table_write_kernel<<<(unsigned)((nt + 255) / 256), 256, 0, c->stream>>>(
+      d, (int)nt, c->opt.max_pages_per_request, c->table, c->table_n);
+  Check(cudaGetLastError(), "table kernels");
+  Sync(c);
+}
+
+// Groups tokens by page (first-seen page order, offsets ascending within a page).
+void GroupTokens(const int32_t* page_ids, const int32_t* offs, int n, std::vector<int>* order,
+                 std::vector<int>* group_page, std::vector<int>* group_first) {
+  std::map<int, std::vector<int>> by_page;
+  std::vector<int> first_seen;
+  for (int i = 0; i < n; ++i) {
+    auto& v = by_page[page_ids[i]];
+    if (v.empty()) first_seen.push_back(page_ids[i]);
+    v.push_back(i);
+  }
+  order->clear();
+  group_page->clear();
+  group_first->clear();
+  for (int p : first_seen) {
+    auto& v = by_page[p];
+    std::stable_sort(v.begin(), v.end(), [&](int a, int b) { return offs[a] < offs[b]; });
+    group_page->push_back(p);
+    group_first->push_back(static_cast<int>(order->size()));
+    order->insert(order->end(), v.begin(), v.end());
+  }
+  group_first->push_back(static_cast<int>(order->size()));
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* dsd_last_error(void) { return g_last_error.c_str(); }
+
+int dsd_available(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    return 0;
+  }
+  int dev = 0;
+  cudaDeviceProp prop{};
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaGetDeviceProperties(&prop, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return prop.major >= 10 ? 1 : 0;
+}
+
+int dsd_kernels_per_step(void) { return 5; }
+
+int dsd_ctx_create(int device, const dsd_model_config* config, const dsd_ctx_options* options,
+                   dsd_ctx** out) {
+  return Guard([&]() {
+    if (!config || !options || !out) Fail(DSD_EINVAL, "null argument");
+    *out = nullptr;
+    const dsd_model_config cfg = *config;
+    const dsd_ctx_options opt = *options;
+    const int D = cfg.head_dim;
+    if (cfg.num_heads <= 0 || D < 4 || D > 128 || (D & (D - 1)) != 0)
+      Fail(DSD_EINVAL, "head_dim must be a power of two in [4, 128] and num_heads positive");
+    if (cfg.page_size <= 0) Fail(DSD_EINVAL, "page_size must be positive");
+    if (cfg.top_k_pages < 0) Fail(DSD_EINVAL, "top_k_pages must be non-negative");
+    if (cfg.top_k_pages > dsdk::kSelectMaxK)
+      Fail(DSD_EINVAL, "top_k_pages exceeds " + std::to_string(dsdk::kSelectMaxK));
+    if (opt.capacity_pages < 0 || opt.max_batch < 0 || opt.max_candidates < 0 ||
+        opt.max_selected < 0 || opt.max_requests < 0 || opt.max_pages_per_request < 0)
+      Fail(DSD_EINVAL, "sparse CUDA context capacities must be non-negative");
+    if (opt.max_batch > dsdk::kMaxBatch) Fail(DSD_EINVAL, "max_batch exceeds 1024");
+    const int ept = cfg.num_heads * D;
+    const int vec = ept / 4;
+    int slots = (vec + dsdk::kAttnThreads - 1) / dsdk::kAttnThreads;
+    if (slots > 8) Fail(DSD_EINVAL, "num_heads*head_dim exceeds 8192");
+    slots = slots <= 1 ? 1 : slots <= 2 ? 2 : slots <= 4 ? 4 : 8;
+
+    Check(cudaSetDevice(device), "cudaSetDevice");
+    cudaDeviceProp prop{};
+    Check(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+    if (prop.major < 10) Fail(DSD_EUNAVAILABLE, "an sm_100 (B200) GPU is required");
+
+    auto* c = new dsd_ctx();
+    try {
+      c->device = device;
+      c->cfg = cfg;
+      c->opt = opt;
+      c->ept = ept;
+      c->num_sms = prop.multiProcessorCount;
+      c->slots_tmpl = slots;
+      c->tps = std::max(1, std::min(cfg.page_size, dsdk::kAttnStageFloats / (2 * ept)));
+      c->attn_smem = size_t(dsdk::kAttnStages) * 2 * c->tps * ept * sizeof(float) +
+                     dsdk::kAttnStages * 8;
+      c->scale = 1.0f / std::sqrt(static_cast<float>(D));
+      Check(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream");
+      for (auto& e : c->ev) Check(cudaEventCreate(&e), "event");
+
+      const size_t cap = size_t(opt.capacity_pages);
+      c->k_pool = DeviceAlloc<float>(cap * cfg.page_size * ept, "key pool");
+      c->v_pool = DeviceAlloc<float>(cap * cfg.page_size * ept, "value pool");
+      c->summaries = DeviceAlloc<float>(cap * ept, "page summaries");
+      c->token_counts = DeviceAlloc<int>(cap, "token counts");
+      c->live = DeviceAlloc<uint8_t>(cap, "live mask");
+      Check(cudaMemsetAsync(c->summaries, 0, std::max<size_t>(1, cap * ept) * 4, c->stream), "memset");
+      Check(cudaMemsetAsync(c->token_counts, 0, std::max<size_t>(1, cap) * 4, c->stream), "memset");
+      Check(cudaMemsetAsync(c->live, 0, std::max<size_t>(1, cap), c->stream), "memset");
+      c->host_counts.assign(cap, 0);
+
+      if (opt.max_requests > 0) {
+        c->table = DeviceAlloc<int>(size_t(opt.max_requests) * std::max(1, opt.max_pages_per_request),
+                                    "request page tables");
+        c->table_n = DeviceAlloc<int>(size_t(opt.max_requests), "request page counts");
+        Check(cudaMemsetAsync(c->table_n, 0, size_t(opt.max_requests) * 4, c->stream), "memset");
+        c->slot_pages.resize(size_t(opt.max_requests));
+        for (int s = opt.max_requests - 1; s >= 0; --s) c->free_slots.push_back(s);
+      }
+
+      const int mb = std::max(1, opt.max_batch);
+      const int mc = std::max(1, opt.max_candidates);
+      const int ms = std::max(1, opt.max_selected);
+      c->in_req_off = 16;
+      c->in_q_off = AlignUp(c->in_req_off + size_t(mb + 1) * 4, 128);
+      c->in_ids_off = AlignUp(c->in_q_off + size_t(mb) * ept * 4, 128);
+      c->in_bytes = c->in_ids_off + size_t(mc) * 4;
+      c->d_in = DeviceAlloc<unsigned char>(c->in_bytes, "step input");
+      c->h_in = PinnedAlloc<unsigned char>(c->in_bytes, "step input staging");
+      c->d_scores = DeviceAlloc<float>(mc, "scores");
+      c->d_selected = DeviceAlloc<int>(ms, "selected ids");
+      c->d_outputs = DeviceAlloc<float>(size_t(mb) * ept, "outputs");
+      // one split-K unit holds at least one selected page
+      c->d_part_acc = DeviceAlloc<float>(size_t(ms) * ept, "attention partials");
+      c->d_part_ml = DeviceAlloc<float>(size_t(ms) * cfg.num_heads * 2, "attention partial stats");
+      const size_t plan_ints = size_t(mb) * 2 + size_t(mb + 1) * 4 + 4;
+      c->d_planbuf = DeviceAlloc<int>(plan_ints, "step plan");
+      c->d_status = DeviceAlloc<int>(1, "status word");
+      Check(cudaMemsetAsync(c->d_status, 0, 4, c->stream), "memset");
+      c->h_outputs = PinnedAlloc<float>(size_t(mb) * ept, "output staging");
+      c->h_scores = PinnedAlloc<float>(mc, "score staging");
+      c->h_selected = PinnedAlloc<int>(ms, "selected staging");
+      c->h_status = PinnedAlloc<int>(1, "status staging");
+
+      dsdk::StepPlan& p = c->plan;
+      p.hdr = reinterpret_cast<const int*>(c->d_in);
+      p.req = reinterpret_cast<const int*>(c->d_in + c->in_req_off);
+      p.cand_ids = reinterpret_cast<const int*>(c->d_in + c->in_ids_off);
+      p.table = c->table;
+      p.table_n = c->table_n;
+      p.table_stride = std::max(1, opt.max_pages_per_request);
+      int* q = c->d_planbuf;
+      p.n_cand = q; q += mb;
+      p.id_base = q; q += mb;
+      p.score_off = q; q += mb + 1;
+      p.sel_off = q; q += mb + 1;
+      p.tile_off = q; q += mb + 1;
+      p.unit_off = q; q += mb + 1;
+      p.misc = q;
+      p.status = c->d_status;
+
+      Check(cudaFuncSetAttribute(dsdk::score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)dsdk::kScoreSmem), "smem attribute");
+      auto set_attn = [&](auto kern) {
+        Check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)c->attn_smem), "smem attribute");
+      };
+      switch (c->slots_tmpl) {
+        case 1: set_attn(dsdk::attn_kernel<1>); break;
+        case 2: set_attn(dsdk::attn_kernel<2>); break;
+        case 4: set_attn(dsdk::attn_kernel<4>); break;
+        default: set_attn(dsdk::attn_kernel<8>); break;
+      }
+      Sync(c);
+    } catch (...) {
+      dsd_ctx_destroy(c);
+      throw;
+    }
+    *out = c;
+  });
+}
+
+int dsd_ctx_destroy(dsd_ctx* c) {
+  if (!c) return DSD_OK;
+  cudaSetDevice(c->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  if (c->graph_exec) cudaGraphExecDestroy(c->graph_exec);
+  if (c->graph) cudaGraphDestroy(c->graph);
+  void* dev[] = {c->k_pool, c->v_pool, c->summaries, c->token_counts, c->live, c->table,
+                 c->table_n, c->d_in, c->d_scores, c->d_selected, c->d_outputs, c->d_part_acc,
+                 c->d_part_ml, c->d_planbuf, c->d_status, c->d_stage};
+  for (void* p : dev)
+    if (p) cudaFree(p);
+  void* host[] = {c->h_in, c->h_outputs, c->h_scores, c->h_selected, c->h_status};
+  for (void* p : host)
+    if (p) cudaFreeHost(p);
+  for (auto& e : c->ev)
+    if (e) cudaEventDestroy(e);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+  return DSD_OK;
+}
+
+int dsd_ctx_device_pointers(dsd_ctx* c, float** keys, float** values, float** summaries,
+                            int32_t** token_counts) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    if (keys) *keys = c->k_pool;
+    if (values) *values = c->v_pool;
+    if (summaries) *summaries = c->summaries;
+    if (token_counts) *token_counts = c->token_counts;
+  });
+}
+
+void* dsd_ctx_stream(dsd_ctx* c) { return c ? static_cast<void*>(c->stream) : nullptr; }
+
+int dsd_pool_reset(dsd_ctx* c) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    SetDevice(c);
+    const size_t cap = size_t(c->opt.capacity_pages);
+    Check(cudaMemsetAsync(c->summaries, 0, std::max<size_t>(1, cap * c->ept) * 4, c->stream), "memset");
+    Check(cudaMemsetAsync(c->token_counts, 0, std::max<size_t>(1, cap) * 4, c->stream), "memset");
+    Check(cudaMemsetAsync(c->live, 0, std::max<size_t>(1, cap), c->stream), "memset");
+    std::fill(c->host_counts.begin(), c->host_counts.end(), 0);
+    if (c->table_n) {
+      Check(cudaMemsetAsync(c->table_n, 0, size_t(c->opt.max_requests) * 4, c->stream), "memset");
+      c->slot_of.clear();
+      c->free_slots.clear();
+      for (int s = c->opt.max_requests - 1; s >= 0; --s) c->free_slots.push_back(s);
+      for (auto& v : c->slot_pages) v.clear();
+    }
+    Sync(c);
+  });
+}
+
+int dsd_pool_upload_pages(dsd_ctx* c, const int32_t* page_ids, const int32_t* token_counts, int n,
+                          const float* keys, const float* values, int compute_summary) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    if (n < 0) Fail(DSD_EINVAL, "negative page count");
+    if (n == 0) return;
+    if (!page_ids || !token_counts) Fail(DSD_EINVAL, "null page metadata");
+    SetDevice(c);
+    long long total_tokens = 0;
+    for (int i = 0; i < n; ++i) {
+      ValidatePage(c, page_ids[i]);
+      if (token_counts[i] <= 0 || token_counts[i] > c->cfg.page_size)
+        Fail(DSD_EINVAL, "token_count must be in (0, page_size]");
+      total_tokens += token_counts[i];
+    }
+    if (!keys || !values) Fail(DSD_EINVAL, "host page payload pointers must be non-null");
+    const size_t row = size_t(c->ept) * sizeof(float);
+    // process in groups whose payload fits a bounded staging buffer
+    const size_t max_stage = size_t(256) << 20;
+    int i0 = 0;
+    long long tok0 = 0;
+    while (i0 < n) {
+      int i1 = i0;
+      long long toks = 0;
+      while (i1 < n && (i1 == i0 || size_t(toks + token_counts[i1]) * row * 2 <= max_stage)) {
+        toks += token_counts[i1];
+        ++i1;
+      }
+      const int np = i1 - i0;
+      const size_t payload = size_t(toks) * row;
+      const size_t meta_off = AlignUp(2 * payload, 256);
+      // meta = [long long src_token_off[np]][int page_ids[np]][int counts[np]]
+      std::vector<long long> meta(size_t(np) + size_t(np + 1) / 2 * 2, 0);
+      long long* m_off = meta.data();
+      int* m_ids = reinterpret_cast<int*>(meta.data() + np);
+      int* m_cnt = m_ids + np;
+      long long acc = 0;
+      for (int i = 0; i < np; ++i) {
+        m_off[i] = acc;
+        m_ids[i] = page_ids[i0 + i];
+        m_cnt[i] = token_counts[i0 + i];
+        acc += token_counts[i0 + i];
+      }
+      const size_t meta_bytes = meta.size() * sizeof(long long);
+      EnsureStage(c, meta_off + meta_bytes);
+      H2D(c, c->d_stage, keys + tok0 * c->ept, payload);
+      H2D(c, c->d_stage + payload, values + tok0 * c->ept, payload);
+      H2D(c, c->d_stage + meta_off, meta.data(), meta_bytes);
+      const long long* d_off = reinterpret_cast<const long long*>(c->d_stage + meta_off);
+      const int* d_ids = reinterpret_cast<const int*>(d_off + np);
+      const int vec = c->ept / 4;
+      dim3 grid(np, (vec + 255) / 256);
+      dsdk::upload_pages_kernel<<<grid, 256, 0, c->stream>>>(
+          d_ids, d_ids + np, d_off, reinterpret_cast<const float*>(c->d_stage),
+          reinterpret_cast<const float*>(c->d_stage + payload), c->ept, c->cfg.page_size,
+          compute_summary, c->k_pool, c->v_pool, c->summaries, c->token_counts, c->live);
+      Check(cudaGetLastError(), "upload kernel");
+      Sync(c);  // the staging buffer is reused by the next group
+      for (int i = i0; i < i1; ++i) c->host_counts[page_ids[i]] = token_counts[i];
+      tok0 += toks;
+      i0 = i1;
+    }
+  });
+}
+
+int dsd_pool_upload_summaries(dsd_ctx* c, const int32_t* page_ids, int n, const float* summaries) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    if (n <= 0) return;
+    SetDevice(c);
+    for (int i = 0; i < n; ++i) ValidatePage(c, page_ids[i]);
+    const size_t sb = size_t(n) * c->ept * sizeof(float);
+    const size_t ids_off = AlignUp(sb, 256);
+    EnsureStage(c, ids_off + size_t(n) * 4);
+    H2D(c, c->d_stage, summaries, sb);
+    H2D(c, c->d_stage + ids_off, page_ids, size_t(n) * 4);
+    dsdk::set_summaries_kernel<<<n, 256, 0, c->stream>>>(
+        reinterpret_cast<const int*>(c->d_stage + ids_off),
+        reinterpret_cast<const float*>(c->d_stage), c->ept, c->summaries);
+    Check(cudaGetLastError(), "summary kernel");
+    Sync(c);
+  });
+}
+
+int dsd_pool_prefill_synthetic(dsd_ctx* c, const int32_t* page_ids, const int32_t* token_counts,
+                               int n, int request_id) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    if (n <= 0) return;
+    SetDevice(c);
+    for (int i = 0; i < n; ++i) {
+      ValidatePage(c, page_ids[i]);
+      if (token_counts[i] <= 0 || token_counts[i] > c->cfg.page_size)
+        Fail(DSD_EINVAL, "token_count must be in (0, page_size]");
+    }
+    EnsureStage(c, size_t(n) * 8);
+    H2D(c, c->d_stage, page_ids, size_t(n) * 4);
+    H2D(c, c->d_stage + size_t(n) * 4, token_counts, size_t(n) * 4);
+    const int* d = reinterpret_cast<const int*>(c->d_stage);
+    dsdk::prefill_synthetic_kernel<<<n, 256, 0, c->stream>>>(d, d + n, request_id, c->ept,
+                                                            c->cfg.page_size, c->k_pool, c->v_pool,
+                                                            c->summaries, c->token_counts, c->live);
+    Check(cudaGetLastError(), "prefill kernel");
+    Sync(c);
+    for (int i = 0; i < n; ++i) c->host_counts[page_ids[i]] = token_counts[i];
+  });
+}
+
+int dsd_pool_generate_normal(dsd_ctx* c, const int32_t* page_ids, const int32_t* token_counts,
+                             const int32_t* request_ids, const int32_t* first_token, int n,
+                             uint64_t seed) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    if (n <= 0) return;
+    SetDevice(c);
+    for (int i = 0; i < n; ++i) {
+      ValidatePage(c, page_ids[i]);
+      if (token_counts[i] <= 0 || token_counts[i] > c->cfg.page_size)
+        Fail(DSD_EINVAL, "token_count must be in (0, page_size]");
+    }
+    const int chunk = 1 << 16;
+    for (int i0 = 0; i0 < n; i0 += chunk) {
+      const int m = std::min(chunk, n - i0);
+      EnsureStage(c, size_t(chunk) * 16);
+      int* d = reinterpret_cast<int*>(c->d_stage);
+      H2D(c, d, page_ids + i0, size_t(m) * 4);
+      H2D(c, d + m, token_counts + i0, size_t(m) * 4);
+      H2D(c, d + 2 * m, request_ids + i0, size_t(m) * 4);
+      H2D(c, d + 3 * m, first_token + i0, size_t(m) * 4);
+      dim3 grid(m, (c->ept + 255) / 256);
+      dsdk::generate_normal_kernel<<<grid, 256, 0, c->stream>>>(
+          d, d + m, d + 2 * m, d + 3 * m, c->ept, c->cfg.page_size, dsdk::normal_seed_mix(seed, 1),
+          dsdk::normal_seed_mix(seed, 2), c->k_pool, c->v_pool, c->summaries, c->token_counts,
+          c->live);
+      Check(cudaGetLastError(), "generate kernel");
+      Sync(c);
+    }
+    for (int i = 0; i < n; ++i) c->host_counts[page_ids[i]] = token_counts[i];
+  });
+}
+
+void dsd_generate_normal_host(uint64_t seed, int kind, uint64_t first_index, int64_t count,
+                              float* out) {
+  const uint64_t mix = dsdk::normal_seed_mix(seed, kind);
+  for (int64_t i = 0; i < count; ++i) out[i] = dsdk::normal_value(mix, first_index + uint64_t(i));
+}
+
+int dsd_append_tokens(dsd_ctx* c, const int32_t* page_ids, const int32_t* token_offsets,
+                      const int32_t* request_ids, int n, const float* keys, const float* values) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    if (n <= 0) return;
+    if (!keys || !values) Fail(DSD_EINVAL, "token payload pointers must be non-null");
+    SetDevice(c);
+    for (int i = 0; i < n; ++i) {
+      ValidatePage(c, page_ids[i]);
+      if (token_offsets[i] < 0 || token_offsets[i] >= c->cfg.page_size)
+        Fail(DSD_ERANGE, "token_offset is outside the page");
+    }
+    std::vector<int> triples, counts;
+    if (request_ids) {
+      RequireTables(c);
+      for (int i = 0; i < n; ++i) {
+        if (token_offsets[i] != 0) continue;
+        const int slot = SlotOf(c, request_ids[i], true);
+        auto& pages = c->slot_pages[slot];
+        if (int(pages.size()) >= c->opt.max_pages_per_request)
+          Fail(DSD_EINVAL, "request page table is full");
+        triples.insert(triples.end(), {slot, int(pages.size()), page_ids[i]});
+        pages.push_back(page_ids[i]);
+      }
+    }
+    std::vector<int> order, gpage, gfirst;
+    GroupTokens(page_ids, token_offsets, n, &order, &gpage, &gfirst);
+    const size_t row = size_t(c->ept) * 4;
+    const size_t payload = size_t(n) * row;
+    const size_t meta_off = AlignUp(2 * payload, 256);
+    std::vector<int> meta;
+    meta.insert(meta.end(), gpage.begin(), gpage.end());
+    meta.insert(meta.end(), gfirst.begin(), gfirst.end());
+    for (int i : order) meta.push_back(token_offsets[i]);
+    EnsureStage(c, meta_off + meta.size() * 4);
+    // payload in grouped order
+    std::vector<float> sk(size_t(n) * c->ept), sv(size_t(n) * c->ept);
+    for (int j = 0; j < n; ++j) {
+      std::memcpy(sk.data() + size_t(j) * c->ept, keys + size_t(order[j]) * c->ept, row);
+      std::memcpy(sv.data() + size_t(j) * c->ept, values + size_t(order[j]) * c->ept, row);
+    }
+    H2D(c, c->d_stage, sk.data(), payload);
+    H2D(c, c->d_stage + payload, sv.data(), payload);
+    H2D(c, c->d_stage + meta_off, meta.data(), meta.size() * 4);
+    const int ng = int(gpage.size());
+    const int* d = reinterpret_cast<const int*>(c->d_stage + meta_off);
+    dsdk::append_tokens_kernel<<<ng, 256, 0, c->stream>>>(
+        d, d + ng, d + 2 * ng + 1, reinterpret_cast<const float*>(c->d_stage),
+        reinterpret_cast<const float*>(c->d_stage + payload), c->ept, c->cfg.page_size,
+        c->k_pool, c->v_pool, c->summaries, c->token_counts, c->live);
+    Check(cudaGetLastError(), "append kernel");
+    Sync(c);
+    for (int i = 0; i < n; ++i)
+      c->host_counts[page_ids[i]] = std::max(c->host_counts[page_ids[i]], token_offsets[i] + 1);
+    UploadTableEntries(c, triples, counts);
+  });
+}
+
+int dsd_append_tokens_synthetic(dsd_ctx* c, const int32_t* page_ids, const int32_t* token_offsets,
+                                const int32_t* request_ids, const int32_t* decode_steps, int n) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    if (n <= 0) return;
+    SetDevice(c);
+    for (int i = 0; i < n; ++i) {
+      ValidatePage(c, page_ids[i]);
+      if (token_offsets[i] < 0 || token_offsets[i] >= c->cfg.page_size)
+        Fail(DSD_ERANGE, "token_offset is outside the page");
+    }
+    std::vector<int> order, gpage, gfirst;
+    GroupTokens(page_ids, token_offsets, n, &order, &gpage, &gfirst);
+    std::vector<int> meta;
+    meta.insert(meta.end(), gpage.begin(), gpage.end());
+    meta.insert(meta.end(), gfirst.begin(), gfirst.end());
+    for (int i : order) meta.push_back(token_offsets[i]);
+    for (int i : order) meta.push_back(request_ids[i]);
+    for (int i : order) meta.push_back(decode_steps[i]);
+    EnsureStage(c, meta.size() * 4);
+    H2D(c, c->d_stage, meta.data(), meta.size() * 4);
+    const int ng = int(gpage.size());
+    const int* d = reinterpret_cast<const int*>(c->d_stage);
+    const int* toff = d + 2 * ng + 1;
+    dsdk::append_synthetic_kernel<<<ng, 256, 0, c->stream>>>(
+        d, d + ng, toff, toff + n, toff + 2 * n, c->ept, c->cfg.page_size, c->k_pool, c->v_pool,
+        c->summaries, c->token_counts, c->live);
+    Check(cudaGetLastError(), "synthetic append kernel");
+    Sync(c);
+    for (int i = 0; i < n; ++i)
+      c->host_counts[page_ids[i]] = std::max(c->host_counts[page_ids[i]], token_offsets[i] + 1);
+  });
+}
+
+int dsd_pool_free_pages(dsd_ctx* c, const int32_t* page_ids, int n) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    if (n <= 0) return;
+    SetDevice(c);
+    for (int i = 0; i < n; ++i) ValidatePage(c, page_ids[i]);
+    EnsureStage(c, size_t(n) * 4);
+    H2D(c, c->d_stage, page_ids, size_t(n) * 4);
+    dsdk::free_pages_kernel<<<n, 256, 0, c->stream>>>(reinterpret_cast<const int*>(c->d_stage),
+                                                      c->ept, c->summaries, c->token_counts,
+                                                      c->live);
+    Check(cudaGetLastError(), "free kernel");
+    Sync(c);
+    for (int i = 0; i < n; ++i) c->host_counts[page_ids[i]] = 0;
+  });
+}
+
+int dsd_download_page(dsd_ctx* c, int page_id, float* keys, float* values, float* summary,
+                      int32_t* token_count) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    ValidatePage(c, page_id);
+    SetDevice(c);
+    const size_t pf = size_t(c->cfg.page_size) * c->ept;
+    if (keys) D2H(c, keys, c->k_pool + size_t(page_id) * pf, pf * 4);
+    if (values) D2H(c, values, c->v_pool + size_t(page_id) * pf, pf * 4);
+    if (summary) D2H(c, summary, c->summaries + size_t(page_id) * c->ept, size_t(c->ept) * 4);
+    if (token_count) D2H(c, token_count, c->token_counts + page_id, 4);
+    Sync(c);
+  });
+}
+
+int dsd_download_metadata(dsd_ctx* c, int32_t* token_counts, uint8_t* live_mask) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    SetDevice(c);
+    const size_t cap = size_t(c->opt.capacity_pages);
+    if (token_counts) D2H(c, token_counts, c->token_counts, cap * 4);
+    if (live_mask) D2H(c, live_mask, c->live, cap);
+    Sync(c);
+  });
+}
+
+int dsd_get_transfer_stats(dsd_ctx* c, dsd_transfer_stats* out) {
+  return Guard([&]() {
+    if (!c || !out) Fail(DSD_EINVAL, "null argument");
+    *out = c->stats;
+  });
+}
+
+int dsd_reset_transfer_stats(dsd_ctx* c) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    c->stats = dsd_transfer_stats{};
+  });
+}
+
+int dsd_decode_batch(dsd_ctx* c, int batch, const float* queries, const int32_t* cand_offsets,
+                     const int32_t* cand_ids, int output_mode, int timing, float* outputs,
+                     float* scores, int32_t* selected, dsd_step_timing* out_timing) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    if (batch < 0) Fail(DSD_EINVAL, "negative batch");
+    if (out_timing) *out_timing = dsd_step_timing{};
+    if (batch == 0) return;
+    if (!queries || !cand_offsets) Fail(DSD_EINVAL, "null step input");
+    if (batch > c->opt.max_batch)
+      Fail(DSD_EINVAL, "request batch exceeds sparse CUDA context capacity");
+    if (cand_offsets[0] != 0) Fail(DSD_EINVAL, "cand_offsets[0] must be 0");
+    int total_sel = 0;
+    for (int r = 0; r < batch; ++r) {
+      const int n = cand_offsets[r + 1] - cand_offsets[r];
+      if (n < 0) Fail(DSD_EINVAL, "cand_offsets must be non-decreasing");
+      total_sel += std::min(c->cfg.top_k_pages, n);
+    }
+    const int total_cand = cand_offsets[batch];
+    if (total_cand > c->opt.max_candidates)
+      Fail(DSD_EINVAL, "candidate page count exceeds sparse CUDA context capacity");
+    if (total_sel > c->opt.max_selected)
+      Fail(DSD_EINVAL, "selected page count exceeds sparse CUDA context capacity");
+    for (int i = 0; i < total_cand; ++i) ValidatePage(c, cand_ids[i]);
+    SetDevice(c);
+    int* hdr = HdrPtr(c);
+    hdr[0] = batch;
+    hdr[1] = 0;
+    std::memcpy(ReqPtr(c), cand_offsets, size_t(batch + 1) * 4);
+    std::memcpy(QPtr(c), queries, size_t(batch) * c->ept * 4);
+    std::memcpy(IdsPtr(c), cand_ids, size_t(total_cand) * 4);
+    H2D(c, c->d_in, c->h_in, c->in_q_off + size_t(batch) * c->ept * 4);
+    if (total_cand > 0) H2D(c, c->d_in + c->in_ids_off, IdsPtr(c), size_t(total_cand) * 4);
+    RunHostStep(c, batch, total_cand, total_sel, output_mode, timing, outputs, scores, selected,
+                out_timing);
+  });
+}
+
+int dsd_request_set_pages(dsd_ctx* c, int request_id, const int32_t* page_ids, int n) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    RequireTables(c);
+    if (n < 0 || n > c->opt.max_pages_per_request)
+      Fail(DSD_EINVAL, "page count exceeds the request page table");
+    for (int i = 0; i < n; ++i) ValidatePage(c, page_ids[i]);
+    SetDevice(c);
+    const int slot = SlotOf(c, request_id, true);
+    std::vector<int> triples;
+    c->slot_pages[slot].assign(page_ids, page_ids + n);
+    for (int i = 0; i < n; ++i) triples.insert(triples.end(), {slot, i, page_ids[i]});
+    UploadTableEntries(c, triples, std::vector<int>{slot, 0});
+  });
+}
+
+int dsd_request_append_pages(dsd_ctx* c, int request_id, const int32_t* page_ids, int n) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    RequireTables(c);
+    for (int i = 0; i < n; ++i) ValidatePage(c, page_ids[i]);
+    SetDevice(c);
+    const int slot = SlotOf(c, request_id, true);
+    auto& pages = c->slot_pages[slot];
+    if (int(pages.size()) + n > c->opt.max_pages_per_request)
+      Fail(DSD_EINVAL, "page count exceeds the request page table");
+    std::vector<int> triples;
+    for (int i = 0; i < n; ++i) {
+      triples.insert(triples.end(), {slot, int(pages.size()), page_ids[i]});
+      pages.push_back(page_ids[i]);
+    }
+    UploadTableEntries(c, triples, {});
+  });
+}
+
+int dsd_request_release(dsd_ctx* c, int request_id, int free_pages) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    RequireTables(c);
+    auto it = c->slot_of.find(request_id);
+    if (it == c->slot_of.end()) return;
+    const int slot = it->second;
+    std::vector<int> pages = c->slot_pages[slot];
+    c->slot_pages[slot].clear();
+    c->slot_of.erase(it);
+    c->free_slots.push_back(slot);
+    UploadTableEntries(c, {}, std::vector<int>{slot, 0});
+    if (free_pages && !pages.empty()) {
+      const int rc = dsd_pool_free_pages(c, pages.data(), int(pages.size()));
+      if (rc != DSD_OK) Fail(rc, g_last_error);
+    }
+  });
+}
+
+int dsd_request_num_pages(dsd_ctx* c, int request_id) {
+  if (!c) return -1;
+  auto it = c->slot_of.find(request_id);
+  if (it == c->slot_of.end()) return 0;
+  return int(c->slot_pages[it->second].size());
+}
+
+namespace {
+void PackSlots(dsd_ctx* c, const int32_t* request_ids, int batch, int* total_cand,
+               int* total_sel) {
+  if (batch > c->opt.max_batch) Fail(DSD_EINVAL, "request batch exceeds sparse CUDA context capacity");
+  int* req = ReqPtr(c);
+  int tc = 0, ts = 0;
+  for (int r = 0; r < batch; ++r) {
+    const int slot = SlotOf(c, request_ids[r], false);
+    req[r] = slot;
+    const int n = int(c->slot_pages[slot].size());
+    tc += n;
+    ts += std::min(c->cfg.top_k_pages, n);
+  }
+  req[batch] = 0;
+  if (tc > c->opt.max_candidates)
+    Fail(DSD_EINVAL, "candidate page count exceeds sparse CUDA context capacity");
+  if (ts > c->opt.max_selected)
+    Fail(DSD_EINVAL, "selected page count exceeds sparse CUDA context capacity");
+  int* hdr = HdrPtr(c);
+  hdr[0] = batch;
+  hdr[1] = 1;
+  *total_cand = tc;
+  *total_sel = ts;
+}
+}  // namespace
+
+int dsd_decode_step(dsd_ctx* c, const int32_t* request_ids, int batch, const float* queries,
+                    int output_mode, int timing, float* outputs, float* scores,
+                    int32_t* selected, dsd_step_timing* out_timing) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    RequireTables(c);
+    if (out_timing) *out_timing = dsd_step_timing{};
+    if (batch <= 0) return;
+    if (!queries || !request_ids) Fail(DSD_EINVAL, "null step input");
+    SetDevice(c);
+    int tc = 0, ts = 0;
+    PackSlots(c, request_ids, batch, &tc, &ts);
+    std::memcpy(QPtr(c), queries, size_t(batch) * c->ept * 4);
+    H2D(c, c->d_in, c->h_in, c->in_q_off + size_t(batch) * c->ept * 4);
+    RunHostStep(c, batch, tc, ts, output_mode, timing, outputs, scores, selected, out_timing);
+  });
+}
+
+int dsd_bind_requests(dsd_ctx* c, const int32_t* request_ids, int batch) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    RequireTables(c);
+    if (batch <= 0) Fail(DSD_EINVAL, "empty request set");
+    SetDevice(c);
+    int tc = 0, ts = 0;
+    PackSlots(c, request_ids, batch, &tc, &ts);
+    H2D(c, c->d_in, c->h_in, c->in_q_off);
+    Sync(c);
+    c->bound_batch = batch;
+  });
+}
+
+int dsd_decode_bound(dsd_ctx* c, const float* d_queries, float* d_outputs) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    if (c->bound_batch <= 0) Fail(DSD_EINVAL, "no request set bound");
+    SetDevice(c);
+    if (!c->graph_exec || c->graph_q != d_queries || c->graph_out != d_outputs) {
+      if (c->graph_exec) cudaGraphExecDestroy(c->graph_exec);
+      if (c->graph) cudaGraphDestroy(c->graph);
+      c->graph_exec = nullptr;
+      c->graph = nullptr;
+      Check(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+      LaunchStep(c, d_queries, d_outputs, false);
+      Check(cudaStreamEndCapture(c->stream, &c->graph), "end capture");
+      Check(cudaGraphInstantiate(&c->graph_exec, c->graph, 0), "graph instantiate");
+      c->graph_q = d_queries;
+      c->graph_out = d_outputs;
+    }
+    Check(cudaGraphLaunch(c->graph_exec, c->stream), "graph launch");
+  });
+}
+
+int dsd_decode_bound_timed(dsd_ctx* c, const float* d_queries, float* d_outputs,
+                           dsd_step_timing* out_timing) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    if (c->bound_batch <= 0) Fail(DSD_EINVAL, "no request set bound");
+    SetDevice(c);
+    LaunchStep(c, d_queries, d_outputs, true);
+    CheckStatus(c);
+    ReadTiming(c, out_timing);
+  });
+}
+
+}  // extern "C"

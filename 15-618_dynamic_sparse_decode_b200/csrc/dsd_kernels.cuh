@@ -1,0 +1,990 @@
+// dsd_kernels.cuh -- sm_100a kernels of the batched page-level sparse decode step.
+//
+// One decode step (SparseCudaContext::RunBatch in the reference,
+// src/cuda/sparse_batched_attention.cu:574-838) is five launches on one stream:
+//
+//   plan_kernel     per-request CSR offsets by a device prefix sum (replaces
+//                   the host PackSparseBatchInto, :24-96)
+//   score_kernel    score[c] = seqdot(q_r, summary[page_c]) * 1/sqrt(D), in the
+//                   CPU's exact operation order (ScorePagesCpu,
+//                   src/reference_kernels.cpp:59-80) so page selection is
+//                   bit-identical to sparse_cpu; summaries stream HBM -> smem
+//                   with cp.async.bulk into an mbarrier ring
+//   select_kernel   per-request top-min(k,n) by (score desc, page id asc)
+//                   (SelectTopKPagesCpu, :82-107) via a 64-bit radix select
+//   attn_kernel     split-K flash decode over the selected pages, all heads
+//                   of a page per CTA; K/V token rows stream HBM -> smem with
+//                   cp.async.bulk (GatherPagesCpu + SparseAttentionCpu,
+//                   :109-194, fused)
+//   combine_kernel  log-sum-exp merge of the split-K partials
+//
+// Pool maintenance kernels (upload with summary, token append with running
+// mean, free, synthetic generators) follow at the end.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dsdk {
+
+constexpr int kMaxBatch = 1024;
+constexpr int kPlanThreads = 1024;
+
+// score tiles: 128 candidates of one request, one per consumer thread
+constexpr int kScoreTile = 128;
+constexpr int kScoreChunk = 64;                     // floats of a summary row per stage
+constexpr int kScoreRowStride = kScoreChunk + 4;    // +16 B: conflict-free float4 rows
+constexpr int kScoreStages = 3;
+constexpr int kScoreConsumerWarps = kScoreTile / 32;
+constexpr int kScoreThreads = kScoreTile + 32;      // + one producer warp
+constexpr int kScoreRows = kScoreTile + 1;          // + the query chunk
+constexpr size_t kScoreSmem =
+    size_t(kScoreStages) * kScoreRows * kScoreRowStride * sizeof(float) + 2 * kScoreStages * 8;
+
+constexpr int kAttnThreads = 256;
+constexpr int kAttnStages = 3;
+constexpr int kAttnStageFloats = 16384;             // K+V floats per stage (64 KiB)
+constexpr int kMaxPagesPerUnit = 16;
+
+constexpr int kSelectThreads = 512;
+constexpr int kSelectMaxK = 4096;                   // selected pages per request
+
+// status bits written by kernels (read by the host after the step)
+constexpr int kStatusTimeout = 1;
+constexpr int kStatusBadInput = 2;
+
+// A bounded wait: ~2^31 cycles (about a second at 1.9 GHz).
+constexpr long long kWaitBudgetCycles = 2LL << 30;
+
+struct StepPlan {
+  // written by the host each step (one packed H2D copy)
+  const int* hdr;          // [0] batch, [1] mode (0 = CSR, 1 = page tables)
+  const int* req;          // CSR: cand_offsets[B+1]; tables: slot[B]
+  const int* cand_ids;     // CSR ids
+  // device page tables
+  const int* table;        // [max_requests][stride]
+  const int* table_n;      // [max_requests]
+  int table_stride;
+  // computed by plan_kernel
+  int* n_cand;             // [B]
+  int* id_base;            // [B]  offset of request r's ids in its id array
+  int* score_off;          // [B+1]
+  int* sel_off;            // [B+1]
+  int* tile_off;           // [B+1]
+  int* unit_off;           // [B+1]
+  int* misc;               // [0] pages per attention unit
+  int* status;             // error bits
+};
+
+// ------------------------------------------------------------------ PTX helpers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the barrier phase with a cycle budget; on expiry sets the
+// timeout bit in *status and returns false (the caller then stops issuing work).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long start = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - start > kWaitBudgetCycles) {
+      atomicOr(status, kStatusTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+// 1-D bulk copy global -> shared (TMA), completion counted on `bar` in bytes.
+// Both addresses 16 B aligned, bytes a multiple of 16.  No multicast.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// index of the last segment whose start offset is <= x (offs ascending, offs[0] = 0)
+__device__ __forceinline__ int upper_segment(const int* offs, int n, int x) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(offs + mid) <= x) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// ------------------------------------------------------------------ plan
+
+// Block-wide exclusive scan of up to 4 ints per thread (one element per thread).
+template <int N>
+__device__ __forceinline__ void block_exclusive_scan(int (&v)[N], int (&total)[N]) {
+  __shared__ int warp_sums[32][N];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    int x = v[i];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    incl[i] = x;
+    if (lane == 31) warp_sums[warp][i] = x;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      int x = lane < nw ? warp_sums[lane][i] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      if (lane < nw) warp_sums[lane][i] = x;  // inclusive over warps
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const int before = warp > 0 ? warp_sums[warp - 1][i] : 0;
+    total[i] = warp_sums[(blockDim.x >> 5) - 1][i];
+    v[i] = before + incl[i] - v[i];
+  }
+  __syncthreads();
+}
+
+// One CTA of 1024 threads.  Computes the step's ragged layout from the
+// request list: candidate counts (CSR offsets or page-table lengths),
+// selected counts min(k, n), score tiles and split-K attention units.
+__global__ void __launch_bounds__(kPlanThreads) plan_kernel(StepPlan plan, int top_k,
+                                                            int target_units) {
+  const int B = plan.hdr[0];
+  const int mode = plan.hdr[1];
+  const int r = threadIdx.x;
+  int n = 0, base = 0;
+  if (r < B) {
+    if (mode == 0) {
+      base = plan.req[r];
+      n = plan.req[r + 1] - base;
+    } else {
+      const int slot = plan.req[r];
+      base = slot * plan.table_stride;
+      n = plan.table_n[slot];
+    }
+    if (n < 0) { n = 0; atomicOr(plan.status, kStatusBadInput); }
+  }
+  const int ksel = max(0, min(top_k, n));
+  int v[3] = {n, ksel, (n + kScoreTile - 1) / kScoreTile};
+  int tot[3];
+  block_exclusive_scan<3>(v, tot);
+  if (r < B) {
+    plan.n_cand[r] = n;
+    plan.id_base[r] = base;
+    plan.score_off[r] = v[0];
+    plan.sel_off[r] = v[1];
+    plan.tile_off[r] = v[2];
+  }
+  if (r == 0) {
+    plan.score_off[B] = tot[0];
+    plan.sel_off[B] = tot[1];
+    plan.tile_off[B] = tot[2];
+  }
+  // pages per attention unit: enough units to fill the GPU, at most 16 pages
+  int ppu = (tot[1] + target_units - 1) / max(1, target_units);
+  ppu = max(1, min(kMaxPagesPerUnit, ppu));
+  int u[1] = {(ksel + ppu - 1) / ppu};
+  int utot[1];
+  block_exclusive_scan<1>(u, utot);
+  if (r < B) plan.unit_off[r] = u[0];
+  if (r == 0) {
+    plan.unit_off[B] = utot[0];
+    plan.misc[0] = ppu;
+  }
+}
+
+// ------------------------------------------------------------------ score
+
+// Persistent CTAs over score tiles.  Consumer thread t owns candidate t of
+// the tile and accumulates q[i]*s[i] for i = 0..E-1 in order with
+// round-to-nearest multiply and add (no FMA), exactly ScorePagesCpu's Dot.
+// A producer warp streams each tile's summary rows chunk by chunk
+// (kScoreChunk floats per row per stage) into a kScoreStages-deep ring with
+// cp.async.bulk; row kScoreTile of every stage holds the query chunk.
+__global__ void __launch_bounds__(kScoreThreads) score_kernel(StepPlan plan,
+                                                              const float* __restrict__ queries,
+                                                              const float* __restrict__ summaries,
+                                                              int ept, float scale,
+                                                              float* __restrict__ scores) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  float* stage_base = reinterpret_cast<float*>(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(
+      smem_raw + size_t(kScoreStages) * kScoreRows * kScoreRowStride * sizeof(float));
+  uint64_t* empty = full + kScoreStages;
+
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    for (int s = 0; s < kScoreStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kScoreConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  const int B = plan.hdr[0];
+  const int mode = plan.hdr[1];
+  const int* ids_src = mode == 0 ? plan.cand_ids : plan.table;
+  const int total_tiles = plan.tile_off[B];
+  const int nchunks = (ept + kScoreChunk - 1) / kScoreChunk;
+  int* status = plan.status;
+
+  if (tid >= kScoreTile) {
+    // ---------------- producer warp
+    const int lane = tid - kScoreTile;
+    uint32_t g = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+      const int r = upper_segment(plan.tile_off, B, tile);
+      const int c0 = (tile - plan.tile_off[r]) * kScoreTile;
+      const int nvalid = min(kScoreTile, plan.n_cand[r] - c0);
+      const int* ids = ids_src + plan.id_base[r] + c0;
+      int my_page[kScoreTile / 32];
+#pragma unroll
+      for (int m = 0; m < kScoreTile / 32; ++m) {
+        const int row = lane + 32 * m;
+        my_page[m] = row < nvalid ? __ldg(ids + row) : 0;
+      }
+      const float* qrow = queries + size_t(r) * ept;
+      for (int ch = 0; ch < nchunks; ++ch, ++g) {
+        const int s = g % kScoreStages;
+        if (g >= kScoreStages) {
+          if (!mbar_wait(&empty[s], ((g / kScoreStages) - 1) & 1, status)) return;
+        }
+        const int len = min(kScoreChunk, ept - ch * kScoreChunk);
+        const uint32_t row_bytes = uint32_t(len) * 4u;
+        float* stage = stage_base + size_t(s) * kScoreRows * kScoreRowStride;
+        if (lane == 0) mbar_arrive_expect_tx(&full[s], row_bytes * uint32_t(nvalid + 1));
+        __syncwarp();
+#pragma unroll
+        for (int m = 0; m < kScoreTile / 32; ++m) {
+          const int row = lane + 32 * m;
+          if (row < nvalid) {
+            bulk_g2s(stage + row * kScoreRowStride,
+                     summaries + size_t(my_page[m]) * ept + size_t(ch) * kScoreChunk, row_bytes,
+                     &full[s]);
+          }
+        }
+        if (lane == 0) {
+          bulk_g2s(stage + kScoreTile * kScoreRowStride, qrow + size_t(ch) * kScoreChunk,
+                   row_bytes, &full[s]);
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers
+  const int lane = tid & 31;
+  uint32_t g = 0;
+  for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+    const int r = upper_segment(plan.tile_off, B, tile);
+    const int c0 = (tile - plan.tile_off[r]) * kScoreTile;
+    const int nvalid = min(kScoreTile, plan.n_cand[r] - c0);
+    float acc = 0.0f;
+    for (int ch = 0; ch < nchunks; ++ch, ++g) {
+      const int s = g % kScoreStages;
+      if (!mbar_wait(&full[s], (g / kScoreStages) & 1, status)) return;
+      const int len = min(kScoreChunk, ept - ch * kScoreChunk);
+      const float* stage = stage_base + size_t(s) * kScoreRows * kScoreRowStride;
+      if (tid < nvalid) {
+        const float4* srow = reinterpret_cast<const float4*>(stage + tid * kScoreRowStride);
+        const float4* qv = reinterpret_cast<const float4*>(stage + kScoreTile * kScoreRowStride);
+        if (len == kScoreChunk) {
+#pragma unroll
+          for (int i = 0; i < kScoreChunk / 4; ++i) {
+            const float4 a = qv[i];
+            const float4 b = srow[i];
+            acc = __fadd_rn(acc, __fmul_rn(a.x, b.x));
+            acc = __fadd_rn(acc, __fmul_rn(a.y, b.y));
+            acc = __fadd_rn(acc, __fmul_rn(a.z, b.z));
+            acc = __fadd_rn(acc, __fmul_rn(a.w, b.w));
+          }
+        } else {
+          for (int i = 0; i < len / 4; ++i) {
+            const float4 a = qv[i];
+            const float4 b = srow[i];
+            acc = __fadd_rn(acc, __fmul_rn(a.x, b.x));
+            acc = __fadd_rn(acc, __fmul_rn(a.y, b.y));
+            acc = __fadd_rn(acc, __fmul_rn(a.z, b.z));
+            acc = __fadd_rn(acc, __fmul_rn(a.w, b.w));
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (tid < nvalid) scores[plan.score_off[r] + c0 + tid] = __fmul_rn(acc, scale);
+  }
+}
+
+// ------------------------------------------------------------------ select
+
+// Order-preserving 64-bit key: larger key = better page.  High word is the
+// score mapped to an unsigned order (-0.0 folded onto +0.0, so they tie as
+// in the CPU comparator); low word is ~page_id so lower ids win ties.
+__device__ __forceinline__ unsigned long long page_key(float score, int page) {
+  uint32_t b = __float_as_uint(score);
+  if (b == 0x80000000u) b = 0u;
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return (static_cast<unsigned long long>(b) << 32) | static_cast<uint32_t>(~page);
+}
+
+// One CTA per request (grid-stride).  Radix select (8 passes of 8 bits, MSB
+// first) finds the k-th largest key; the k winners are gathered into shared
+// memory, bitonic-sorted descending and written as page ids.
+__global__ void __launch_bounds__(kSelectThreads) select_kernel(StepPlan plan,
+                                                                const float* __restrict__ scores,
+                                                                int* __restrict__ selected) {
+  __shared__ unsigned long long keys[kSelectMaxK];
+  __shared__ int hist[256];
+  __shared__ unsigned long long s_prefix;
+  __shared__ int s_remaining;
+  __shared__ int s_count_gt;
+  __shared__ int s_count_eq;
+
+  const int B = plan.hdr[0];
+  const int mode = plan.hdr[1];
+  const int* ids_src = mode == 0 ? plan.cand_ids : plan.table;
+  const int tid = threadIdx.x;
+
+  for (int r = blockIdx.x; r < B; r += gridDim.x) {
+    const int n = plan.n_cand[r];
+    const int k = plan.sel_off[r + 1] - plan.sel_off[r];
+    if (k <= 0) continue;
+    if (k > kSelectMaxK) {
+      if (tid == 0) atomicOr(plan.status, kStatusBadInput);
+      continue;
+    }
+    const float* sc = scores + plan.score_off[r];
+    const int* ids = ids_src + plan.id_base[r];
+
+    unsigned long long threshold = 0;  // keys >= threshold are candidates for selection
+    if (k < n) {
+      // ---- radix select of the k-th largest key
+      if (tid == 0) { s_prefix = 0; s_remaining = k; }
+      unsigned long long mask = 0;
+      for (int pass = 0; pass < 8; ++pass) {
+        const int shift = 56 - 8 * pass;
+        for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+        __syncthreads();
+        const unsigned long long prefix = s_prefix;
+        for (int i = tid; i < n; i += blockDim.x) {
+          const unsigned long long key = page_key(sc[i], __ldg(ids + i));
+          if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xff], 1);
+        }
+        __syncthreads();
+        if (tid < 32) {
+          // find the digit (from 255 down) where the cumulative count reaches `remaining`
+          const int rem = s_remaining;
+          int cnt[8];
+          int local = 0;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            cnt[j] = hist[255 - (tid * 8 + j)];
+            local += cnt[j];
+          }
+          int incl = local;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (tid >= o) incl += y;
+          }
+          const int excl = incl - local;
+          if (excl < rem && incl >= rem) {
+            int acc = excl;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              if (acc + cnt[j] >= rem) {
+                const int digit = 255 - (tid * 8 + j);
+                s_prefix = prefix | (static_cast<unsigned long long>(digit) << shift);
+                s_remaining = rem - acc;
+                break;
+              }
+              acc += cnt[j];
+            }
+          }
+        }
+        __syncthreads();
+        mask |= 0xffULL << shift;
+      }
+      threshold = s_prefix;  // the exact k-th largest key
+    }
+
+    // ---- gather keys > threshold, then fill with keys == threshold
+    if (tid == 0) { s_count_gt = 0; s_count_eq = 0; }
+    __syncthreads();
+    for (int i = tid; i < n; i += blockDim.x) {
+      const unsigned long long key = page_key(sc[i], __ldg(ids + i));
+      if (key > threshold || k == n) {
+        const int pos = atomicAdd(&s_count_gt, 1);
+        if (pos < k) keys[pos] = key;
+      }
+    }
+    __syncthreads();
+    const int gt = min(s_count_gt, k);
+    if (gt < k) {
+      for (int i = tid; i < n; i += blockDim.x) {
+        const unsigned long long key = page_key(sc[i], __ldg(ids + i));
+        if (key == threshold) {
+          const int pos = gt + atomicAdd(&s_count_eq, 1);
+          if (pos < k) keys[pos] = key;
+        }
+      }
+    }
+    __syncthreads();
+
+    // ---- bitonic sort (descending) of the k winners, padded with zero keys
+    int m = 1;
+    while (m < k) m <<= 1;
+    for (int i = k + tid; i < m; i += blockDim.x) keys[i] = 0ULL;
+    __syncthreads();
+    for (int size = 2; size <= m; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int i = tid; i < m; i += blockDim.x) {
+          const int j = i ^ stride;
+          if (j > i) {
+            const unsigned long long a = keys[i], b = keys[j];
+            const bool desc = (i & size) == 0;
+            if (desc ? (a < b) : (a > b)) {
+              keys[i] = b;
+              keys[j] = a;
+            }
+          }
+        }
+        __syncthreads();
+      }
+    }
+    int* out = selected + plan.sel_off[r];
+    for (int i = tid; i < k; i += blockDim.x) out[i] = ~static_cast<int>(keys[i] & 0xffffffffULL);
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------ attention
+
+// Walks this CTA's split-K work: units u = blockIdx.x + i*gridDim.x, each a
+// run of up to `ppu` selected pages of one request; every non-empty page is
+// cut into stages of up to `tps` tokens.  Producer and consumers walk the
+// same sequence, the producer kScoreStages ahead.
+struct AttnWalk {
+  int u, p, p_end, page, n, t0;
+  bool has_page;
+};
+
+__device__ __forceinline__ void attn_unit_range(const StepPlan& plan, int B, int ppu, int u,
+                                                int* r_out, int* p_begin, int* p_end) {
+  const int r = upper_segment(plan.unit_off, B, u);
+  const int lu = u - plan.unit_off[r];
+  const int sb = plan.sel_off[r];
+  *r_out = r;
+  *p_begin = sb + lu * ppu;
+  *p_end = min(*p_begin + ppu, plan.sel_off[r + 1]);
+}
+
+__device__ __forceinline__ bool attn_walk_next(AttnWalk& w, const StepPlan& plan, int B,
+                                               int total_units, int ppu, int tps, int page_size,
+                                               const int* __restrict__ selected,
+                                               const int* __restrict__ token_counts) {
+  if (w.has_page) {
+    if (w.t0 + tps < w.n) { w.t0 += tps; return true; }
+    ++w.p;
+  }
+  w.has_page = false;
+  for (;;) {
+    if (w.p >= w.p_end) {
+      w.u += gridDim.x;
+      if (w.u >= total_units) return false;
+      int r;
+      attn_unit_range(plan, B, ppu, w.u, &r, &w.p, &w.p_end);
+      continue;
+    }
+    w.page = __ldg(selected + w.p);
+    w.n = min(__ldg(token_counts + w.page), page_size);
+    w.t0 = 0;
+    if (w.n > 0) { w.has_page = true; return true; }
+    ++w.p;
+  }
+}
+
+// Split-K flash decode.  CTA = 256 threads; thread t owns float4 columns
+// j = t + 256*m (m < SLOTS) of the H*D token row, i.e. a 4-wide slice of
+// head (4j)/D.  The D/4 threads of a head reduce q.k with xor shuffles, so
+// every thread of the group holds the logit and runs the online softmax for
+// its slice.  Stages hold `tps` K rows then `tps` V rows of one page,
+// fetched by thread 0 with two cp.async.bulk copies (they are contiguous in
+// the page-major pool).  Each unit writes (m, l) per head and acc[H*D].
+template <int SLOTS>
+__global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(
+    StepPlan plan, const float* __restrict__ queries, const float* __restrict__ key_pool,
+    const float* __restrict__ value_pool, const int* __restrict__ token_counts,
+    const int* __restrict__ selected, float* __restrict__ part_acc, float* __restrict__ part_ml,
+    int num_heads, int head_dim, int page_size, int tps, float scale) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  const int ept = num_heads * head_dim;
+  const int vec = ept >> 2;                       // float4 per token row
+  const size_t stage_floats = size_t(2) * tps * ept;
+  float* stages = reinterpret_cast<float*>(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + kAttnStages * stage_floats * 4);
+
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    for (int s = 0; s < kAttnStages; ++s) mbar_init(&full[s], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  const int B = plan.hdr[0];
+  const int total_units = plan.unit_off[B];
+  const int ppu = plan.misc[0];
+  const size_t page_floats = size_t(page_size) * ept;
+  int* status = plan.status;
+
+  AttnWalk w{static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x), 0, 0, 0, 0, 0, false};
+  auto issue = [&](int s) {
+    const int nt = min(tps, w.n - w.t0);
+    const uint32_t bytes = uint32_t(nt) * uint32_t(ept) * 4u;
+    float* st = stages + size_t(s) * stage_floats;
+    const size_t src = size_t(w.page) * page_floats + size_t(w.t0) * ept;
+    mbar_arrive_expect_tx(&full[s], 2u * bytes);
+    bulk_g2s(st, key_pool + src, bytes, &full[s]);
+    bulk_g2s(st + size_t(tps) * ept, value_pool + src, bytes, &full[s]);
+  };
+  if (tid == 0) {
+    for (int s = 0; s < kAttnStages; ++s) {
+      if (!attn_walk_next(w, plan, B, total_units, ppu, tps, page_size, selected, token_counts))
+        break;
+      issue(s);
+    }
+  }
+
+  const int gsize = head_dim >> 2;  // threads per head (power of two <= 32)
+  uint32_t g = 0;
+  bool alive = true;
+  for (int u = blockIdx.x; u < total_units && alive; u += gridDim.x) {
+    int r, p_begin, p_end;
+    attn_unit_range(plan, B, ppu, u, &r, &p_begin, &p_end);
+    float4 q[SLOTS], acc[SLOTS];
+    float mrun[SLOTS], lrun[SLOTS];
+#pragma unroll
+    for (int m = 0; m < SLOTS; ++m) {
+      const int j = tid + kAttnThreads * m;
+      q[m] = j < vec ? __ldg(reinterpret_cast<const float4*>(queries + size_t(r) * ept) + j)
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+      acc[m] = make_float4(0.f, 0.f, 0.f, 0.f);
+      mrun[m] = -INFINITY;
+      lrun[m] = 0.f;
+    }
+    for (int p = p_begin; p < p_end && alive; ++p) {
+      const int page = __ldg(selected + p);
+      const int n = min(__ldg(token_counts + page), page_size);
+      for (int t0 = 0; t0 < n; t0 += tps, ++g) {
+        const int s = g % kAttnStages;
+        if (!mbar_wait(&full[s], (g / kAttnStages) & 1, status)) { alive = false; break; }
+        const int nt = min(tps, n - t0);
+        const float4* kst = reinterpret_cast<const float4*>(stages + size_t(s) * stage_floats);
+        const float4* vst = kst + size_t(tps) * vec;
+        for (int t = 0; t < nt; ++t) {
+#pragma unroll
+          for (int m = 0; m < SLOTS; ++m) {
+            const int j = tid + kAttnThreads * m;
+            const bool ok = j < vec;
+            const float4 kk = ok ? kst[size_t(t) * vec + j] : make_float4(0.f, 0.f, 0.f, 0.f);
+            float d = q[m].x * kk.x + q[m].y * kk.y + q[m].z * kk.z + q[m].w * kk.w;
+            for (int o = gsize >> 1; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+            const float logit = d * scale;
+            const float mnew = fmaxf(mrun[m], logit);
+            const float alpha = expf(mrun[m] - mnew);
+            const float beta = expf(logit - mnew);
+            const float4 vv = ok ? vst[size_t(t) * vec + j] : make_float4(0.f, 0.f, 0.f, 0.f);
+            acc[m].x = acc[m].x * alpha + beta * vv.x;
+            acc[m].y = acc[m].y * alpha + beta * vv.y;
+            acc[m].z = acc[m].z * alpha + beta * vv.z;
+            acc[m].w = acc[m].w * alpha + beta * vv.w;
+            lrun[m] = lrun[m] * alpha + beta;
+            mrun[m] = mnew;
+          }
+        }
+        __syncthreads();  // every thread is done with stage s
+        if (tid == 0) {
+          if (attn_walk_next(w, plan, B, total_units, ppu, tps, page_size, selected, token_counts))
+            issue(s);
+        }
+      }
+    }
+    // partial of unit u
+#pragma unroll
+    for (int m = 0; m < SLOTS; ++m) {
+      const int j = tid + kAttnThreads * m;
+      if (j < vec) {
+        reinterpret_cast<float4*>(part_acc + size_t(u) * ept)[j] = acc[m];
+        if ((j & (gsize - 1)) == 0) {
+          const int head = (j << 2) / head_dim;
+          part_ml[(size_t(u) * num_heads + head) * 2 + 0] = mrun[m];
+          part_ml[(size_t(u) * num_heads + head) * 2 + 1] = lrun[m];
+        }
+      }
+    }
+  }
+}
+
+// One warp per (request, head): out = sum_u e^{m_u-M} acc_u / sum_u e^{m_u-M} l_u,
+// zero when the request attended to no token (SparseAttentionCpu returns zeros).
+__global__ void __launch_bounds__(256) combine_kernel(StepPlan plan,
+                                                      const float* __restrict__ part_acc,
+                                                      const float* __restrict__ part_ml,
+                                                      int num_heads, int head_dim,
+                                                      float* __restrict__ outputs) {
+  const int B = plan.hdr[0];
+  const int lane = threadIdx.x & 31;
+  const int ept = num_heads * head_dim;
+  const int pairs = B * num_heads;
+  for (int wg = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wg < pairs;
+       wg += (gridDim.x * blockDim.x) >> 5) {
+    const int r = wg / num_heads, h = wg % num_heads;
+    const int u0 = plan.unit_off[r], u1 = plan.unit_off[r + 1];
+    float M = -INFINITY;
+    for (int u = u0; u < u1; ++u) M = fmaxf(M, part_ml[(size_t(u) * num_heads + h) * 2]);
+    float* out = outputs + size_t(r) * ept + size_t(h) * head_dim;
+    if (M == -INFINITY) {
+      for (int d = lane; d < head_dim; d += 32) out[d] = 0.0f;
+      continue;
+    }
+    float L = 0.f;
+    for (int u = u0; u < u1; ++u) {
+      const float* ml = part_ml + (size_t(u) * num_heads + h) * 2;
+      L += ml[1] * expf(ml[0] - M);
+    }
+    for (int d = lane; d < head_dim; d += 32) {
+      float o = 0.f;
+      for (int u = u0; u < u1; ++u) {
+        const float wgt = expf(part_ml[(size_t(u) * num_heads + h) * 2] - M);
+        o += wgt * part_acc[size_t(u) * ept + size_t(h) * head_dim + d];
+      }
+      out[d] = L > 0.f ? o / L : 0.0f;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ pool maintenance
+
+// Scatter packed pages from a staging buffer into the pool and compute the
+// summary with PagedKvCache::AppendPage's formula (src/paged_kv_cache.cpp:88-99):
+// token-order sum, then * (1.0f / n), both rounded to nearest, no FMA.
+// grid (pages, ceil(E/4/256)); thread = one float4 column.
+__global__ void upload_pages_kernel(const int* __restrict__ page_ids,
+                                    const int* __restrict__ counts,
+                                    const long long* __restrict__ src_token_off,
+                                    const float* __restrict__ staged_k,
+                                    const float* __restrict__ staged_v, int ept, int page_size,
+                                    int compute_summary, float* __restrict__ key_pool,
+                                    float* __restrict__ value_pool, float* __restrict__ summaries,
+                                    int* __restrict__ token_counts, uint8_t* __restrict__ live) {
+  const int i = blockIdx.x;
+  const int j = blockIdx.y * blockDim.x + threadIdx.x;
+  const int vec = ept >> 2;
+  const int page = page_ids[i];
+  const int n = counts[i];
+  if (j < vec) {
+    const float4* sk = reinterpret_cast<const float4*>(staged_k + src_token_off[i] * ept);
+    const float4* sv = reinterpret_cast<const float4*>(staged_v + src_token_off[i] * ept);
+    float4* dk = reinterpret_cast<float4*>(key_pool + size_t(page) * page_size * ept);
+    float4* dv = reinterpret_cast<float4*>(value_pool + size_t(page) * page_size * ept);
+    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int t = 0; t < n; ++t) {
+      const float4 k = sk[size_t(t) * vec + j];
+      dk[size_t(t) * vec + j] = k;
+      dv[size_t(t) * vec + j] = sv[size_t(t) * vec + j];
+      sum.x = __fadd_rn(sum.x, k.x);
+      sum.y = __fadd_rn(sum.y, k.y);
+      sum.z = __fadd_rn(sum.z, k.z);
+      sum.w = __fadd_rn(sum.w, k.w);
+    }
+    float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (compute_summary && n > 0) {
+      const float inv = __fdiv_rn(1.0f, static_cast<float>(n));
+      out = make_float4(__fmul_rn(sum.x, inv), __fmul_rn(sum.y, inv), __fmul_rn(sum.z, inv),
+                        __fmul_rn(sum.w, inv));
+    }
+    reinterpret_cast<float4*>(summaries + size_t(page) * ept)[j] = out;
+  }
+  if (blockIdx.y == 0 && threadIdx.x == 0) {
+    token_counts[page] = n;
+    live[page] = 1;
+  }
+}
+
+__global__ void set_summaries_kernel(const int* __restrict__ page_ids,
+                                     const float* __restrict__ staged, int ept,
+                                     float* __restrict__ summaries) {
+  const int i = blockIdx.x;
+  const int page = page_ids[i];
+  for (int e = threadIdx.x; e < ept; e += blockDim.x)
+    summaries[size_t(page) * ept + e] = staged[size_t(i) * ept + e];
+}
+
+// Token append.  One block per distinct page; its tokens (token_first[i] ..
+// token_first[i+1]) are applied in offset order with PagedKvCache::AppendToken's
+// running mean (src/paged_kv_cache.cpp:231-238): s = (s*old + k) / (old + 1).
+// Optional page-table entries (slot, position, page) are written first.
+__global__ void append_tokens_kernel(const int* __restrict__ group_page,
+                                     const int* __restrict__ token_first,
+                                     const int* __restrict__ token_offset,
+                                     const float* __restrict__ staged_k,
+                                     const float* __restrict__ staged_v, int ept, int page_size,
+                                     float* __restrict__ key_pool, float* __restrict__ value_pool,
+                                     float* __restrict__ summaries, int* __restrict__ token_counts,
+                                     uint8_t* __restrict__ live) {
+  const int gidx = blockIdx.x;
+  const int page = group_page[gidx];
+  float* summ = summaries + size_t(page) * ept;
+  int last = -1;
+  for (int i = token_first[gidx]; i < token_first[gidx + 1]; ++i) {
+    const int off = token_offset[i];
+    const float old_c = static_cast<float>(off);
+    const float new_c = __fadd_rn(old_c, 1.0f);
+    float* dk = key_pool + (size_t(page) * page_size + off) * ept;
+    float* dv = value_pool + (size_t(page) * page_size + off) * ept;
+    for (int e = threadIdx.x; e < ept; e += blockDim.x) {
+      const float k = staged_k[size_t(i) * ept + e];
+      dk[e] = k;
+      dv[e] = staged_v[size_t(i) * ept + e];
+      const float s = off == 0 ? 0.0f : summ[e];
+      summ[e] = __fdiv_rn(__fadd_rn(__fmul_rn(s, old_c), k), new_c);
+    }
+    last = max(last, off);
+  }
+  if (threadIdx.x == 0 && last >= 0) {
+    token_counts[page] = last + 1;
+    live[page] = 1;
+  }
+}
+
+__global__ void table_write_kernel(const int* __restrict__ entries, int n, int stride,
+                                   int* __restrict__ table, int* __restrict__ table_n) {
+  // entries: triples (slot, position, page)
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int slot = entries[3 * i], pos = entries[3 * i + 1], page = entries[3 * i + 2];
+  table[size_t(slot) * stride + pos] = page;
+  atomicMax(table_n + slot, pos + 1);
+}
+
+__global__ void table_set_count_kernel(const int* __restrict__ pairs, int n,
+                                       int* __restrict__ table_n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) table_n[pairs[2 * i]] = pairs[2 * i + 1];
+}
+
+// DevicePagePool::MarkPagesFree: count 0, not live, summary zeroed.
+__global__ void free_pages_kernel(const int* __restrict__ page_ids, int ept,
+                                  float* __restrict__ summaries, int* __restrict__ token_counts,
+                                  uint8_t* __restrict__ live) {
+  const int page = page_ids[blockIdx.x];
+  for (int e = threadIdx.x; e < ept; e += blockDim.x) summaries[size_t(page) * ept + e] = 0.0f;
+  if (threadIdx.x == 0) {
+    token_counts[page] = 0;
+    live[page] = 0;
+  }
+}
+
+// The reference's synthetic prompt / decode payload hash
+// (src/device_page_pool.cpp:102-138): boost-style combine of the indices,
+// a 32-bit finaliser, then (x % 2001 - 1000) / 1000.
+__device__ __forceinline__ uint32_t combine_hash(uint32_t x, int v, uint32_t salt) {
+  return x ^ (static_cast<uint32_t>(v + static_cast<int>(salt)) + (x << 6) + (x >> 2));
+}
+__device__ __forceinline__ float hash_to_unit(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return static_cast<float>(static_cast<int>(x % 2001u) - 1000) / 1000.0f;
+}
+__device__ __forceinline__ float prompt_value(int request, int page_idx, int token, int element,
+                                              int stream) {
+  uint32_t x = 0x9e3779b9u;
+  x = combine_hash(x, request, 0x85ebca6bu);
+  x = combine_hash(x, page_idx, 0xc2b2ae35u);
+  x = combine_hash(x, token, 0x27d4eb2fu);
+  x = combine_hash(x, element, 0x165667b1u);
+  x = combine_hash(x, stream, 0xd3a2646cu);
+  return hash_to_unit(x);
+}
+__device__ __forceinline__ float decode_value(int request, int step, int element, int stream) {
+  uint32_t x = 0x9e3779b9u;
+  x = combine_hash(x, request, 0x85ebca6bu);
+  x = combine_hash(x, step, 0xc2b2ae35u);
+  x = combine_hash(x, element, 0x165667b1u);
+  x = combine_hash(x, stream, 0xd3a2646cu);
+  return hash_to_unit(x);
+}
+
+// Synthetic prefill: page i is page_idx i of `request`; summary by AppendPage's formula.
+__global__ void prefill_synthetic_kernel(const int* __restrict__ page_ids,
+                                         const int* __restrict__ counts, int request, int ept,
+                                         int page_size, float* __restrict__ key_pool,
+                                         float* __restrict__ value_pool,
+                                         float* __restrict__ summaries,
+                                         int* __restrict__ token_counts,
+                                         uint8_t* __restrict__ live) {
+  const int i = blockIdx.x;
+  const int page = page_ids[i];
+  const int n = counts[i];
+  for (int e = threadIdx.x; e < ept; e += blockDim.x) {
+    float sum = 0.0f;
+    for (int t = 0; t < n; ++t) {
+      const float k = prompt_value(request, i, t, e, 1);
+      const float v = prompt_value(request, i, t, e, 2);
+      key_pool[(size_t(page) * page_size + t) * ept + e] = k;
+      value_pool[(size_t(page) * page_size + t) * ept + e] = v;
+      sum = __fadd_rn(sum, k);
+    }
+    summaries[size_t(page) * ept + e] =
+        n > 0 ? __fmul_rn(sum, __fdiv_rn(1.0f, static_cast<float>(n))) : 0.0f;
+  }
+  if (threadIdx.x == 0) {
+    token_counts[page] = n;
+    live[page] = 1;
+  }
+}
+
+// Synthetic append: token i = decode step steps[i] of request reqs[i].
+__global__ void append_synthetic_kernel(const int* __restrict__ group_page,
+                                        const int* __restrict__ token_first,
+                                        const int* __restrict__ token_offset,
+                                        const int* __restrict__ reqs, const int* __restrict__ steps,
+                                        int ept, int page_size, float* __restrict__ key_pool,
+                                        float* __restrict__ value_pool,
+                                        float* __restrict__ summaries,
+                                        int* __restrict__ token_counts,
+                                        uint8_t* __restrict__ live) {
+  const int gidx = blockIdx.x;
+  const int page = group_page[gidx];
+  float* summ = summaries + size_t(page) * ept;
+  int last = -1;
+  for (int i = token_first[gidx]; i < token_first[gidx + 1]; ++i) {
+    const int off = token_offset[i];
+    const float old_c = static_cast<float>(off);
+    const float new_c = __fadd_rn(old_c, 1.0f);
+    for (int e = threadIdx.x; e < ept; e += blockDim.x) {
+      const float k = decode_value(reqs[i], steps[i], e, 1);
+      key_pool[(size_t(page) * page_size + off) * ept + e] = k;
+      value_pool[(size_t(page) * page_size + off) * ept + e] = decode_value(reqs[i], steps[i], e, 2);
+      const float s = off == 0 ? 0.0f : summ[e];
+      summ[e] = __fdiv_rn(__fadd_rn(__fmul_rn(s, old_c), k), new_c);
+    }
+    last = max(last, off);
+  }
+  if (threadIdx.x == 0 && last >= 0) {
+    token_counts[page] = last + 1;
+    live[page] = 1;
+  }
+}
+
+// Counter-based normal workload: Irwin-Hall(4) of 16-bit uniforms from a
+// splitmix64-style mix of (seed, kind, index).  Integer sum, one conversion,
+// one multiply: bit-identical on host and device.
+__host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
+  return z ^ (z >> 31);
+}
+__host__ __device__ __forceinline__ float normal_value(uint64_t seed_mix, uint64_t index) {
+  const uint64_t h = mix64(index ^ seed_mix);
+  const int sum = static_cast<int>(h & 0xffff) + static_cast<int>((h >> 16) & 0xffff) +
+                  static_cast<int>((h >> 32) & 0xffff) + static_cast<int>((h >> 48) & 0xffff);
+#ifdef __CUDA_ARCH__
+  return __fmul_rn(static_cast<float>(sum - 131070), 2.6429e-5f);
+#else
+  return static_cast<float>(sum - 131070) * 2.6429e-5f;
+#endif
+}
+__host__ __device__ __forceinline__ uint64_t normal_seed_mix(uint64_t seed, int kind) {
+  return mix64(seed * 0x9e3779b97f4a7c15ULL + static_cast<uint64_t>(kind));
+}
+__host__ __device__ __forceinline__ uint64_t normal_index(int request, long long token, int ept,
+                                                          int element) {
+  return (static_cast<uint64_t>(request) << 40) + static_cast<uint64_t>(token) * ept +
+         static_cast<uint64_t>(element);
+}
+
+// grid (pages, ceil(E/256)); thread = one element column of one page.
+__global__ void generate_normal_kernel(const int* __restrict__ page_ids,
+                                       const int* __restrict__ counts,
+                                       const int* __restrict__ reqs,
+                                       const int* __restrict__ first_token, int ept,
+                                       int page_size, uint64_t kmix, uint64_t vmix,
+                                       float* __restrict__ key_pool,
+                                       float* __restrict__ value_pool,
+                                       float* __restrict__ summaries,
+                                       int* __restrict__ token_counts,
+                                       uint8_t* __restrict__ live) {
+  const int i = blockIdx.x;
+  const int e = blockIdx.y * blockDim.x + threadIdx.x;
+  const int page = page_ids[i];
+  const int n = counts[i];
+  if (e < ept) {
+    float sum = 0.0f;
+    for (int t = 0; t < n; ++t) {
+      const uint64_t idx = normal_index(reqs[i], first_token[i] + t, ept, e);
+      const float k = normal_value(kmix, idx);
+      key_pool[(size_t(page) * page_size + t) * ept + e] = k;
+      value_pool[(size_t(page) * page_size + t) * ept + e] = normal_value(vmix, idx);
+      sum = __fadd_rn(sum, k);
+    }
+    summaries[size_t(page) * ept + e] =
+        n > 0 ? __fmul_rn(sum, __fdiv_rn(1.0f, static_cast<float>(n))) : 0.0f;
+  }
+  if (blockIdx.y == 0 && threadIdx.x == 0) {
+    token_counts[page] = n;
+    live[page] = 1;
+  }
+}
+
+}  // namespace dsdk

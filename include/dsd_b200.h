@@ -1,0 +1,204 @@
+/*
+ * dsd_b200.h -- C ABI of the B200 batched page-level dynamic sparse decode path.
+ *
+ * Plain C: pointers, sizes and status codes only.  Every function returns
+ * DSD_OK (0) or a negative-free error code below and leaves a message for
+ * dsd_last_error() (thread local).  Host pointers are borrowed for the call.
+ *
+ * The entry points replace the device side of the reference's
+ * SparseCudaContext / DevicePagePool (JudySun233/15-618_Dynamic_Sparse_Decode):
+ *   include/dsd/cuda_sparse_attention.h:50-104  (SparseCudaContext)
+ *   include/dsd/device_page_pool.h:17-100       (DevicePagePool)
+ * The C++ drop-in classes in the package (csrc/host) are thin wrappers over
+ * this ABI; a C, cgo, JNI or ctypes caller binds it directly.
+ *
+ * Data layout in HBM (one context = one GPU):
+ *   keys, values  float [capacity_pages][page_size][H*D]   page-major, 16 B aligned rows
+ *   summaries     float [capacity_pages][H*D]              mean key of the page
+ *   token_counts  int32 [capacity_pages]; live  uint8 [capacity_pages]
+ *   request page tables int32 [max_requests][max_pages_per_request] (+ counts)
+ */
+#ifndef DSD_B200_H_
+#define DSD_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  The C++ wrapper maps them to the reference's exception
+ * types: EINVAL -> std::invalid_argument, ERANGE -> std::out_of_range,
+ * everything else -> std::runtime_error (include/dsd/cuda_utils.h:43-53). */
+enum {
+  DSD_OK = 0,
+  DSD_EINVAL = 1,       /* bad argument / size / capacity overflow            */
+  DSD_ERANGE = 2,       /* page id or token offset out of range               */
+  DSD_ENOMEM = 3,       /* device allocation failed / page pool exhausted     */
+  DSD_ECUDA = 4,        /* CUDA runtime error                                 */
+  DSD_ETIMEOUT = 5,     /* a bounded device-side wait gave up                 */
+  DSD_EUNAVAILABLE = 6  /* no sm_100 GPU visible                              */
+};
+
+/* SparseBatchOutputMode (include/dsd/cuda_sparse_attention.h:19-23). */
+enum { DSD_OUTPUT_NONE = 0, DSD_OUTPUT_OUTPUTS = 1, DSD_OUTPUT_DEBUG = 2 };
+
+/* ModelConfig (include/dsd/config.h:5-10). */
+typedef struct dsd_model_config {
+  int32_t num_heads;
+  int32_t head_dim;     /* power of two in [4, 128] */
+  int32_t page_size;
+  int32_t top_k_pages;
+} dsd_model_config;
+
+/* Capacities fixed at creation (SparseCudaContext ctor arguments,
+ * include/dsd/cuda_sparse_attention.h:52-57, plus the device page tables). */
+typedef struct dsd_ctx_options {
+  int32_t capacity_pages;
+  int32_t max_batch;              /* <= 1024 */
+  int32_t max_candidates;         /* total candidate pages per step */
+  int32_t max_selected;           /* total selected pages per step */
+  int32_t max_requests;           /* device page-table slots (0 = none) */
+  int32_t max_pages_per_request;  /* page-table row length */
+} dsd_ctx_options;
+
+/* StageTimings of one step (include/dsd/types.h:69-75); CUDA-event ms. */
+typedef struct dsd_step_timing {
+  float score_ms;
+  float topk_ms;
+  float attention_ms;   /* attention + log-sum-exp combine */
+  float total_ms;       /* first to last kernel of the step */
+} dsd_step_timing;
+
+/* DeviceTransferStats (include/dsd/types.h:50-57). */
+typedef struct dsd_transfer_stats {
+  uint64_t h2d_bytes, d2h_bytes, h2d_calls, d2h_calls, h2d_large_calls, d2h_large_calls;
+} dsd_transfer_stats;
+
+typedef struct dsd_ctx dsd_ctx;
+
+const char* dsd_last_error(void);
+
+/* SparseAttentionCudaAvailable (include/dsd/cuda_sparse_attention.h:17):
+ * 1 when an sm_100 device is visible, else 0. */
+int dsd_available(void);
+
+/* SparseCudaContext ctor / dtor (src/cuda/sparse_batched_attention.cu:444-549);
+ * allocates the page pool (DevicePagePool ctor, src/device_page_pool.cpp:241-284)
+ * and all per-step scratch once.  No allocation happens per step. */
+int dsd_ctx_create(int device, const dsd_model_config* config, const dsd_ctx_options* options,
+                   dsd_ctx** out);
+int dsd_ctx_destroy(dsd_ctx* ctx);
+
+/* Device pointers for callers that keep their own data in HBM (bench, tests). */
+int dsd_ctx_device_pointers(dsd_ctx* ctx, float** keys, float** values, float** summaries,
+                            int32_t** token_counts);
+/* The CUDA stream every call of this context is ordered on (cudaStream_t). */
+void* dsd_ctx_stream(dsd_ctx* ctx);
+
+/* DevicePagePool::Reset (src/device_page_pool.cpp:286-302): zero counts, live
+ * flags and summaries; drop every request page table. */
+int dsd_pool_reset(dsd_ctx* ctx);
+
+/* DevicePagePool::UploadPage / UploadPagesFromCache / UploadPromptDirect
+ * (src/device_page_pool.cpp:304-624).  keys/values hold the pages' tokens
+ * back to back ([sum token_counts][H*D]).  compute_summary = 1 computes the
+ * summary on the device with PagedKvCache::AppendPage's formula
+ * (src/paged_kv_cache.cpp:88-99: token-order sum, then * (1/n)); 0 leaves it
+ * zero (AppendPage with compute_summary = false). */
+int dsd_pool_upload_pages(dsd_ctx* ctx, const int32_t* page_ids, const int32_t* token_counts,
+                          int n, const float* keys, const float* values, int compute_summary);
+
+/* Overwrite page summaries with host values ([n][H*D]), e.g. a host cache
+ * whose summaries were built by running-mean appends. */
+int dsd_pool_upload_summaries(dsd_ctx* ctx, const int32_t* page_ids, int n,
+                              const float* summaries);
+
+/* DevicePagePool::PrefillPromptSynthetic (src/device_page_pool.cpp:626-679):
+ * K/V from the reference's integer hash; summary by AppendPage's formula. */
+int dsd_pool_prefill_synthetic(dsd_ctx* ctx, const int32_t* page_ids,
+                               const int32_t* token_counts, int n, int request_id);
+
+/* Long-context workload generator (no reference counterpart: the reference
+ * draws everything on the host).  Page i holds tokens
+ * [first_token[i], first_token[i] + token_counts[i]) of request
+ * request_ids[i]; values are Irwin-Hall(4) normals of (seed, kind, index),
+ * summaries by AppendPage's formula. */
+int dsd_pool_generate_normal(dsd_ctx* ctx, const int32_t* page_ids, const int32_t* token_counts,
+                             const int32_t* request_ids, const int32_t* first_token, int n,
+                             uint64_t seed);
+/* Host copy of the same generator (queries, checks). kind 0=query 1=key 2=value. */
+void dsd_generate_normal_host(uint64_t seed, int kind, uint64_t first_index, int64_t count,
+                              float* out);
+
+/* DevicePagePool::UploadTokensDirect / UploadTokensFromCache + K7
+ * (src/device_page_pool.cpp:700-902), with the summary updated ON DEVICE by
+ * PagedKvCache::AppendToken's running mean (src/paged_kv_cache.cpp:231-238).
+ * Token i goes to (page_ids[i], token_offsets[i]); the page's count becomes
+ * token_offsets[i] + 1.  Tokens of one page must come in offset order.
+ * request_ids may be NULL; otherwise a token whose offset is 0 also appends
+ * its page to that request's device page table. */
+int dsd_append_tokens(dsd_ctx* ctx, const int32_t* page_ids, const int32_t* token_offsets,
+                      const int32_t* request_ids, int n, const float* keys, const float* values);
+
+/* DevicePagePool::AppendTokensSynthetic + K9 (src/device_page_pool.cpp:904-983). */
+int dsd_append_tokens_synthetic(dsd_ctx* ctx, const int32_t* page_ids,
+                                const int32_t* token_offsets, const int32_t* request_ids,
+                                const int32_t* decode_steps, int n);
+
+/* DevicePagePool::MarkPagesFree (src/device_page_pool.cpp:989-1043). */
+int dsd_pool_free_pages(dsd_ctx* ctx, const int32_t* page_ids, int n);
+
+/* DevicePagePool::DownloadPage / DownloadMetadata (src/device_page_pool.cpp:1045-1091).
+ * keys/values receive page_size*H*D floats, summary H*D (each nullable). */
+int dsd_download_page(dsd_ctx* ctx, int page_id, float* keys, float* values, float* summary,
+                      int32_t* token_count);
+int dsd_download_metadata(dsd_ctx* ctx, int32_t* token_counts, uint8_t* live_mask);
+
+int dsd_get_transfer_stats(dsd_ctx* ctx, dsd_transfer_stats* out);
+int dsd_reset_transfer_stats(dsd_ctx* ctx);
+
+/* SparseCudaContext::RunBatch (src/cuda/sparse_batched_attention.cu:574-838)
+ * with the caller's candidate lists in CSR: request r scores candidates
+ * cand_ids[cand_offsets[r] .. cand_offsets[r+1]) against summaries with the
+ * query queries[r*H*D ..], selects min(k, n_r) pages (score desc, page id
+ * asc) and attends over their tokens.  Outputs [batch][H*D]; in
+ * DSD_OUTPUT_DEBUG mode scores [C] (candidate order) and selected ids packed
+ * by min(k, n_r) per request.  timing != 0 fills *timing with CUDA events. */
+int dsd_decode_batch(dsd_ctx* ctx, int batch, const float* queries, const int32_t* cand_offsets,
+                     const int32_t* cand_ids, int output_mode, int timing, float* outputs,
+                     float* scores, int32_t* selected, dsd_step_timing* out_timing);
+
+/* Device request page tables (north-star item 5: no host CSR packing).
+ * set replaces the request's page list, append extends it, release drops it
+ * (and frees its pages on the device when free_pages != 0). */
+int dsd_request_set_pages(dsd_ctx* ctx, int request_id, const int32_t* page_ids, int n);
+int dsd_request_append_pages(dsd_ctx* ctx, int request_id, const int32_t* page_ids, int n);
+int dsd_request_release(dsd_ctx* ctx, int request_id, int free_pages);
+int dsd_request_num_pages(dsd_ctx* ctx, int request_id);
+
+/* One decode step over requests whose candidates are their device page
+ * tables (the continuous-batching step).  The CSR offsets are a device prefix
+ * sum; only the queries cross H2D and the outputs D2H. */
+int dsd_decode_step(dsd_ctx* ctx, const int32_t* request_ids, int batch, const float* queries,
+                    int output_mode, int timing, float* outputs, float* scores,
+                    int32_t* selected, dsd_step_timing* out_timing);
+
+/* Device-resident variant: bind a request set once, then run steps whose
+ * queries and outputs already live in HBM ([batch][H*D] each).  The step is
+ * replayed from a CUDA graph; nothing crosses PCIe. */
+int dsd_bind_requests(dsd_ctx* ctx, const int32_t* request_ids, int batch);
+int dsd_decode_bound(dsd_ctx* ctx, const float* d_queries, float* d_outputs);
+/* Same, launched kernel by kernel with CUDA events around each stage. */
+int dsd_decode_bound_timed(dsd_ctx* ctx, const float* d_queries, float* d_outputs,
+                           dsd_step_timing* out_timing);
+
+/* Number of kernels one decode step launches (for launch accounting). */
+int dsd_kernels_per_step(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSD_B200_H_ */

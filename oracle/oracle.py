@@ -1,0 +1,269 @@
+"""ctypes front end for the CPU checkers (test infrastructure only).
+
+* ``liboracle.so`` -- the restatement of the reference algorithm
+  (``oracle/dsd_oracle.cpp``); always available once ``make -C oracle`` ran.
+* ``_ref/libdsd_ref.so`` -- the unmodified reference CPU sources plus a flat
+  shim (``oracle/ref_shim.cpp``); present where the reference sources were
+  available at build time.
+
+Everything here is numpy in / numpy out; nothing touches a GPU.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from dataclasses import dataclass
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+REF_LIB_PATH = os.path.join(HERE, "_ref", "libdsd_ref.so")
+
+_F = ctypes.POINTER(ctypes.c_float)
+_I = ctypes.POINTER(ctypes.c_int)
+
+
+def build(with_reference: bool | None = None) -> None:
+    """Compile the restatement (and, when the reference sources exist, _ref)."""
+    targets = ["oracle"]
+    ref_root = os.environ.get("REF_ROOT", "/root/reference")
+    if with_reference is None:
+        with_reference = os.path.isdir(os.path.join(ref_root, "src"))
+    if with_reference:
+        targets.append("ref")
+    subprocess.run(["make", "-s", "-C", HERE, f"REF_ROOT={ref_root}", *targets], check=True)
+
+
+_lib = None
+_ref = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build(with_reference=False)
+        L = ctypes.CDLL(LIB_PATH)
+        L.orc_page_summary.argtypes = [_F, ctypes.c_int, ctypes.c_int, _F]
+        L.orc_running_mean_append.argtypes = [_F, _F, ctypes.c_int, ctypes.c_int]
+        L.orc_sparse_decode.argtypes = [ctypes.c_int] * 4 + [_F, _F, _F, _I, ctypes.c_int, _F,
+                                                             _I, _I, _I, _F, _F, ctypes.c_int]
+        L.orc_dense_decode.argtypes = [ctypes.c_int] * 3 + [_F, _F, _I, ctypes.c_int, _F, _I, _I, _F]
+        L.orc_synthetic_batch_contexts.argtypes = [ctypes.c_int] * 5 + [_I]
+        L.orc_synthetic_batch_contexts.restype = ctypes.c_int
+        L.orc_synthetic_batch_fill.argtypes = [ctypes.c_int] * 7 + [_F, _F, _F, _I, _F, _I, _I]
+        L.orc_deterministic_token_vector.argtypes = [ctypes.c_int] * 4 + [_F]
+        L.orc_continuous_workload.argtypes = [ctypes.c_int] * 9 + [_I, _I, _I, _I, _F, _F, _F]
+        L.orc_normal_value.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_uint64]
+        L.orc_normal_value.restype = ctypes.c_float
+        L.orc_normal_fill.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_uint64,
+                                      ctypes.c_longlong, _F]
+        _lib = L
+    return _lib
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_LIB_PATH)
+
+
+def ref():
+    global _ref
+    if _ref is None:
+        R = ctypes.CDLL(REF_LIB_PATH)
+        R.ref_batch_create.argtypes = [ctypes.c_int] * 8
+        R.ref_batch_create.restype = ctypes.c_void_p
+        R.ref_batch_destroy.argtypes = [ctypes.c_void_p]
+        R.ref_batch_capacity.argtypes = [ctypes.c_void_p]
+        R.ref_batch_total_candidates.argtypes = [ctypes.c_void_p]
+        R.ref_batch_export.argtypes = [ctypes.c_void_p, _F, _F, _F, _I, _F, _I, _I]
+        R.ref_batch_sparse_cpu.argtypes = [ctypes.c_void_p, _I, _F, _F]
+        R.ref_batch_dense_cpu.argtypes = [ctypes.c_void_p, _F]
+        R.ref_batch_time_sparse_cpu.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
+        R.ref_batch_time_sparse_cpu.restype = ctypes.c_double
+        _ref = R
+    return _ref
+
+
+def fp(a):
+    return a.ctypes.data_as(_F)
+
+
+def ip(a):
+    return a.ctypes.data_as(_I)
+
+
+@dataclass
+class Batch:
+    """A decode batch in the flat layout shared by the oracle and the CUDA path."""
+    num_heads: int
+    head_dim: int
+    page_size: int
+    top_k: int
+    key_pool: np.ndarray      # [capacity, page_size, E] float32
+    value_pool: np.ndarray    # [capacity, page_size, E] float32
+    summaries: np.ndarray     # [capacity, E] float32
+    token_counts: np.ndarray  # [capacity] int32
+    queries: np.ndarray       # [B, E] float32
+    cand_offsets: np.ndarray  # [B+1] int32
+    cand_ids: np.ndarray      # [C] int32
+
+    @property
+    def ept(self) -> int:
+        return self.num_heads * self.head_dim
+
+    @property
+    def capacity(self) -> int:
+        return int(self.token_counts.shape[0])
+
+    @property
+    def batch(self) -> int:
+        return int(self.queries.shape[0])
+
+    def selected_offsets(self, top_k: int | None = None) -> np.ndarray:
+        k = self.top_k if top_k is None else top_k
+        n = np.diff(self.cand_offsets)
+        return np.concatenate([[0], np.cumsum(np.clip(np.minimum(n, k), 0, None))]).astype(np.int32)
+
+
+def _empty_batch(h, d, p, k, capacity, batch, total_cand):
+    e = h * d
+    return Batch(h, d, p, k,
+                 np.zeros((capacity, p, e), np.float32), np.zeros((capacity, p, e), np.float32),
+                 np.zeros((capacity, e), np.float32), np.zeros(capacity, np.int32),
+                 np.zeros((batch, e), np.float32), np.zeros(batch + 1, np.int32),
+                 np.zeros(total_cand, np.int32))
+
+
+def synthetic_batch(num_heads, head_dim, page_size, top_k, batch, min_ctx, max_ctx, seed) -> Batch:
+    """BuildSyntheticBatch restated (mt19937 U(-1,1), LIFO page ids)."""
+    L = lib()
+    ctx = np.zeros(batch, np.int32)
+    cap = L.orc_synthetic_batch_contexts(page_size, batch, min_ctx, max_ctx, seed, ip(ctx))
+    b = _empty_batch(num_heads, head_dim, page_size, top_k, cap, batch, cap)
+    L.orc_synthetic_batch_fill(num_heads, head_dim, page_size, batch, min_ctx, max_ctx, seed,
+                               fp(b.key_pool), fp(b.value_pool), fp(b.summaries),
+                               ip(b.token_counts), fp(b.queries), ip(b.cand_offsets),
+                               ip(b.cand_ids))
+    return b
+
+
+def sparse_decode(b: Batch, top_k: int | None = None, n_threads: int = 1):
+    """sparse_cpu over a flat batch.  Returns (selected, sel_offsets, outputs, scores)."""
+    k = b.top_k if top_k is None else top_k
+    so = b.selected_offsets(k)
+    sel = np.zeros(max(1, int(so[-1])), np.int32)
+    out = np.zeros((b.batch, b.ept), np.float32)
+    scores = np.zeros(max(1, len(b.cand_ids)), np.float32)
+    lib().orc_sparse_decode(b.num_heads, b.head_dim, b.page_size, k, fp(b.key_pool),
+                            fp(b.value_pool), fp(b.summaries), ip(b.token_counts), b.batch,
+                            fp(b.queries), ip(b.cand_offsets), ip(b.cand_ids), ip(sel), fp(out),
+                            fp(scores), n_threads)
+    return sel[: so[-1]], so, out, scores[: len(b.cand_ids)]
+
+
+def dense_decode(b: Batch):
+    out = np.zeros((b.batch, b.ept), np.float32)
+    lib().orc_dense_decode(b.num_heads, b.head_dim, b.page_size, fp(b.key_pool), fp(b.value_pool),
+                           ip(b.token_counts), b.batch, fp(b.queries), ip(b.cand_offsets),
+                           ip(b.cand_ids), fp(out))
+    return out
+
+
+def page_summary(keys: np.ndarray) -> np.ndarray:
+    keys = np.ascontiguousarray(keys, np.float32)
+    out = np.zeros(keys.shape[-1], np.float32)
+    lib().orc_page_summary(fp(keys), keys.shape[0], keys.shape[-1], fp(out))
+    return out
+
+
+def running_mean_append(summary: np.ndarray, key: np.ndarray, old_count: int) -> np.ndarray:
+    s = np.array(summary, np.float32, copy=True)
+    key = np.ascontiguousarray(key, np.float32)
+    lib().orc_running_mean_append(fp(s), fp(key), old_count, s.shape[0])
+    return s
+
+
+def deterministic_token_vector(count, request_id, decode_step, stream) -> np.ndarray:
+    out = np.zeros(count, np.float32)
+    lib().orc_deterministic_token_vector(count, request_id, decode_step, stream, fp(out))
+    return out
+
+
+def normal_fill(seed: int, kind: int, first_index: int, count: int) -> np.ndarray:
+    out = np.zeros(count, np.float32)
+    lib().orc_normal_fill(seed, kind, first_index, count, fp(out))
+    return out
+
+
+def continuous_workload(num_heads, head_dim, num_requests, arrival_window, min_prompt,
+                        max_prompt, min_decode, max_decode, seed, with_payloads=True):
+    """BuildSyntheticContinuousWorkload restated; specs in (arrival, id) order."""
+    L = lib()
+    ids, arr, pt, ds = (np.zeros(num_requests, np.int32) for _ in range(4))
+    if not with_payloads:
+        L.orc_continuous_workload(num_heads, head_dim, num_requests, arrival_window, min_prompt,
+                                  max_prompt, min_decode, max_decode, seed, ip(ids), ip(arr),
+                                  ip(pt), ip(ds), None, None, None)
+        return dict(request_ids=ids, arrival_steps=arr, prompt_tokens=pt, decode_steps=ds)
+    # first pass for the sizes, second for the payloads
+    L.orc_continuous_workload(num_heads, head_dim, num_requests, arrival_window, min_prompt,
+                              max_prompt, min_decode, max_decode, seed, ip(ids), ip(arr), ip(pt),
+                              ip(ds), None, None, None)
+    e = num_heads * head_dim
+    total = int(pt.sum())
+    pk = np.zeros((total, e), np.float32)
+    pv = np.zeros((total, e), np.float32)
+    q = np.zeros((num_requests, e), np.float32)
+    L.orc_continuous_workload(num_heads, head_dim, num_requests, arrival_window, min_prompt,
+                              max_prompt, min_decode, max_decode, seed, ip(ids), ip(arr), ip(pt),
+                              ip(ds), fp(pk), fp(pv), fp(q))
+    return dict(request_ids=ids, arrival_steps=arr, prompt_tokens=pt, decode_steps=ds,
+                prompt_keys=pk, prompt_values=pv, initial_queries=q)
+
+
+class RefBatch:
+    """The reference's own BuildSyntheticBatch + sparse_cpu (needs _ref)."""
+
+    def __init__(self, num_heads, head_dim, page_size, top_k, batch, min_ctx, max_ctx, seed):
+        self.R = ref()
+        self.h = self.R.ref_batch_create(num_heads, head_dim, page_size, top_k, batch, min_ctx,
+                                         max_ctx, seed)
+        self.cfg = (num_heads, head_dim, page_size, top_k)
+        self.batch = batch
+
+    def close(self):
+        if self.h:
+            self.R.ref_batch_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def export(self) -> Batch:
+        h, d, p, k = self.cfg
+        cap = self.R.ref_batch_capacity(self.h)
+        c = self.R.ref_batch_total_candidates(self.h)
+        b = _empty_batch(h, d, p, k, cap, self.batch, c)
+        self.R.ref_batch_export(self.h, fp(b.key_pool), fp(b.value_pool), fp(b.summaries),
+                                ip(b.token_counts), fp(b.queries), ip(b.cand_offsets),
+                                ip(b.cand_ids))
+        return b
+
+    def sparse_cpu(self):
+        b = self.export()
+        so = b.selected_offsets()
+        sel = np.zeros(max(1, int(so[-1])), np.int32)
+        out = np.zeros((b.batch, b.ept), np.float32)
+        scores = np.zeros(max(1, len(b.cand_ids)), np.float32)
+        self.R.ref_batch_sparse_cpu(self.h, ip(sel), fp(out), fp(scores))
+        return sel[: so[-1]], so, out, scores[: len(b.cand_ids)]
+
+    def dense_cpu(self):
+        out = np.zeros((self.batch, self.cfg[0] * self.cfg[1]), np.float32)
+        self.R.ref_batch_dense_cpu(self.h, fp(out))
+        return out
+
+    def time_sparse_cpu(self, iterations: int, n_threads: int) -> float:
+        return self.R.ref_batch_time_sparse_cpu(self.h, iterations, n_threads)
