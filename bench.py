@@ -1,0 +1,342 @@
+"""Benchmark of the batched page-level sparse decode step (one JSON line on rank 0).
+
+Workload (the north star's headline): 64 requests per GPU,
+context ~ U{16384..32768} tokens (numpy default_rng(7)), 32 heads x 128 dims,
+page_size 16, top_k_pages 64, fp32 K/V/Q ~ N(0,1) (Irwin-Hall(4) counter-based
+generator, seed 7) generated on the device.  One step = one decode token for
+every request: score all candidate pages, select the top 64, attend.
+
+  value  tokens/s with queries and outputs resident in HBM (the step launched
+         kernel by kernel on the context stream; CUDA events, max over ranks)
+  e2e    tokens/s through the public C ABI call dsd_decode_step with host
+         queries in and host outputs out (H2D + D2H inside the timed region)
+
+--impl reference times the reference's own sparse_cpu code (oracle/_ref) on a
+bounded sample of the same workload shape on the host cores.
+
+Multi-GPU: torchrun, one process per GPU, each GPU owns its own 64 requests
+and page pool (request sharding, weak scaling, no collective on the data path).
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, D, P, K_TOP = 32, 128, 16, 64
+E = H * D
+BATCH = 64
+CTX_LO, CTX_HI = 16384, 32768
+SEED = 7
+CPU_SAMPLE_REQUESTS = 4
+
+
+def workload_contexts(batch=BATCH, seed=SEED):
+    return np.random.default_rng(seed).integers(CTX_LO, CTX_HI + 1, size=batch)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (getattr(self, "out", "") or "").splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ---------------------------------------------------------------- reference arm
+
+def cpu_sample(steps, warmup):
+    """Reference sparse_cpu on CPU_SAMPLE_REQUESTS requests of the config-3 shape."""
+    from oracle import oracle as o
+    if not o.ref_available():
+        o.build()
+    kind = "reference" if o.ref_available() else "port"
+    threads = max(1, min(CPU_SAMPLE_REQUESTS, os.cpu_count() or 1))
+    if kind == "reference":
+        rb = o.RefBatch(H, D, P, K_TOP, CPU_SAMPLE_REQUESTS, CTX_LO, CTX_HI, SEED)
+        for _ in range(warmup):
+            rb.time_sparse_cpu(1, threads)
+        ms = [rb.time_sparse_cpu(1, threads) for _ in range(steps)]
+        rb.close()
+    else:
+        b = o.synthetic_batch(H, D, P, K_TOP, CPU_SAMPLE_REQUESTS, CTX_LO, CTX_HI, SEED)
+        for _ in range(warmup):
+            o.sparse_decode(b, n_threads=threads)
+        ms = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            o.sparse_decode(b, n_threads=threads)
+            ms.append((time.perf_counter() - t0) * 1e3)
+    ms_step = float(np.mean(ms))
+    return {
+        "value": CPU_SAMPLE_REQUESTS / (ms_step / 1e3), "unit": "tokens/s", "cores": threads,
+        "kind": kind, "ms_per_step": ms_step,
+        "sample": (f"{CPU_SAMPLE_REQUESTS} requests of the config-3 shape (ctx U{{{CTX_LO}.."
+                   f"{CTX_HI}}}, H{H} D{D} P{P} k{K_TOP}, reference BuildSyntheticBatch seed {SEED}),"
+                   f" sparse_cpu RunNaiveSparseStep, requests over {threads} host threads"),
+    }
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    cb = cpu_sample(args.steps, args.warmup)
+    line = {
+        "impl": "reference", "metric": "sparse decode tokens/s", "value": cb["value"],
+        "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": cb["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config3 sample (host)", "requests": CPU_SAMPLE_REQUESTS,
+                   "context": [CTX_LO, CTX_HI], "num_heads": H, "head_dim": D, "page_size": P,
+                   "top_k_pages": K_TOP},
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- our arm
+
+def build_workload(dsd, ctx_lens, device):
+    """Allocates the pool, generates K/V on device, sets the request page tables."""
+    pages_per = (ctx_lens + P - 1) // P
+    cap = int(pages_per.sum())
+    ctx = dsd.SparseDecodeContext(H, D, P, K_TOP, cap, BATCH, cap, BATCH * K_TOP,
+                                  max_requests=BATCH, max_pages_per_request=int(pages_per.max()),
+                                  device=device)
+    page_ids, counts, reqs, first = [], [], [], []
+    nxt = cap - 1
+    table = []
+    for r, (n_tok, n_pages) in enumerate(zip(ctx_lens, pages_per)):
+        ids = np.arange(nxt, nxt - n_pages, -1, dtype=np.int32)  # LIFO PagePool order
+        nxt -= n_pages
+        table.append(ids)
+        page_ids.append(ids)
+        counts.append(np.minimum(P, n_tok - np.arange(n_pages) * P).astype(np.int32))
+        reqs.append(np.full(n_pages, r, np.int32))
+        first.append((np.arange(n_pages) * P).astype(np.int32))
+    ctx.generate_normal(np.concatenate(page_ids), np.concatenate(counts), np.concatenate(reqs),
+                        np.concatenate(first), SEED)
+    for r, ids in enumerate(table):
+        ctx.set_request_pages(r, ids)
+    return ctx, cap, np.concatenate(page_ids), np.concatenate(counts)
+
+
+def queries_host(dsd):
+    q = np.empty((BATCH, E), np.float32)
+    for r in range(BATCH):
+        q[r] = dsd.generate_normal_host(SEED, 0, dsd.normal_index(r, 0, E), E)
+    return q
+
+
+def run_ours(args):
+    import torch
+    world, rank, local = dist_env()
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl")
+    dsd = importlib.import_module("15-618_dynamic_sparse_decode_b200")
+    if not dsd.available():
+        raise RuntimeError("no sm_100 GPU visible")
+    torch.cuda.set_device(local)
+    ctx_lens = workload_contexts()
+    ctx, cap, all_ids, all_counts = build_workload(dsd, ctx_lens, local)
+    qh = queries_host(dsd)
+    reqs = np.arange(BATCH, dtype=np.int32)
+
+    # algorithmic bytes of one step (exact selected token count from a debug step)
+    dbg = ctx.decode_step(reqs, qh, output_mode=dsd.OUTPUT_DEBUG)
+    page_tokens = np.zeros(cap, np.int64)
+    page_tokens[all_ids] = all_counts
+    C = cap
+    S = int(dbg["selected"].size)
+    T_sel = int(page_tokens[dbg["selected"]].sum())
+    score_bytes = 4 * E * C + 4 * E * BATCH + 4 * C            # summaries + queries + ids/scores
+    attn_bytes = 8 * E * T_sel + 4 * E * BATCH + 4 * S          # selected K/V + queries + ids
+    step_bytes = 4 * E * C + 8 * E * T_sel + 8 * E * BATCH + 4 * (C + 2 * S + 3 * BATCH + 3)
+
+    dq = torch.from_numpy(qh).cuda(local)
+    do = torch.zeros_like(dq)
+    torch.cuda.synchronize()
+    ctx.bind_requests(reqs)
+    stream = torch.cuda.ExternalStream(ctx.stream(), device=local)
+
+    for _ in range(args.warmup):
+        ctx.decode_bound_timed(dq.data_ptr(), do.data_ptr())
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    per_kernel = {"score_ms": [], "topk_ms": [], "attention_ms": [], "total_ms": []}
+    with ClockSampler(local) as clk:
+        time.sleep(0.3)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            t = ctx.decode_bound_timed(dq.data_ptr(), do.data_ptr())
+            for k_, v in t.items():
+                per_kernel[k_].append(v)
+        stop.record(stream)
+        torch.cuda.synchronize()
+    ms_total = start.elapsed_time(stop)
+    if world > 1:
+        tt = torch.tensor([ms_total], device=f"cuda:{local}")
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        ms_total = float(tt.item())
+    ms_step = ms_total / args.steps
+
+    # graph-replayed step (device resident) for reference
+    for _ in range(3):
+        ctx.decode_bound(dq.data_ptr(), do.data_ptr())
+    torch.cuda.synchronize()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(stream)
+    for _ in range(args.steps):
+        ctx.decode_bound(dq.data_ptr(), do.data_ptr())
+    g1.record(stream)
+    torch.cuda.synchronize()
+    graph_ms = g0.elapsed_time(g1) / args.steps
+
+    # e2e through the public C ABI: host queries in, host outputs out
+    for _ in range(max(1, args.warmup)):
+        ctx.decode_step(reqs, qh, output_mode=dsd.OUTPUT_OUTPUTS)
+    ctx.reset_transfer_stats()
+    if world > 1:
+        torch.distributed.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        res = ctx.decode_step(reqs, qh, output_mode=dsd.OUTPUT_OUTPUTS)
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+    st = ctx.transfer_stats()
+    if world > 1:
+        tt = torch.tensor([e2e_ms], device=f"cuda:{local}")
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+    assert np.array_equal(res["outputs"], do.cpu().numpy()), "e2e and device-resident outputs differ"
+
+    peak, peak_kind = peaks()
+    score_ms = float(np.mean(per_kernel["score_ms"]))
+    attn_ms = float(np.mean(per_kernel["attention_ms"]))
+    dom = ("attention", attn_ms, attn_bytes) if attn_ms >= score_ms else ("score", score_ms, score_bytes)
+    achieved = dom[2] / (dom[1] * 1e-3) / 1e9
+    line = {
+        "metric": "sparse decode tokens/s", "value": world * BATCH / (ms_step * 1e-3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (device-generated N(0,1) Irwin-Hall, seed 7)",
+        "config": {"workload": "config3: batch 64/GPU, ctx U{16384..32768}, H32 D128 P16 k64",
+                   "requests_per_gpu": BATCH, "candidate_pages_per_gpu": C,
+                   "selected_pages_per_gpu": S, "selected_tokens_per_gpu": T_sel,
+                   "step_bytes_per_gpu": step_bytes,
+                   "step_hbm_gbps": step_bytes / (ms_step * 1e-3) / 1e9,
+                   "step_roofline_frac": step_bytes / (ms_step * 1e-3) / 1e9 / peak,
+                   "graph_ms_per_step": graph_ms,
+                   "kernel_ms": {"score(+plan)": score_ms,
+                                 "select": float(np.mean(per_kernel["topk_ms"])),
+                                 "attention(+combine)": attn_ms},
+                   "l2": "inputs larger than L2 (3.7 GB read per step)",
+                   "parallelism": f"request-sharded x{world}"},
+        "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None},
+        "e2e": {"value": world * BATCH / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": st["h2d_bytes"] / args.steps,
+                "d2h_bytes_per_step": st["d2h_bytes"] / args.steps},
+        "gpu_launches": dsd.load_library().dsd_kernels_per_step() * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_sample(1, 0)
+        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()
