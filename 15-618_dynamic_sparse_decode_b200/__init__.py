@@ -91,6 +91,9 @@ SIGNATURES = [
     ("dsd_decode_bound", ctypes.c_int, [_VP, _VP, _VP]),
     ("dsd_decode_bound_timed", ctypes.c_int, [_VP, _VP, _VP, ctypes.POINTER(StepTiming)]),
     ("dsd_kernels_per_step", ctypes.c_int, []),
+    ("dsd_decode_batch_noalloc", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ModelConfig),
+                                                ctypes.c_int, _I32P, _VP, _VP, _VP, _VP, _VP,
+                                                _VP, _VP, _VP]),
 ]
 
 _lib = None

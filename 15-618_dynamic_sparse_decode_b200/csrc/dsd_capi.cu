@@ -11,6 +11,7 @@
 #include <cstdint>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 #include <unordered_map>
@@ -1022,3 +1023,174 @@ int dsd_decode_bound_timed(dsd_ctx* c, const float* d_queries, float* d_outputs,
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ allocation-free step
+//
+// For callers that may not allocate device memory (see dsd_decode_batch_noalloc
+// in include/dsd_b200.h).  The step's working memory is one file-scope device
+// array; its host-side name is only a stand-in, so host code passes the
+// address that cudaGetSymbolAddress returns for the current device.
+namespace {
+
+constexpr int kNaMaxBatch = 256;
+constexpr int kNaMaxCandidates = 131072;
+constexpr int kNaMaxSelected = 8192;
+constexpr int kNaMaxEpt = 4096;
+constexpr int kNaMaxUnitsTarget = 512;   // split-K units requested from the plan
+// units <= max(target, selected / kMaxPagesPerUnit) + batch
+constexpr int kNaMaxUnits =
+    (kNaMaxUnitsTarget > kNaMaxSelected / dsdk::kMaxPagesPerUnit
+         ? kNaMaxUnitsTarget : kNaMaxSelected / dsdk::kMaxPagesPerUnit) + kNaMaxBatch;
+
+// layout of the array, in 4-byte words (each region 64-word aligned)
+constexpr size_t NaAlign(size_t w) { return (w + 63) / 64 * 64; }
+constexpr size_t kNaHdr = 0;                                            // hdr[4] + status
+constexpr size_t kNaReq = 64;                                           // cand offsets [B+1]
+constexpr size_t kNaPlan = kNaReq + NaAlign(kNaMaxBatch + 1);           // 2B + 4(B+1) + 4
+constexpr size_t kNaScores = kNaPlan + NaAlign(6 * (kNaMaxBatch + 1) + 4);
+constexpr size_t kNaSelected = kNaScores + NaAlign(kNaMaxCandidates);
+constexpr size_t kNaPartAcc = kNaSelected + NaAlign(kNaMaxSelected);
+constexpr size_t kNaPartMl = kNaPartAcc + NaAlign(size_t(kNaMaxUnits) * kNaMaxEpt);
+constexpr size_t kNaWords = kNaPartMl + NaAlign(size_t(kNaMaxUnits) * (kNaMaxEpt / 4) * 2);
+
+static __device__ __align__(256) int g_noalloc_scratch[kNaWords];
+
+struct NaDevice {
+  bool ready = false;
+  int* scratch = nullptr;   // device address of g_noalloc_scratch on this device
+  int num_sms = 0;
+};
+std::mutex g_na_mutex;
+NaDevice g_na[64];
+
+__global__ void noalloc_init_kernel(int* hdr, int batch) {
+  hdr[0] = batch;
+  hdr[1] = 0;   // CSR mode
+  hdr[4] = 0;   // status word: the previous call's bits must not leak
+}
+
+template <int S>
+void NaSetAttn(size_t smem) {
+  Check(cudaFuncSetAttribute(dsdk::attn_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(smem)), "smem attribute");
+}
+
+NaDevice& NaSetup(int device) {
+  if (device < 0 || device >= 64) Fail(DSD_EINVAL, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_na_mutex);
+  NaDevice& d = g_na[device];
+  if (d.ready) return d;
+  void* p = nullptr;
+  Check(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(scratch)");
+  Check(cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, device), "SM count");
+  Check(cudaFuncSetAttribute(dsdk::score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(dsdk::kScoreSmem)), "smem attribute");
+  // largest attention stage for any shape within the limits
+  const size_t max_attn = size_t(dsdk::kAttnStages) * dsdk::kAttnStageFloats * 4 +
+                          dsdk::kAttnStages * 8;
+  NaSetAttn<1>(max_attn);
+  NaSetAttn<2>(max_attn);
+  NaSetAttn<4>(max_attn);
+  d.scratch = static_cast<int*>(p);
+  d.ready = true;
+  return d;
+}
+
+}  // namespace
+
+extern "C" int dsd_decode_batch_noalloc(int device, const dsd_model_config* config, int batch,
+                                        const int32_t* cand_offsets, const int32_t* d_cand_ids,
+                                        const float* d_queries, const float* d_summaries,
+                                        const float* d_keys, const float* d_values,
+                                        const int32_t* d_token_counts, float* d_outputs,
+                                        void* stream) {
+  return Guard([&]() {
+    if (!config || !cand_offsets) Fail(DSD_EINVAL, "null argument");
+    const dsd_model_config cfg = *config;
+    const int D = cfg.head_dim;
+    if (cfg.num_heads <= 0 || D < 4 || D > 128 || (D & (D - 1)) != 0 || cfg.page_size <= 0 ||
+        cfg.top_k_pages < 0 || cfg.top_k_pages > dsdk::kSelectMaxK)
+      Fail(DSD_EINVAL, "unsupported model config");
+    const int ept = cfg.num_heads * D;
+    if (ept > kNaMaxEpt) Fail(DSD_EINVAL, "num_heads*head_dim exceeds the no-alloc limit 4096");
+    if (batch < 0 || batch > kNaMaxBatch)
+      Fail(DSD_EINVAL, "batch exceeds the no-alloc limit of 256 requests");
+    if (batch == 0) return;
+    if (cand_offsets[0] != 0) Fail(DSD_EINVAL, "cand_offsets[0] must be 0");
+    long long total_sel = 0;
+    for (int r = 0; r < batch; ++r) {
+      const int n = cand_offsets[r + 1] - cand_offsets[r];
+      if (n < 0) Fail(DSD_EINVAL, "cand_offsets must be non-decreasing");
+      total_sel += std::min(cfg.top_k_pages, n);
+    }
+    if (cand_offsets[batch] > kNaMaxCandidates)
+      Fail(DSD_EINVAL, "total candidates exceed the no-alloc limit of 131072");
+    if (total_sel > kNaMaxSelected)
+      Fail(DSD_EINVAL, "total selected pages exceed the no-alloc limit of 8192");
+    const void* ptrs[] = {d_queries, d_summaries, d_keys, d_values, d_outputs};
+    for (const void* p : ptrs)
+      if (!p || (reinterpret_cast<uintptr_t>(p) & 15u) != 0)
+        Fail(DSD_EINVAL, "device float arrays must be non-null and 16-byte aligned");
+    if (!d_token_counts || (cand_offsets[batch] > 0 && !d_cand_ids))
+      Fail(DSD_EINVAL, "null device array");
+
+    Check(cudaSetDevice(device), "cudaSetDevice");
+    NaDevice& nd = NaSetup(device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int* base = nd.scratch;
+
+    dsdk::StepPlan plan{};
+    plan.hdr = base + kNaHdr;
+    plan.req = base + kNaReq;
+    plan.cand_ids = d_cand_ids;
+    plan.table = nullptr;
+    plan.table_n = nullptr;
+    plan.table_stride = 1;
+    int* q = base + kNaPlan;
+    plan.n_cand = q; q += kNaMaxBatch;
+    plan.id_base = q; q += kNaMaxBatch;
+    plan.score_off = q; q += kNaMaxBatch + 1;
+    plan.sel_off = q; q += kNaMaxBatch + 1;
+    plan.tile_off = q; q += kNaMaxBatch + 1;
+    plan.unit_off = q; q += kNaMaxBatch + 1;
+    plan.misc = q;
+    plan.status = base + kNaHdr + 4;
+    float* scores = reinterpret_cast<float*>(base + kNaScores);
+    int* selected = base + kNaSelected;
+    float* part_acc = reinterpret_cast<float*>(base + kNaPartAcc);
+    float* part_ml = reinterpret_cast<float*>(base + kNaPartMl);
+
+    noalloc_init_kernel<<<1, 1, 0, s>>>(base + kNaHdr, batch);
+    Check(cudaMemcpyAsync(base + kNaReq, cand_offsets, size_t(batch + 1) * sizeof(int),
+                          cudaMemcpyHostToDevice, s), "offsets copy");
+    const int target = std::min(kNaMaxUnitsTarget, 2 * nd.num_sms);
+    const float scale = 1.0f / std::sqrt(static_cast<float>(D));
+    dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, s>>>(plan, cfg.top_k_pages, target);
+    dsdk::score_kernel<<<2 * nd.num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, s>>>(
+        plan, d_queries, d_summaries, ept, scale, scores);
+    dsdk::select_kernel<<<std::min(batch, 2 * nd.num_sms), dsdk::kSelectThreads, 0, s>>>(
+        plan, scores, selected);
+    const int vec = ept / 4;
+    const int slots = (vec + dsdk::kAttnThreads - 1) / dsdk::kAttnThreads;
+    const int tps = std::max(1, std::min(cfg.page_size, dsdk::kAttnStageFloats / (2 * ept)));
+    const size_t smem = size_t(dsdk::kAttnStages) * 2 * tps * ept * 4 + dsdk::kAttnStages * 8;
+#define DSD_NA_ATTN(S)                                                                       \
+  dsdk::attn_kernel<S><<<nd.num_sms, dsdk::kAttnThreads, smem, s>>>(                        \
+      plan, d_queries, d_keys, d_values, d_token_counts, selected, part_acc, part_ml,        \
+      cfg.num_heads, D, cfg.page_size, tps, scale)
+    if (slots <= 1) DSD_NA_ATTN(1);
+    else if (slots <= 2) DSD_NA_ATTN(2);
+    else DSD_NA_ATTN(4);
+#undef DSD_NA_ATTN
+    const int pairs = batch * cfg.num_heads;
+    dsdk::combine_kernel<<<std::max(1, std::min((pairs + 7) / 8, 8 * nd.num_sms)), 256, 0, s>>>(
+        plan, part_acc, part_ml, cfg.num_heads, D, d_outputs);
+    Check(cudaGetLastError(), "kernel launch");
+    int status = 0;
+    Check(cudaMemcpyAsync(&status, plan.status, sizeof(int), cudaMemcpyDeviceToHost, s),
+          "status read");
+    Check(cudaStreamSynchronize(s), "stream synchronize");
+    if (status & dsdk::kStatusTimeout) Fail(DSD_ETIMEOUT, "a device-side wait exceeded its budget");
+    if (status) Fail(DSD_EINVAL, "device kernels rejected the step input");
+  });
+}

@@ -197,6 +197,33 @@ int dsd_decode_bound_timed(dsd_ctx* ctx, const float* d_queries, float* d_output
 /* Number of kernels one decode step launches (for launch accounting). */
 int dsd_kernels_per_step(void);
 
+/* Allocation-free decode step.  No counterpart in the reference: it exists
+ * for callers that must not allocate device memory at all -- code running
+ * under a host framework that owns every allocation (a custom caching
+ * allocator or a fixed memory budget), or code that runs where cudaMalloc is
+ * not allowed.  It needs no context: the caller passes every input and the
+ * output as device pointers, and the step's working memory (plan, scores,
+ * selected ids, split-K partials) lives in one static device array of about
+ * 20 MiB that every GPU which loads this library keeps until the process
+ * exits.  Limits: batch <= 256, total candidates <= 131072, total selected
+ * pages (sum of min(k, n_r)) <= 8192, num_heads*head_dim <= 4096, top_k <= 4096;
+ * larger sizes are rejected with DSD_EINVAL.
+ *   cand_offsets  HOST array [batch+1] (validated here, copied to the device)
+ *   d_cand_ids, d_queries [batch][H*D], d_summaries [cap][H*D],
+ *   d_keys/d_values [cap][page_size][H*D], d_token_counts [cap], d_outputs
+ *   [batch][H*D]: device pointers, float arrays 16-byte aligned.
+ * Page ids are not range-checked (they live on the device).  Work is queued on
+ * `stream` (a cudaStream_t, NULL = default stream) and the call waits for it.
+ * The first call on a device looks up the array's device address and sets
+ * kernel attributes; make that first call before any stream capture.  All
+ * calls share the one array: calls that overlap on the GPU (other threads,
+ * other streams) race and must be serialised by the caller. */
+int dsd_decode_batch_noalloc(int device, const dsd_model_config* config, int batch,
+                             const int32_t* cand_offsets, const int32_t* d_cand_ids,
+                             const float* d_queries, const float* d_summaries,
+                             const float* d_keys, const float* d_values,
+                             const int32_t* d_token_counts, float* d_outputs, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
