@@ -207,7 +207,7 @@ void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed) {
   if (timed) Check(cudaEventRecord(c->ev[0], c->stream), "event");
   dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, c->stream>>>(plan, c->cfg.top_k_pages,
                                                              target_units);
-  dsdk::score_kernel<<<2 * c->num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, c->stream>>>(
+  dsdk::score_kernel<<<c->num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, c->stream>>>(
       plan, d_q, c->summaries, c->ept, c->scale, c->d_scores);
   if (timed) Check(cudaEventRecord(c->ev[1], c->stream), "event");
   const int sel_grid = std::max(1, std::min(c->opt.max_batch, 2 * c->num_sms));
@@ -1166,7 +1166,7 @@ extern "C" int dsd_decode_batch_noalloc(int device, const dsd_model_config* conf
     const int target = std::min(kNaMaxUnitsTarget, 2 * nd.num_sms);
     const float scale = 1.0f / std::sqrt(static_cast<float>(D));
     dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, s>>>(plan, cfg.top_k_pages, target);
-    dsdk::score_kernel<<<2 * nd.num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, s>>>(
+    dsdk::score_kernel<<<nd.num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, s>>>(
         plan, d_queries, d_summaries, ept, scale, scores);
     dsdk::select_kernel<<<std::min(batch, 2 * nd.num_sms), dsdk::kSelectThreads, 0, s>>>(
         plan, scores, selected);

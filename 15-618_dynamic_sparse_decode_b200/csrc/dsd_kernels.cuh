@@ -9,7 +9,7 @@
 //                   CPU's exact operation order (ScorePagesCpu,
 //                   src/reference_kernels.cpp:59-80) so page selection is
 //                   bit-identical to sparse_cpu; summaries stream HBM -> smem
-//                   with cp.async.bulk into an mbarrier ring
+//                   through a 6-deep ring of coalesced 16 B cp.async copies
 //   select_kernel   per-request top-min(k,n) by (score desc, page id asc)
 //                   (SelectTopKPagesCpu, :82-107) via a 64-bit radix select
 //   attn_kernel     split-K flash decode over the selected pages, all heads
@@ -34,12 +34,10 @@ constexpr int kPlanThreads = 1024;
 constexpr int kScoreTile = 128;
 constexpr int kScoreChunk = 64;                     // floats of a summary row per stage
 constexpr int kScoreRowStride = kScoreChunk + 4;    // +16 B: conflict-free float4 rows
-constexpr int kScoreStages = 3;
-constexpr int kScoreConsumerWarps = kScoreTile / 32;
-constexpr int kScoreThreads = kScoreTile + 32;      // + one producer warp
+constexpr int kScoreStages = 6;
+constexpr int kScoreThreads = kScoreTile;
 constexpr int kScoreRows = kScoreTile + 1;          // + the query chunk
-constexpr size_t kScoreSmem =
-    size_t(kScoreStages) * kScoreRows * kScoreRowStride * sizeof(float) + 2 * kScoreStages * 8;
+constexpr size_t kScoreSmem = size_t(kScoreStages) * kScoreRows * kScoreRowStride * sizeof(float);
 
 constexpr int kAttnThreads = 256;
 constexpr int kAttnStages = 3;
@@ -240,100 +238,106 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(StepPlan plan, int t
 
 // ------------------------------------------------------------------ score
 
-// Persistent CTAs over score tiles.  Consumer thread t owns candidate t of
-// the tile and accumulates q[i]*s[i] for i = 0..E-1 in order with
-// round-to-nearest multiply and add (no FMA), exactly ScorePagesCpu's Dot.
-// A producer warp streams each tile's summary rows chunk by chunk
-// (kScoreChunk floats per row per stage) into a kScoreStages-deep ring with
-// cp.async.bulk; row kScoreTile of every stage holds the query chunk.
-__global__ void __launch_bounds__(kScoreThreads) score_kernel(StepPlan plan,
-                                                              const float* __restrict__ queries,
-                                                              const float* __restrict__ summaries,
-                                                              int ept, float scale,
-                                                              float* __restrict__ scores) {
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Persistent CTAs over score tiles.  Thread t owns candidate t of the tile
+// and accumulates q[i]*s[i] for i = 0..E-1 in order with round-to-nearest
+// multiply and add (no FMA), exactly ScorePagesCpu's Dot.  The tile's
+// summary rows stream through a kScoreStages-deep shared-memory ring,
+// kScoreChunk floats per row per stage, filled by all threads with coalesced
+// 16-byte cp.async copies (one warp moves two 256 B row chunks per
+// instruction); row kScoreTile of every stage holds the query chunk.
+// Thread t always copies rows (t>>4) + 8j, column t&15, so it keeps the
+// page ids of the tile it is loading in registers.
+__global__ void __launch_bounds__(kScoreThreads, 1) score_kernel(
+    StepPlan plan, const float* __restrict__ queries, const float* __restrict__ summaries,
+    int ept, float scale, float* __restrict__ scores) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   float* stage_base = reinterpret_cast<float*>(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(
-      smem_raw + size_t(kScoreStages) * kScoreRows * kScoreRowStride * sizeof(float));
-  uint64_t* empty = full + kScoreStages;
+  constexpr int kRowsPerThread = (kScoreRows + 7) / 8;   // 17
+  constexpr int kStageFloats = kScoreRows * kScoreRowStride;
 
   const int tid = threadIdx.x;
-  if (tid == 0) {
-    for (int s = 0; s < kScoreStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kScoreConsumerWarps);
-    }
-    fence_barrier_init();
-  }
-  __syncthreads();
-
   const int B = plan.hdr[0];
   const int mode = plan.hdr[1];
   const int* ids_src = mode == 0 ? plan.cand_ids : plan.table;
   const int total_tiles = plan.tile_off[B];
   const int nchunks = (ept + kScoreChunk - 1) / kScoreChunk;
-  int* status = plan.status;
+  const int col = tid & 15;
+  const int row0 = tid >> 4;
 
-  if (tid >= kScoreTile) {
-    // ---------------- producer warp
-    const int lane = tid - kScoreTile;
-    uint32_t g = 0;
-    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
-      const int r = upper_segment(plan.tile_off, B, tile);
-      const int c0 = (tile - plan.tile_off[r]) * kScoreTile;
-      const int nvalid = min(kScoreTile, plan.n_cand[r] - c0);
-      const int* ids = ids_src + plan.id_base[r] + c0;
-      int my_page[kScoreTile / 32];
+  // ---- loader state (runs kScoreStages-1 chunks ahead of the compute)
+  int ld_tile = blockIdx.x, ld_ch = 0, ld_slot = 0, ld_nvalid = 0;
+  const float* ld_q = queries;
+  size_t ld_off[kRowsPerThread];
+  auto load_tile = [&]() {
+    if (ld_tile >= total_tiles) return;
+    const int r = upper_segment(plan.tile_off, B, ld_tile);
+    const int c0 = (ld_tile - plan.tile_off[r]) * kScoreTile;
+    ld_nvalid = min(kScoreTile, plan.n_cand[r] - c0);
+    ld_q = queries + size_t(r) * ept;
+    const int* ids = ids_src + plan.id_base[r] + c0;
 #pragma unroll
-      for (int m = 0; m < kScoreTile / 32; ++m) {
-        const int row = lane + 32 * m;
-        my_page[m] = row < nvalid ? __ldg(ids + row) : 0;
-      }
-      const float* qrow = queries + size_t(r) * ept;
-      for (int ch = 0; ch < nchunks; ++ch, ++g) {
-        const int s = g % kScoreStages;
-        if (g >= kScoreStages) {
-          if (!mbar_wait(&empty[s], ((g / kScoreStages) - 1) & 1, status)) return;
-        }
-        const int len = min(kScoreChunk, ept - ch * kScoreChunk);
-        const uint32_t row_bytes = uint32_t(len) * 4u;
-        float* stage = stage_base + size_t(s) * kScoreRows * kScoreRowStride;
-        if (lane == 0) mbar_arrive_expect_tx(&full[s], row_bytes * uint32_t(nvalid + 1));
-        __syncwarp();
+    for (int j = 0; j < kRowsPerThread; ++j) {
+      const int row = row0 + 8 * j;
+      ld_off[j] = row < ld_nvalid ? size_t(__ldg(ids + row)) * ept : 0;
+    }
+  };
+  auto issue = [&]() {
+    if (ld_tile < total_tiles) {
+      const int len = min(kScoreChunk, ept - ld_ch * kScoreChunk);
+      float* st = stage_base + size_t(ld_slot) * kStageFloats;
+      if (col * 4 < len) {
+        const size_t coff = size_t(ld_ch) * kScoreChunk + col * 4;
 #pragma unroll
-        for (int m = 0; m < kScoreTile / 32; ++m) {
-          const int row = lane + 32 * m;
-          if (row < nvalid) {
-            bulk_g2s(stage + row * kScoreRowStride,
-                     summaries + size_t(my_page[m]) * ept + size_t(ch) * kScoreChunk, row_bytes,
-                     &full[s]);
+        for (int j = 0; j < kRowsPerThread; ++j) {
+          const int row = row0 + 8 * j;
+          if (row < ld_nvalid) {
+            cp_async16(st + row * kScoreRowStride + col * 4, summaries + ld_off[j] + coff);
+          } else if (row == kScoreTile) {
+            cp_async16(st + row * kScoreRowStride + col * 4, ld_q + coff);
           }
         }
-        if (lane == 0) {
-          bulk_g2s(stage + kScoreTile * kScoreRowStride, qrow + size_t(ch) * kScoreChunk,
-                   row_bytes, &full[s]);
-        }
+      }
+      if (++ld_ch == nchunks) {
+        ld_ch = 0;
+        ld_tile += gridDim.x;
+        load_tile();
       }
     }
-    return;
-  }
+    cp_async_commit();
+    ld_slot = ld_slot + 1 == kScoreStages ? 0 : ld_slot + 1;
+  };
 
-  // ---------------- consumers
-  const int lane = tid & 31;
-  uint32_t g = 0;
+  load_tile();
+#pragma unroll 1
+  for (int i = 0; i < kScoreStages - 1; ++i) issue();
+
+  int slot = 0;
   for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
     const int r = upper_segment(plan.tile_off, B, tile);
     const int c0 = (tile - plan.tile_off[r]) * kScoreTile;
     const int nvalid = min(kScoreTile, plan.n_cand[r] - c0);
     float acc = 0.0f;
-    for (int ch = 0; ch < nchunks; ++ch, ++g) {
-      const int s = g % kScoreStages;
-      if (!mbar_wait(&full[s], (g / kScoreStages) & 1, status)) return;
+    for (int ch = 0; ch < nchunks; ++ch) {
+      cp_async_wait<kScoreStages - 2>();
+      __syncthreads();   // chunk `slot` landed for all threads; slot-1 is free again
+      issue();
       const int len = min(kScoreChunk, ept - ch * kScoreChunk);
-      const float* stage = stage_base + size_t(s) * kScoreRows * kScoreRowStride;
+      const float* st = stage_base + size_t(slot) * kStageFloats;
       if (tid < nvalid) {
-        const float4* srow = reinterpret_cast<const float4*>(stage + tid * kScoreRowStride);
-        const float4* qv = reinterpret_cast<const float4*>(stage + kScoreTile * kScoreRowStride);
+        const float4* srow = reinterpret_cast<const float4*>(st + tid * kScoreRowStride);
+        const float4* qv = reinterpret_cast<const float4*>(st + kScoreTile * kScoreRowStride);
         if (len == kScoreChunk) {
 #pragma unroll
           for (int i = 0; i < kScoreChunk / 4; ++i) {
@@ -355,11 +359,11 @@ __global__ void __launch_bounds__(kScoreThreads) score_kernel(StepPlan plan,
           }
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
+      slot = slot + 1 == kScoreStages ? 0 : slot + 1;
     }
     if (tid < nvalid) scores[plan.score_off[r] + c0 + tid] = __fmul_rn(acc, scale);
   }
+  cp_async_wait<0>();
 }
 
 // ------------------------------------------------------------------ select

@@ -40,7 +40,8 @@ SEED = 7
 CPU_SAMPLE_REQUESTS = 4
 
 
-def workload_contexts(batch=BATCH, seed=SEED):
+def workload_contexts(batch=None, seed=SEED):
+    batch = BATCH if batch is None else batch
     return np.random.default_rng(seed).integers(CTX_LO, CTX_HI + 1, size=batch)
 
 
@@ -325,13 +326,18 @@ def run_ours(args):
 
 
 def main():
+    global BATCH
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=BATCH,
+                    help="requests per GPU (default: the config-3 batch of 64; smaller only "
+                         "for profiling captures)")
     args = ap.parse_args()
+    BATCH = args.batch
     if args.impl == "reference":
         run_reference(args)
     else:
