@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <initializer_list>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -82,6 +83,67 @@ T* PinnedAlloc(size_t count, const char* what) {
 
 size_t AlignUp(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+
+// Attention launch shape: NV float4 per lane, LP = D/(4*NV) lanes per head,
+// SLOTS items per thread, tokens per stage and dynamic shared memory.
+struct AttnShape {
+  int nv = 1, slots = 1, tps = 1;
+  size_t smem = 0;
+};
+
+AttnShape MakeAttnShape(int num_heads, int head_dim, int page_size) {
+  AttnShape a;
+  const int ept = num_heads * head_dim;
+  const int G = head_dim / 4;
+  a.nv = G >= 4 ? 4 : G;
+  const int items = num_heads * (G / a.nv);
+  const int slots = (items + dsdk::kAttnThreads - 1) / dsdk::kAttnThreads;
+  if (slots > 8) Fail(DSD_EINVAL, "num_heads*head_dim is too large for the attention kernel");
+  a.slots = slots <= 1 ? 1 : slots <= 2 ? 2 : slots <= 4 ? 4 : 8;
+  a.tps = std::max(1, std::min({page_size, dsdk::kAttnStageFloats / (2 * ept),
+                                dsdk::kAttnMaxTokensPerStage}));
+  a.smem = size_t(dsdk::kAttnStages) * 2 * a.tps * ept * sizeof(float) + dsdk::kAttnStages * 8;
+  return a;
+}
+
+template <int NV, int S>
+void SetAttnAttr(size_t smem) {
+  Check(cudaFuncSetAttribute(dsdk::attn_kernel<NV, S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(smem)), "smem attribute");
+}
+
+// Raises the dynamic shared-memory limit of every attention instantiation.
+// NV = 4 serves head_dim >= 16 (at most 512 items for H*D <= 8192), NV = 2
+// head_dim 8 (<= 1024 items), NV = 1 head_dim 4 (<= 2048 items).
+void SetAllAttnAttributes(size_t smem) {
+  SetAttnAttr<1, 1>(smem); SetAttnAttr<1, 2>(smem); SetAttnAttr<1, 4>(smem); SetAttnAttr<1, 8>(smem);
+  SetAttnAttr<2, 1>(smem); SetAttnAttr<2, 2>(smem); SetAttnAttr<2, 4>(smem);
+  SetAttnAttr<4, 1>(smem); SetAttnAttr<4, 2>(smem);
+}
+
+template <int NV, int S>
+void LaunchAttnT(const AttnShape& a, int grid, cudaStream_t st, const dsdk::StepPlan& plan,
+                 const float* q, const float* k, const float* v, const int* tc, const int* sel,
+                 float* pacc, float* pml, int H, int D, int P, float scale) {
+  dsdk::attn_kernel<NV, S><<<grid, dsdk::kAttnThreads, a.smem, st>>>(plan, q, k, v, tc, sel, pacc,
+                                                                     pml, H, D, P, a.tps, scale);
+}
+
+void LaunchAttn(const AttnShape& a, int grid, cudaStream_t st, const dsdk::StepPlan& plan,
+                const float* q, const float* k, const float* v, const int* tc, const int* sel,
+                float* pacc, float* pml, int H, int D, int P, float scale) {
+#define DSD_ATTN_CASE(NV, S)                                                        \
+  if (a.nv == NV && a.slots == S) {                                                 \
+    LaunchAttnT<NV, S>(a, grid, st, plan, q, k, v, tc, sel, pacc, pml, H, D, P, scale); \
+    return;                                                                         \
+  }
+  DSD_ATTN_CASE(1, 1) DSD_ATTN_CASE(1, 2) DSD_ATTN_CASE(1, 4) DSD_ATTN_CASE(1, 8)
+  DSD_ATTN_CASE(2, 1) DSD_ATTN_CASE(2, 2) DSD_ATTN_CASE(2, 4)
+  DSD_ATTN_CASE(4, 1) DSD_ATTN_CASE(4, 2)
+#undef DSD_ATTN_CASE
+  Fail(DSD_EINVAL, "unsupported attention shape");
+}
+
 }  // namespace
 
 struct dsd_ctx {
@@ -90,9 +152,7 @@ struct dsd_ctx {
   dsd_ctx_options opt{};
   int ept = 0;
   int num_sms = 0;
-  int slots_tmpl = 1;  // attention register slots (E/4/256 rounded up to 1,2,4,8)
-  int tps = 1;         // tokens per attention stage
-  size_t attn_smem = 0;
+  AttnShape attn;     // attention launch shape
   float scale = 0.f;
   cudaStream_t stream = nullptr;
   cudaEvent_t ev[6] = {};
@@ -215,17 +275,8 @@ void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed) {
                                                                          c->d_selected);
   if (timed) Check(cudaEventRecord(c->ev[2], c->stream), "event");
   const int H = c->cfg.num_heads, D = c->cfg.head_dim, P = c->cfg.page_size;
-#define DSD_ATTN(S)                                                                              \
-  dsdk::attn_kernel<S><<<c->num_sms, dsdk::kAttnThreads, c->attn_smem, c->stream>>>(            \
-      plan, d_q, c->k_pool, c->v_pool, c->token_counts, c->d_selected, c->d_part_acc,             \
-      c->d_part_ml, H, D, P, c->tps, c->scale)
-  switch (c->slots_tmpl) {
-    case 1: DSD_ATTN(1); break;
-    case 2: DSD_ATTN(2); break;
-    case 4: DSD_ATTN(4); break;
-    default: DSD_ATTN(8); break;
-  }
-#undef DSD_ATTN
+  LaunchAttn(c->attn, c->num_sms, c->stream, plan, d_q, c->k_pool, c->v_pool, c->token_counts,
+             c->d_selected, c->d_part_acc, c->d_part_ml, H, D, P, c->scale);
   const int pairs = c->opt.max_batch * H;
   const int comb_grid = std::max(1, std::min((pairs + 7) / 8, 8 * c->num_sms));
   dsdk::combine_kernel<<<comb_grid, 256, 0, c->stream>>>(plan, c->d_part_acc, c->d_part_ml, H, D,
@@ -375,10 +426,7 @@ int dsd_ctx_create(int device, const dsd_model_config* config, const dsd_ctx_opt
       Fail(DSD_EINVAL, "sparse CUDA context capacities must be non-negative");
     if (opt.max_batch > dsdk::kMaxBatch) Fail(DSD_EINVAL, "max_batch exceeds 1024");
     const int ept = cfg.num_heads * D;
-    const int vec = ept / 4;
-    int slots = (vec + dsdk::kAttnThreads - 1) / dsdk::kAttnThreads;
-    if (slots > 8) Fail(DSD_EINVAL, "num_heads*head_dim exceeds 8192");
-    slots = slots <= 1 ? 1 : slots <= 2 ? 2 : slots <= 4 ? 4 : 8;
+    if (ept > 8192) Fail(DSD_EINVAL, "num_heads*head_dim exceeds 8192");
 
     Check(cudaSetDevice(device), "cudaSetDevice");
     cudaDeviceProp prop{};
@@ -392,10 +440,7 @@ int dsd_ctx_create(int device, const dsd_model_config* config, const dsd_ctx_opt
       c->opt = opt;
       c->ept = ept;
       c->num_sms = prop.multiProcessorCount;
-      c->slots_tmpl = slots;
-      c->tps = std::max(1, std::min(cfg.page_size, dsdk::kAttnStageFloats / (2 * ept)));
-      c->attn_smem = size_t(dsdk::kAttnStages) * 2 * c->tps * ept * sizeof(float) +
-                     dsdk::kAttnStages * 8;
+      c->attn = MakeAttnShape(cfg.num_heads, D, cfg.page_size);
       c->scale = 1.0f / std::sqrt(static_cast<float>(D));
       Check(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream");
       for (auto& e : c->ev) Check(cudaEventCreate(&e), "event");
@@ -463,16 +508,7 @@ int dsd_ctx_create(int device, const dsd_model_config* config, const dsd_ctx_opt
 
       Check(cudaFuncSetAttribute(dsdk::score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)dsdk::kScoreSmem), "smem attribute");
-      auto set_attn = [&](auto kern) {
-        Check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)c->attn_smem), "smem attribute");
-      };
-      switch (c->slots_tmpl) {
-        case 1: set_attn(dsdk::attn_kernel<1>); break;
-        case 2: set_attn(dsdk::attn_kernel<2>); break;
-        case 4: set_attn(dsdk::attn_kernel<4>); break;
-        default: set_attn(dsdk::attn_kernel<8>); break;
-      }
+      SetAllAttnAttributes(c->attn.smem);
       Sync(c);
     } catch (...) {
       dsd_ctx_destroy(c);
@@ -1069,12 +1105,6 @@ __global__ void noalloc_init_kernel(int* hdr, int batch) {
   hdr[4] = 0;   // status word: the previous call's bits must not leak
 }
 
-template <int S>
-void NaSetAttn(size_t smem) {
-  Check(cudaFuncSetAttribute(dsdk::attn_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             int(smem)), "smem attribute");
-}
-
 NaDevice& NaSetup(int device) {
   if (device < 0 || device >= 64) Fail(DSD_EINVAL, "device index out of range");
   std::lock_guard<std::mutex> lock(g_na_mutex);
@@ -1088,9 +1118,7 @@ NaDevice& NaSetup(int device) {
   // largest attention stage for any shape within the limits
   const size_t max_attn = size_t(dsdk::kAttnStages) * dsdk::kAttnStageFloats * 4 +
                           dsdk::kAttnStages * 8;
-  NaSetAttn<1>(max_attn);
-  NaSetAttn<2>(max_attn);
-  NaSetAttn<4>(max_attn);
+  SetAllAttnAttributes(max_attn);
   d.scratch = static_cast<int*>(p);
   d.ready = true;
   return d;
@@ -1170,18 +1198,9 @@ extern "C" int dsd_decode_batch_noalloc(int device, const dsd_model_config* conf
         plan, d_queries, d_summaries, ept, scale, scores);
     dsdk::select_kernel<<<std::min(batch, 2 * nd.num_sms), dsdk::kSelectThreads, 0, s>>>(
         plan, scores, selected);
-    const int vec = ept / 4;
-    const int slots = (vec + dsdk::kAttnThreads - 1) / dsdk::kAttnThreads;
-    const int tps = std::max(1, std::min(cfg.page_size, dsdk::kAttnStageFloats / (2 * ept)));
-    const size_t smem = size_t(dsdk::kAttnStages) * 2 * tps * ept * 4 + dsdk::kAttnStages * 8;
-#define DSD_NA_ATTN(S)                                                                       \
-  dsdk::attn_kernel<S><<<nd.num_sms, dsdk::kAttnThreads, smem, s>>>(                        \
-      plan, d_queries, d_keys, d_values, d_token_counts, selected, part_acc, part_ml,        \
-      cfg.num_heads, D, cfg.page_size, tps, scale)
-    if (slots <= 1) DSD_NA_ATTN(1);
-    else if (slots <= 2) DSD_NA_ATTN(2);
-    else DSD_NA_ATTN(4);
-#undef DSD_NA_ATTN
+    const AttnShape ash = MakeAttnShape(cfg.num_heads, D, cfg.page_size);
+    LaunchAttn(ash, nd.num_sms, s, plan, d_queries, d_keys, d_values, d_token_counts, selected,
+               part_acc, part_ml, cfg.num_heads, D, cfg.page_size, scale);
     const int pairs = batch * cfg.num_heads;
     dsdk::combine_kernel<<<std::max(1, std::min((pairs + 7) / 8, 8 * nd.num_sms)), 256, 0, s>>>(
         plan, part_acc, part_ml, cfg.num_heads, D, d_outputs);

@@ -43,6 +43,7 @@ constexpr int kAttnThreads = 256;
 constexpr int kAttnStages = 3;
 constexpr int kAttnStageFloats = 16384;             // K+V floats per stage (64 KiB)
 constexpr int kMaxPagesPerUnit = 16;
+constexpr int kAttnMaxTokensPerStage = 8;           // logits held in registers per stage
 
 constexpr int kSelectThreads = 512;
 constexpr int kSelectMaxK = 4096;                   // selected pages per request
@@ -555,22 +556,29 @@ __device__ __forceinline__ bool attn_walk_next(AttnWalk& w, const StepPlan& plan
   }
 }
 
-// Split-K flash decode.  CTA = 256 threads; thread t owns float4 columns
-// j = t + 256*m (m < SLOTS) of the H*D token row, i.e. a 4-wide slice of
-// head (4j)/D.  The D/4 threads of a head reduce q.k with xor shuffles, so
-// every thread of the group holds the logit and runs the online softmax for
-// its slice.  Stages hold `tps` K rows then `tps` V rows of one page,
-// fetched by thread 0 with two cp.async.bulk copies (they are contiguous in
-// the page-major pool).  Each unit writes (m, l) per head and acc[H*D].
-template <int SLOTS>
+// Split-K flash decode.  CTA = 256 threads.  A head's D/4 float4 columns are
+// split over LP = D/(4*NV) consecutive lanes ("items"), NV float4 each at
+// stride LP (so the 8 lanes of a quarter warp read 8 consecutive float4 of
+// shared memory: no bank conflicts at D = 128).  Item i = t + 256*m
+// (m < SLOTS) is lane i % LP of head i / LP.  q.k is reduced over the LP
+// lanes with xor shuffles, so every lane of a head holds the logit.
+// Stages hold `tps` K rows then `tps` V rows of one page, fetched by thread 0
+// with two cp.async.bulk copies (they are contiguous in the page-major pool)
+// into a kAttnStages-deep mbarrier ring.  The online softmax is blocked per
+// stage: all logits of the stage first, one rescale of the accumulator, then
+// the weighted V rows.  Each unit writes (m, l) per head and acc[H*D].
+template <int NV, int SLOTS>
 __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(
     StepPlan plan, const float* __restrict__ queries, const float* __restrict__ key_pool,
     const float* __restrict__ value_pool, const int* __restrict__ token_counts,
     const int* __restrict__ selected, float* __restrict__ part_acc, float* __restrict__ part_ml,
     int num_heads, int head_dim, int page_size, int tps, float scale) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
+  constexpr int kMaxTps = kAttnMaxTokensPerStage;
   const int ept = num_heads * head_dim;
   const int vec = ept >> 2;                       // float4 per token row
+  const int G = head_dim >> 2;                    // float4 per head
+  const int LP = G / NV;                          // lanes per head
   const size_t stage_floats = size_t(2) * tps * ept;
   float* stages = reinterpret_cast<float*>(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + kAttnStages * stage_floats * 4);
@@ -606,20 +614,33 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(
     }
   }
 
-  const int gsize = head_dim >> 2;  // threads per head (power of two <= 32)
+  // float4 column of (slot m, vector j) and whether the item is a real head lane
+  int colv[SLOTS][NV];
+  bool ok[SLOTS];
+#pragma unroll
+  for (int m = 0; m < SLOTS; ++m) {
+    const int item = tid + kAttnThreads * m;
+    const int head = item / LP, li = item - (item / LP) * LP;
+    ok[m] = head < num_heads;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) colv[m][j] = ok[m] ? head * G + li + LP * j : 0;
+  }
+
   uint32_t g = 0;
   bool alive = true;
   for (int u = blockIdx.x; u < total_units && alive; u += gridDim.x) {
     int r, p_begin, p_end;
     attn_unit_range(plan, B, ppu, u, &r, &p_begin, &p_end);
-    float4 q[SLOTS], acc[SLOTS];
+    float4 q[SLOTS][NV], acc[SLOTS][NV];
     float mrun[SLOTS], lrun[SLOTS];
+    const float4* qrow = reinterpret_cast<const float4*>(queries + size_t(r) * ept);
 #pragma unroll
     for (int m = 0; m < SLOTS; ++m) {
-      const int j = tid + kAttnThreads * m;
-      q[m] = j < vec ? __ldg(reinterpret_cast<const float4*>(queries + size_t(r) * ept) + j)
-                     : make_float4(0.f, 0.f, 0.f, 0.f);
-      acc[m] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        q[m][j] = ok[m] ? __ldg(qrow + colv[m][j]) : make_float4(0.f, 0.f, 0.f, 0.f);
+        acc[m][j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
       mrun[m] = -INFINITY;
       lrun[m] = 0.f;
     }
@@ -632,26 +653,45 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(
         const int nt = min(tps, n - t0);
         const float4* kst = reinterpret_cast<const float4*>(stages + size_t(s) * stage_floats);
         const float4* vst = kst + size_t(tps) * vec;
-        for (int t = 0; t < nt; ++t) {
 #pragma unroll
-          for (int m = 0; m < SLOTS; ++m) {
-            const int j = tid + kAttnThreads * m;
-            const bool ok = j < vec;
-            const float4 kk = ok ? kst[size_t(t) * vec + j] : make_float4(0.f, 0.f, 0.f, 0.f);
-            float d = q[m].x * kk.x + q[m].y * kk.y + q[m].z * kk.z + q[m].w * kk.w;
-            for (int o = gsize >> 1; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-            const float logit = d * scale;
-            const float mnew = fmaxf(mrun[m], logit);
-            const float alpha = expf(mrun[m] - mnew);
-            const float beta = expf(logit - mnew);
-            const float4 vv = ok ? vst[size_t(t) * vec + j] : make_float4(0.f, 0.f, 0.f, 0.f);
-            acc[m].x = acc[m].x * alpha + beta * vv.x;
-            acc[m].y = acc[m].y * alpha + beta * vv.y;
-            acc[m].z = acc[m].z * alpha + beta * vv.z;
-            acc[m].w = acc[m].w * alpha + beta * vv.w;
-            lrun[m] = lrun[m] * alpha + beta;
-            mrun[m] = mnew;
+        for (int m = 0; m < SLOTS; ++m) {
+          float logit[kMaxTps];
+          float cmax = mrun[m];
+#pragma unroll
+          for (int t = 0; t < kMaxTps; ++t) {
+            if (t < nt) {
+              float d = 0.f;
+#pragma unroll
+              for (int j = 0; j < NV; ++j) {
+                const float4 kk = kst[size_t(t) * vec + colv[m][j]];
+                d += q[m][j].x * kk.x + q[m][j].y * kk.y + q[m][j].z * kk.z + q[m][j].w * kk.w;
+              }
+              for (int o = LP >> 1; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+              logit[t] = d * scale;
+              cmax = fmaxf(cmax, logit[t]);
+            }
           }
+          const float alpha = expf(mrun[m] - cmax);
+          float l = lrun[m] * alpha;
+#pragma unroll
+          for (int j = 0; j < NV; ++j) {
+            acc[m][j].x *= alpha; acc[m][j].y *= alpha; acc[m][j].z *= alpha; acc[m][j].w *= alpha;
+          }
+#pragma unroll
+          for (int t = 0; t < kMaxTps; ++t) {
+            if (t < nt) {
+              const float beta = expf(logit[t] - cmax);
+              l += beta;
+#pragma unroll
+              for (int j = 0; j < NV; ++j) {
+                const float4 vv = vst[size_t(t) * vec + colv[m][j]];
+                acc[m][j].x += beta * vv.x; acc[m][j].y += beta * vv.y;
+                acc[m][j].z += beta * vv.z; acc[m][j].w += beta * vv.w;
+              }
+            }
+          }
+          lrun[m] = l;
+          mrun[m] = cmax;
         }
         __syncthreads();  // every thread is done with stage s
         if (tid == 0) {
@@ -663,14 +703,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(
     // partial of unit u
 #pragma unroll
     for (int m = 0; m < SLOTS; ++m) {
-      const int j = tid + kAttnThreads * m;
-      if (j < vec) {
-        reinterpret_cast<float4*>(part_acc + size_t(u) * ept)[j] = acc[m];
-        if ((j & (gsize - 1)) == 0) {
-          const int head = (j << 2) / head_dim;
-          part_ml[(size_t(u) * num_heads + head) * 2 + 0] = mrun[m];
-          part_ml[(size_t(u) * num_heads + head) * 2 + 1] = lrun[m];
-        }
+      if (!ok[m]) continue;
+      float4* pa = reinterpret_cast<float4*>(part_acc + size_t(u) * ept);
+#pragma unroll
+      for (int j = 0; j < NV; ++j) pa[colv[m][j]] = acc[m][j];
+      const int item = tid + kAttnThreads * m;
+      if (item % LP == 0) {
+        const int head = item / LP;
+        part_ml[(size_t(u) * num_heads + head) * 2 + 0] = mrun[m];
+        part_ml[(size_t(u) * num_heads + head) * 2 + 1] = lrun[m];
       }
     }
   }
