@@ -90,6 +90,7 @@ SIGNATURES = [
     ("dsd_bind_requests", ctypes.c_int, [_VP, _I32P, ctypes.c_int]),
     ("dsd_decode_bound", ctypes.c_int, [_VP, _VP, _VP]),
     ("dsd_decode_bound_timed", ctypes.c_int, [_VP, _VP, _VP, ctypes.POINTER(StepTiming)]),
+    ("dsd_read_step_timing", ctypes.c_int, [_VP, ctypes.POINTER(StepTiming)]),
     ("dsd_kernels_per_step", ctypes.c_int, []),
     ("dsd_decode_batch_noalloc", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ModelConfig),
                                                 ctypes.c_int, _I32P, _VP, _VP, _VP, _VP, _VP,
@@ -325,13 +326,21 @@ class SparseDecodeContext:
     def request_num_pages(self, request_id) -> int:
         return self.lib.dsd_request_num_pages(self.h, request_id)
 
-    def decode_step(self, request_ids, queries, output_mode=OUTPUT_DEBUG, timing=False):
+    def decode_step(self, request_ids, queries, output_mode=OUTPUT_DEBUG, timing=False,
+                    out=None):
         req = _i32(request_ids)
         q = _f32(queries)
         B = len(req)
-        n = np.array([self.request_num_pages(int(r)) for r in req])
-        total_sel = int(np.minimum(n, self.cfg.top_k_pages).sum())
-        out, scores, sel = self._results(B, int(n.sum()), total_sel, output_mode)
+        if output_mode == OUTPUT_DEBUG:
+            n = np.array([self.request_num_pages(int(r)) for r in req])
+            total_sel = int(np.minimum(n, self.cfg.top_k_pages).sum())
+            out, scores, sel = self._results(B, int(n.sum()), total_sel, output_mode)
+        else:
+            n = np.zeros(1, np.int64)
+            total_sel = 0
+            scores = sel = None
+            if out is None:
+                out = np.zeros((B, self.ept), np.float32)
         t = StepTiming()
         _check(self.lib.dsd_decode_step(self.h, _ip(req), B, _fp(q), output_mode, int(timing),
                                         _fp(out), _fp(scores), _ip(sel), ctypes.byref(t)))
@@ -347,8 +356,14 @@ class SparseDecodeContext:
     def decode_bound(self, d_queries: int, d_outputs: int):
         _check(self.lib.dsd_decode_bound(self.h, _VP(d_queries), _VP(d_outputs)))
 
-    def decode_bound_timed(self, d_queries: int, d_outputs: int) -> dict:
+    def decode_bound_timed(self, d_queries: int, d_outputs: int, wait: bool = True):
+        """Timed graph replay; wait=False queues it and returns None (see read_step_timing)."""
         t = StepTiming()
         _check(self.lib.dsd_decode_bound_timed(self.h, _VP(d_queries), _VP(d_outputs),
-                                               ctypes.byref(t)))
+                                               ctypes.byref(t) if wait else None))
+        return {n: getattr(t, n) for n, _ in StepTiming._fields_} if wait else None
+
+    def read_step_timing(self) -> dict:
+        t = StepTiming()
+        _check(self.lib.dsd_read_step_timing(self.h, ctypes.byref(t)))
         return {n: getattr(t, n) for n, _ in StepTiming._fields_}

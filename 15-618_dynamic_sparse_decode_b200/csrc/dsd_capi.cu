@@ -195,10 +195,17 @@ struct dsd_ctx {
 
   // bound (device-resident) steps
   int bound_batch = -1;
-  cudaGraph_t graph = nullptr;
-  cudaGraphExec_t graph_exec = nullptr;
-  const float* graph_q = nullptr;
-  float* graph_out = nullptr;
+  // captured steps, keyed by (queries, outputs, timed); the plan inside a
+  // graph reads the batch from the device header, so one graph serves every
+  // batch size and composition
+  struct StepGraph {
+    const float* q;
+    float* out;
+    bool timed;
+    cudaGraph_t graph;
+    cudaGraphExec_t exec;
+  };
+  std::vector<StepGraph> graphs;
 
   dsd_transfer_stats stats{};
 };
@@ -261,19 +268,25 @@ void CheckStatus(dsd_ctx* c) {
 
 // ------------------------------------------------------------------ step
 
-void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed) {
+void RecordEvent(dsd_ctx* c, int i, bool capturing) {
+  // inside a capture the record must become a graph node of its own
+  Check(capturing ? cudaEventRecordWithFlags(c->ev[i], c->stream, cudaEventRecordExternal)
+                  : cudaEventRecord(c->ev[i], c->stream), "event record");
+}
+
+void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool capturing = false) {
   const dsdk::StepPlan& plan = c->plan;
   const int target_units = 8 * c->num_sms;
-  if (timed) Check(cudaEventRecord(c->ev[0], c->stream), "event");
+  if (timed) RecordEvent(c, 0, capturing);
   dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, c->stream>>>(plan, c->cfg.top_k_pages,
                                                              target_units);
   dsdk::score_kernel<<<c->num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, c->stream>>>(
       plan, d_q, c->summaries, c->ept, c->scale, c->d_scores);
-  if (timed) Check(cudaEventRecord(c->ev[1], c->stream), "event");
+  if (timed) RecordEvent(c, 1, capturing);
   const int sel_grid = std::max(1, std::min(c->opt.max_batch, 2 * c->num_sms));
   dsdk::select_kernel<<<sel_grid, dsdk::kSelectThreads, 0, c->stream>>>(plan, c->d_scores,
                                                                          c->d_selected);
-  if (timed) Check(cudaEventRecord(c->ev[2], c->stream), "event");
+  if (timed) RecordEvent(c, 2, capturing);
   const int H = c->cfg.num_heads, D = c->cfg.head_dim, P = c->cfg.page_size;
   LaunchAttn(c->attn, c->num_sms, c->stream, plan, d_q, c->k_pool, c->v_pool, c->token_counts,
              c->d_selected, c->d_part_acc, c->d_part_ml, H, D, P, c->scale);
@@ -282,7 +295,31 @@ void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed) {
   dsdk::combine_kernel<<<comb_grid, 256, 0, c->stream>>>(plan, c->d_part_acc, c->d_part_ml, H, D,
                                                          d_out);
   Check(cudaGetLastError(), "kernel launch");
-  if (timed) Check(cudaEventRecord(c->ev[3], c->stream), "event");
+  if (timed) RecordEvent(c, 3, capturing);
+}
+
+// Replays the step as a CUDA graph (captured on first use for this pointer pair).
+void LaunchStepGraph(dsd_ctx* c, const float* d_q, float* d_out, bool timed) {
+  for (auto& g : c->graphs) {
+    if (g.q == d_q && g.out == d_out && g.timed == timed) {
+      Check(cudaGraphLaunch(g.exec, c->stream), "graph launch");
+      return;
+    }
+  }
+  dsd_ctx::StepGraph g{d_q, d_out, timed, nullptr, nullptr};
+  Check(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+  try {
+    LaunchStep(c, d_q, d_out, timed, true);
+  } catch (...) {
+    cudaGraph_t dead = nullptr;
+    cudaStreamEndCapture(c->stream, &dead);
+    if (dead) cudaGraphDestroy(dead);
+    throw;
+  }
+  Check(cudaStreamEndCapture(c->stream, &g.graph), "end capture");
+  Check(cudaGraphInstantiate(&g.exec, g.graph, 0), "graph instantiate");
+  c->graphs.push_back(g);
+  Check(cudaGraphLaunch(g.exec, c->stream), "graph launch");
 }
 
 void ReadTiming(dsd_ctx* c, dsd_step_timing* t) {
@@ -303,7 +340,8 @@ int* IdsPtr(dsd_ctx* c) { return reinterpret_cast<int*>(c->h_in + c->in_ids_off)
 void RunHostStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int output_mode,
                  int timing, float* outputs, float* scores, int32_t* selected,
                  dsd_step_timing* out_timing) {
-  LaunchStep(c, reinterpret_cast<const float*>(c->d_in + c->in_q_off), c->d_outputs, timing != 0);
+  LaunchStepGraph(c, reinterpret_cast<const float*>(c->d_in + c->in_q_off), c->d_outputs,
+                  timing != 0);
   const size_t out_bytes = size_t(batch) * c->ept * sizeof(float);
   if (output_mode != DSD_OUTPUT_NONE && outputs) D2H(c, c->h_outputs, c->d_outputs, out_bytes);
   if (output_mode == DSD_OUTPUT_DEBUG) {
@@ -522,8 +560,10 @@ int dsd_ctx_destroy(dsd_ctx* c) {
   if (!c) return DSD_OK;
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
-  if (c->graph_exec) cudaGraphExecDestroy(c->graph_exec);
-  if (c->graph) cudaGraphDestroy(c->graph);
+  for (auto& g : c->graphs) {
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+    if (g.graph) cudaGraphDestroy(g.graph);
+  }
   void* dev[] = {c->k_pool, c->v_pool, c->summaries, c->token_counts, c->live, c->table,
                  c->table_n, c->d_in, c->d_scores, c->d_selected, c->d_outputs, c->d_part_acc,
                  c->d_part_ml, c->d_planbuf, c->d_status, c->d_stage};
@@ -1030,19 +1070,7 @@ int dsd_decode_bound(dsd_ctx* c, const float* d_queries, float* d_outputs) {
     if (!c) Fail(DSD_EINVAL, "null context");
     if (c->bound_batch <= 0) Fail(DSD_EINVAL, "no request set bound");
     SetDevice(c);
-    if (!c->graph_exec || c->graph_q != d_queries || c->graph_out != d_outputs) {
-      if (c->graph_exec) cudaGraphExecDestroy(c->graph_exec);
-      if (c->graph) cudaGraphDestroy(c->graph);
-      c->graph_exec = nullptr;
-      c->graph = nullptr;
-      Check(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
-      LaunchStep(c, d_queries, d_outputs, false);
-      Check(cudaStreamEndCapture(c->stream, &c->graph), "end capture");
-      Check(cudaGraphInstantiate(&c->graph_exec, c->graph, 0), "graph instantiate");
-      c->graph_q = d_queries;
-      c->graph_out = d_outputs;
-    }
-    Check(cudaGraphLaunch(c->graph_exec, c->stream), "graph launch");
+    LaunchStepGraph(c, d_queries, d_outputs, false);
   });
 }
 
@@ -1052,7 +1080,18 @@ int dsd_decode_bound_timed(dsd_ctx* c, const float* d_queries, float* d_outputs,
     if (!c) Fail(DSD_EINVAL, "null context");
     if (c->bound_batch <= 0) Fail(DSD_EINVAL, "no request set bound");
     SetDevice(c);
-    LaunchStep(c, d_queries, d_outputs, true);
+    LaunchStepGraph(c, d_queries, d_outputs, true);
+    if (out_timing) {
+      CheckStatus(c);
+      ReadTiming(c, out_timing);
+    }
+  });
+}
+
+int dsd_read_step_timing(dsd_ctx* c, dsd_step_timing* out_timing) {
+  return Guard([&]() {
+    if (!c || !out_timing) Fail(DSD_EINVAL, "null argument");
+    SetDevice(c);
     CheckStatus(c);
     ReadTiming(c, out_timing);
   });

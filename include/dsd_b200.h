@@ -190,9 +190,13 @@ int dsd_decode_step(dsd_ctx* ctx, const int32_t* request_ids, int batch, const f
  * replayed from a CUDA graph; nothing crosses PCIe. */
 int dsd_bind_requests(dsd_ctx* ctx, const int32_t* request_ids, int batch);
 int dsd_decode_bound(dsd_ctx* ctx, const float* d_queries, float* d_outputs);
-/* Same, launched kernel by kernel with CUDA events around each stage. */
+/* Same step from a second graph that also records a CUDA event between the
+ * stages.  out_timing != NULL waits for the step and fills it; NULL returns
+ * at once (steps stay back to back) and dsd_read_step_timing later reads the
+ * stage times of the most recent timed step. */
 int dsd_decode_bound_timed(dsd_ctx* ctx, const float* d_queries, float* d_outputs,
                            dsd_step_timing* out_timing);
+int dsd_read_step_timing(dsd_ctx* ctx, dsd_step_timing* out_timing);
 
 /* Number of kernels one decode step launches (for launch accounting). */
 int dsd_kernels_per_step(void);
