@@ -424,7 +424,8 @@ ContinuousBatchStats RunContinuousSparseDecode(const ModelConfig& config,
       } else {
         ctx.SyncAppendedTokens(cache, results);
       }
-      for (const auto& np : new_pages) ctx.AppendRequestPages(np.first, {np.second});
+      if (tables)
+        for (const auto& np : new_pages) ctx.AppendRequestPages(np.first, {np.second});
     }
     stats.append_sync_ms += Ms(a0, Clock::now());
 

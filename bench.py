@@ -204,7 +204,7 @@ def run_ours(args):
     if world > 1:
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl")
+        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"))
     dsd = importlib.import_module("15-618_dynamic_sparse_decode_b200")
     if not dsd.available():
         raise RuntimeError("no sm_100 GPU visible")
@@ -247,11 +247,11 @@ def run_ours(args):
         stop.record(stream)
         torch.cuda.synchronize()
     last = ctx.read_step_timing()   # stage times of the last timed step
-    ms_total = start.elapsed_time(stop)
-    if world > 1:
-        tt = torch.tensor([ms_total], device=f"cuda:{local}")
-        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        ms_total = float(tt.item())
+    sharding = importlib.import_module("15-618_dynamic_sparse_decode_b200.sharding")
+    ms_local = start.elapsed_time(stop)
+    per_rank = sharding.gather_rank_stats({"ms_per_step": ms_local / args.steps},
+                                          device=f"cuda:{local}")
+    ms_total = sharding.max_over_ranks(ms_local, device=f"cuda:{local}")
     ms_step = ms_total / args.steps
     per_kernel = {k_: [v] for k_, v in last.items()}
 
@@ -279,10 +279,7 @@ def run_ours(args):
         res = ctx.decode_step(reqs, qh, output_mode=dsd.OUTPUT_OUTPUTS, out=host_out)
     e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
     st = ctx.transfer_stats()
-    if world > 1:
-        tt = torch.tensor([e2e_ms], device=f"cuda:{local}")
-        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = float(tt.item())
+    e2e_ms = sharding.max_over_ranks(e2e_ms, device=f"cuda:{local}")
     assert np.array_equal(res["outputs"], do.cpu().numpy()), "e2e and device-resident outputs differ"
 
     peak, peak_kind = peaks()
@@ -306,7 +303,8 @@ def run_ours(args):
                                  "select": float(np.mean(per_kernel["topk_ms"])),
                                  "attention(+combine)": attn_ms},
                    "l2": "inputs larger than L2 (3.7 GB read per step)",
-                   "parallelism": f"request-sharded x{world}"},
+                   "parallelism": f"request-sharded x{world}",
+                   "per_rank_ms_per_step": [round(r["ms_per_step"], 4) for r in per_rank]},
         "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": None},
