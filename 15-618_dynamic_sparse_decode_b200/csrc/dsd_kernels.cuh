@@ -719,6 +719,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(
 
 // One warp per (request, head): out = sum_u e^{m_u-M} acc_u / sum_u e^{m_u-M} l_u,
 // zero when the request attended to no token (SparseAttentionCpu returns zeros).
+// Lanes split the units for M and L (warp reductions), then each lane owns
+// float4 columns of the head and sums the units' partials with their weights.
 __global__ void __launch_bounds__(256) combine_kernel(StepPlan plan,
                                                       const float* __restrict__ part_acc,
                                                       const float* __restrict__ part_ml,
@@ -728,29 +730,38 @@ __global__ void __launch_bounds__(256) combine_kernel(StepPlan plan,
   const int lane = threadIdx.x & 31;
   const int ept = num_heads * head_dim;
   const int pairs = B * num_heads;
+  const int g4 = head_dim >> 2;
   for (int wg = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wg < pairs;
        wg += (gridDim.x * blockDim.x) >> 5) {
-    const int r = wg / num_heads, h = wg % num_heads;
+    const int r = wg / num_heads, h = wg - (wg / num_heads) * num_heads;
     const int u0 = plan.unit_off[r], u1 = plan.unit_off[r + 1];
     float M = -INFINITY;
-    for (int u = u0; u < u1; ++u) M = fmaxf(M, part_ml[(size_t(u) * num_heads + h) * 2]);
-    float* out = outputs + size_t(r) * ept + size_t(h) * head_dim;
+    for (int u = u0 + lane; u < u1; u += 32) M = fmaxf(M, part_ml[(size_t(u) * num_heads + h) * 2]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float4* out = reinterpret_cast<float4*>(outputs + size_t(r) * ept + size_t(h) * head_dim);
     if (M == -INFINITY) {
-      for (int d = lane; d < head_dim; d += 32) out[d] = 0.0f;
+      for (int d = lane; d < g4; d += 32) out[d] = make_float4(0.f, 0.f, 0.f, 0.f);
       continue;
     }
     float L = 0.f;
-    for (int u = u0; u < u1; ++u) {
+    for (int u = u0 + lane; u < u1; u += 32) {
       const float* ml = part_ml + (size_t(u) * num_heads + h) * 2;
       L += ml[1] * expf(ml[0] - M);
     }
-    for (int d = lane; d < head_dim; d += 32) {
-      float o = 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    const float inv = L > 0.f ? 1.0f / L : 0.0f;
+    for (int d = lane; d < g4; d += 32) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int u = u0; u < u1; ++u) {
-        const float wgt = expf(part_ml[(size_t(u) * num_heads + h) * 2] - M);
-        o += wgt * part_acc[size_t(u) * ept + size_t(h) * head_dim + d];
+        const float w = expf(part_ml[(size_t(u) * num_heads + h) * 2] - M);
+        const float4 a = reinterpret_cast<const float4*>(part_acc + size_t(u) * ept +
+                                                         size_t(h) * head_dim)[d];
+        acc.x += w * a.x; acc.y += w * a.y; acc.z += w * a.z; acc.w += w * a.w;
       }
-      out[d] = L > 0.f ? o / L : 0.0f;
+      out[d] = L > 0.f ? make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
 }

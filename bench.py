@@ -103,6 +103,18 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def profiled_traffic(kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_kernel_config3.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_per_launch="):
+                return int(line.split("=")[1])
+    except OSError:
+        pass
+    return None
+
+
 def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -307,7 +319,9 @@ def run_ours(args):
                    "per_rank_ms_per_step": [round(r["ms_per_step"], 4) for r in per_rank]},
         "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None},
+                     "algorithmic_bytes": dom[2],
+                     "traffic": (profiled_traffic("attn" if dom[0] == "attention" else "score")
+                                 if BATCH == 64 else None)},
         "e2e": {"value": world * BATCH / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": st["h2d_bytes"] / args.steps,
                 "d2h_bytes_per_step": st["d2h_bytes"] / args.steps},
