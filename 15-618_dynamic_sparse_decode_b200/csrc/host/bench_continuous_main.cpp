@@ -8,7 +8,9 @@
 //   16 gpu_synthetic_append 17 lazy_release 18 output_mode (0 none, 1 outputs,
 //   2 debug) 19 timing (0 none, 1 kernel_events) 20 benchmark_mode (0 sparse,
 //   1 dense_gpu: not part of this build)
-// Added: 21 device_page_tables (default 1), 22 skip the serial run (default 0).
+// Added: 21 device_page_tables (default 1), 22 skip the serial run (default 0),
+// 23 shard_world (default 1), 24 shard_rank (default 0): serve only requests
+// with request_id % shard_world == shard_rank (one process per GPU).
 #include <cstdlib>
 #include <iomanip>
 #include <iostream>
@@ -99,6 +101,10 @@ int main(int argc, char** argv) try {
   const int bench_mode = Arg(argc, argv, 20, 0);
   o.device_page_tables = Arg(argc, argv, 21, 1) != 0;
   const bool skip_serial = Arg(argc, argv, 22, 0) != 0;
+  const int shard_world = Arg(argc, argv, 23, 1);
+  const int shard_rank = Arg(argc, argv, 24, 0);
+  if (shard_world < 1 || shard_rank < 0 || shard_rank >= shard_world)
+    throw std::invalid_argument("shard_rank must be in [0, shard_world)");
   const char* adm[] = {"cpu_cache", "direct_gpu_upload", "synthetic_gpu_prefill"};
   const char* outn[] = {"no_outputs", "outputs_only", "debug_tensors"};
 
@@ -118,7 +124,8 @@ int main(int argc, char** argv) try {
             << "\nrun_batch_timing_mode="
             << (o.run_batch_timing_mode == dsd::SparseBatchTimingMode::kNone ? "none" : "kernel_events")
             << "\nbenchmark_mode=" << (bench_mode == 1 ? "dense_gpu" : "sparse")
-            << "\ndevice_page_tables=" << o.device_page_tables << "\n";
+            << "\ndevice_page_tables=" << o.device_page_tables << "\nshard_world=" << shard_world
+            << "\nshard_rank=" << shard_rank << "\n";
   if (bench_mode == 1) {
     std::cout << "continuous_dense_gpu_available=0\n"
               << "continuous dense GPU benchmark skipped: not part of this build\n";
@@ -130,12 +137,19 @@ int main(int argc, char** argv) try {
     return 0;
   }
   std::cout << "continuous_sparse_available=1\n";
-  const auto specs =
+  auto specs =
       admission == 2
           ? dsd::BuildSyntheticContinuousSpecs(config, num_requests, arrival_window, min_prompt,
                                                max_prompt, min_decode, max_decode, seed)
           : dsd::BuildSyntheticContinuousWorkload(config, num_requests, arrival_window, min_prompt,
                                                   max_prompt, min_decode, max_decode, seed);
+  if (shard_world > 1) {
+    decltype(specs) mine;
+    for (auto& sp : specs)
+      if (sp.request_id % shard_world == shard_rank) mine.push_back(std::move(sp));
+    specs.swap(mine);
+  }
+  std::cout << "shard_requests=" << specs.size() << "\n";
   if (skip_serial) {
     const auto s = dsd::RunContinuousSparseDecode(config, specs, o);
     std::cout << "total_generated_tokens=" << s.total_generated_tokens << "\n";

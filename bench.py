@@ -338,6 +338,82 @@ def run_ours(args):
         torch.distributed.destroy_process_group()
 
 
+# ---------------------------------------------------------------- continuous serving
+
+CONTINUOUS = {
+    # BASELINE config 4 with the options of the reference's published run
+    # (results/report_experiments/05_continuous_batching_load_sweep/...csv:25: direct GPU
+    # upload, preadmit, precomputed payloads, GPU synthetic append, lazy release)
+    "config4": dict(argv=[128, 32, 64, 1024, 4096, 16, 64, 7, 32, 128, 16, 8, 1, 1, 1, 1, 1, 1, 1, 0, 1, 1],
+                    desc="config4: 128 req, max_active 32/GPU, arrival [0,64], prompt 1024-4096, "
+                         "decode 16-64, H32 D128 P16 k8, direct GPU upload, preadmit, "
+                         "precompute, GPU synthetic append, lazy release",
+                    published=36236.393529),
+    # box-scale serving, synthetic GPU prefill and append
+    "config5": dict(argv=[2048, 128, 512, 8192, 32768, 64, 256, 11, 32, 128, 32, 32, 2, 0, 0, 1, 0, 1, 0, 0, 1, 1],
+                    desc="config5: 2048 req, max_active 128/GPU, arrival [0,512], prompt 8192-32768, "
+                         "decode 64-256, H32 D128 P32 k32, synthetic GPU prefill + append"),
+}
+
+
+def run_continuous(args):
+    """Runs dsd_continuous_bench for this rank's shard (request_id % world == rank)."""
+    world, rank, local = dist_env()
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"))
+        dist.barrier()
+    spec = CONTINUOUS[args.workload]
+    exe = os.path.join(ROOT, "15-618_dynamic_sparse_decode_b200", "bin", "dsd_continuous_bench")
+    argv = [str(x) for x in spec["argv"]] + [str(world), str(rank)]
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES=str(local))
+    out = subprocess.run([exe, *argv], capture_output=True, text=True, env=env)
+    if out.returncode != 0:
+        raise RuntimeError(out.stderr)
+    kv = dict(line.split("=", 1) for line in out.stdout.splitlines() if "=" in line)
+    tokens = float(kv["total_generated_tokens"])
+    ms = float(kv["continuous_sparse_total_ms"])
+    steps = float(kv["continuous_sparse_run_batch_wall_ms"]) / max(1e-9, float(kv["continuous_sparse_avg_step_ms"]))
+    h2d = float(kv["continuous_sparse_device_h2d_bytes"]) / max(1.0, steps)
+    d2h = float(kv["continuous_sparse_device_d2h_bytes"]) / max(1.0, steps)
+    local_stats = {"tokens": tokens, "ms": ms, "steps": steps, "h2d": h2d, "d2h": d2h,
+                   "avg_step_ms": float(kv["continuous_sparse_avg_step_ms"]),
+                   "avg_kernel_ms": float(kv["continuous_sparse_avg_kernel_ms"]),
+                   "admission_ms": float(kv["continuous_sparse_runtime_admission_ms"])}
+    if world > 1:
+        sharding = importlib.import_module("15-618_dynamic_sparse_decode_b200.sharding")
+        ranks = sharding.gather_rank_stats(local_stats, device=f"cuda:{local}")
+    else:
+        ranks = [local_stats]
+    if rank == 0:
+        tot = sum(r["tokens"] for r in ranks)
+        wall = max(r["ms"] for r in ranks)
+        value = tot / (wall * 1e-3)
+        line = {
+            "metric": "continuous sparse decode tokens/s", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": int(max(r["steps"] for r in ranks)), "warmup": 0,
+            "ms_per_step": float(np.mean([r["avg_step_ms"] for r in ranks])),
+            "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": (value / spec["published"] if spec.get("published") and world == 1
+                            else None),
+            "dtype": "f32", "data": "synthetic (reference mt19937 workload generator)",
+            "config": {"workload": spec["desc"], "argv": argv,
+                       "per_rank": [{k: round(v, 3) for k, v in r.items()} for r in ranks],
+                       "timing": "host wall time of the serving loop per rank (admission, "
+                                 "steps, appends, releases); max over ranks"},
+            "e2e": {"value": value, "unit": "tokens/s",
+                    "h2d_bytes_per_step": float(np.mean([r["h2d"] for r in ranks])),
+                    "d2h_bytes_per_step": float(np.mean([r["d2h"] for r in ranks]))},
+            "gpu_launches": None,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def main():
     global BATCH
     ap = argparse.ArgumentParser()
@@ -346,6 +422,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="config3", choices=["config3", "config4", "config5"],
+                    help="config3: the headline batched decode step; config4/5: continuous "
+                         "serving through dsd_continuous_bench, request-sharded per GPU")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="requests per GPU (default: the config-3 batch of 64; smaller only "
                          "for profiling captures)")
@@ -353,6 +432,8 @@ def main():
     BATCH = args.batch
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "config3":
+        run_continuous(args)
     else:
         run_ours(args)
 
