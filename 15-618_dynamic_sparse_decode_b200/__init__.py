@@ -60,6 +60,7 @@ SIGNATURES = [
     ("dsd_ctx_device_pointers", ctypes.c_int, [_VP, ctypes.POINTER(_VP), ctypes.POINTER(_VP),
                                                ctypes.POINTER(_VP), ctypes.POINTER(_VP)]),
     ("dsd_ctx_stream", _VP, [_VP]),
+    ("dsd_step_host_buffers", ctypes.c_int, [_VP, ctypes.POINTER(_VP), ctypes.POINTER(_VP)]),
     ("dsd_pool_reset", ctypes.c_int, [_VP]),
     ("dsd_pool_upload_pages", ctypes.c_int, [_VP, _I32P, _I32P, ctypes.c_int, _F32P, _F32P,
                                              ctypes.c_int]),

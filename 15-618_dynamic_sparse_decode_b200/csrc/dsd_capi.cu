@@ -11,7 +11,6 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
-#include <map>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -352,7 +351,8 @@ void RunHostStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int outpu
   }
   CheckStatus(c);  // synchronises the stream
   if (timing) ReadTiming(c, out_timing);
-  if (output_mode != DSD_OUTPUT_NONE && outputs) std::memcpy(outputs, c->h_outputs, out_bytes);
+  if (output_mode != DSD_OUTPUT_NONE && outputs && outputs != c->h_outputs)
+    std::memcpy(outputs, c->h_outputs, out_bytes);
   if (output_mode == DSD_OUTPUT_DEBUG) {
     if (scores && total_cand > 0)
       std::memcpy(scores, c->h_scores, size_t(total_cand) * sizeof(float));
@@ -396,30 +396,27 @@ void UploadTableEntries(dsd_ctx* c, const std::vector<int>& triples,
   if (nt) dsdk::table_write_kernel<<<(unsigned)((nt + 255) / 256), 256, 0, c->stream>>>(
       d, (int)nt, c->opt.max_pages_per_request, c->table, c->table_n);
   Check(cudaGetLastError(), "table kernels");
-  Sync(c);
+  // no wait: later users of the staging buffer are ordered on the same stream
 }
 
-// Groups tokens by page (first-seen page order, offsets ascending within a page).
+// Groups tokens by page: indices sorted by (page, offset); one group per page.
 void GroupTokens(const int32_t* page_ids, const int32_t* offs, int n, std::vector<int>* order,
                  std::vector<int>* group_page, std::vector<int>* group_first) {
-  std::map<int, std::vector<int>> by_page;
-  std::vector<int> first_seen;
-  for (int i = 0; i < n; ++i) {
-    auto& v = by_page[page_ids[i]];
-    if (v.empty()) first_seen.push_back(page_ids[i]);
-    v.push_back(i);
-  }
-  order->clear();
+  order->resize(static_cast<size_t>(n));
+  for (int i = 0; i < n; ++i) (*order)[static_cast<size_t>(i)] = i;
+  std::sort(order->begin(), order->end(), [&](int a, int b) {
+    return page_ids[a] != page_ids[b] ? page_ids[a] < page_ids[b] : offs[a] < offs[b];
+  });
   group_page->clear();
   group_first->clear();
-  for (int p : first_seen) {
-    auto& v = by_page[p];
-    std::stable_sort(v.begin(), v.end(), [&](int a, int b) { return offs[a] < offs[b]; });
-    group_page->push_back(p);
-    group_first->push_back(static_cast<int>(order->size()));
-    order->insert(order->end(), v.begin(), v.end());
+  for (int j = 0; j < n; ++j) {
+    const int i = (*order)[static_cast<size_t>(j)];
+    if (j == 0 || page_ids[i] != page_ids[(*order)[static_cast<size_t>(j - 1)]]) {
+      group_page->push_back(page_ids[i]);
+      group_first->push_back(j);
+    }
   }
-  group_first->push_back(static_cast<int>(order->size()));
+  group_first->push_back(n);
 }
 
 }  // namespace
@@ -591,6 +588,14 @@ int dsd_ctx_device_pointers(dsd_ctx* c, float** keys, float** values, float** su
 }
 
 void* dsd_ctx_stream(dsd_ctx* c) { return c ? static_cast<void*>(c->stream) : nullptr; }
+
+int dsd_step_host_buffers(dsd_ctx* c, float** queries, float** outputs) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    if (queries) *queries = QPtr(c);
+    if (outputs) *outputs = c->h_outputs;
+  });
+}
 
 int dsd_pool_reset(dsd_ctx* c) {
   return Guard([&]() {
@@ -810,7 +815,7 @@ int dsd_append_tokens(dsd_ctx* c, const int32_t* page_ids, const int32_t* token_
         reinterpret_cast<const float*>(c->d_stage + payload), c->ept, c->cfg.page_size,
         c->k_pool, c->v_pool, c->summaries, c->token_counts, c->live);
     Check(cudaGetLastError(), "append kernel");
-    Sync(c);
+    // no wait: later users of the staging buffer are ordered on the same stream
     for (int i = 0; i < n; ++i)
       c->host_counts[page_ids[i]] = std::max(c->host_counts[page_ids[i]], token_offsets[i] + 1);
     UploadTableEntries(c, triples, counts);
@@ -845,7 +850,7 @@ int dsd_append_tokens_synthetic(dsd_ctx* c, const int32_t* page_ids, const int32
         d, d + ng, toff, toff + n, toff + 2 * n, c->ept, c->cfg.page_size, c->k_pool, c->v_pool,
         c->summaries, c->token_counts, c->live);
     Check(cudaGetLastError(), "synthetic append kernel");
-    Sync(c);
+    // no wait: later users of the staging buffer are ordered on the same stream
     for (int i = 0; i < n; ++i)
       c->host_counts[page_ids[i]] = std::max(c->host_counts[page_ids[i]], token_offsets[i] + 1);
   });
@@ -863,7 +868,7 @@ int dsd_pool_free_pages(dsd_ctx* c, const int32_t* page_ids, int n) {
                                                       c->ept, c->summaries, c->token_counts,
                                                       c->live);
     Check(cudaGetLastError(), "free kernel");
-    Sync(c);
+    // no wait: later users of the staging buffer are ordered on the same stream
     for (int i = 0; i < n; ++i) c->host_counts[page_ids[i]] = 0;
   });
 }
@@ -937,7 +942,7 @@ int dsd_decode_batch(dsd_ctx* c, int batch, const float* queries, const int32_t*
     hdr[0] = batch;
     hdr[1] = 0;
     std::memcpy(ReqPtr(c), cand_offsets, size_t(batch + 1) * 4);
-    std::memcpy(QPtr(c), queries, size_t(batch) * c->ept * 4);
+    if (queries != QPtr(c)) std::memcpy(QPtr(c), queries, size_t(batch) * c->ept * 4);
     std::memcpy(IdsPtr(c), cand_ids, size_t(total_cand) * 4);
     H2D(c, c->d_in, c->h_in, c->in_q_off + size_t(batch) * c->ept * 4);
     if (total_cand > 0) H2D(c, c->d_in + c->in_ids_off, IdsPtr(c), size_t(total_cand) * 4);
@@ -1045,7 +1050,7 @@ int dsd_decode_step(dsd_ctx* c, const int32_t* request_ids, int batch, const flo
     SetDevice(c);
     int tc = 0, ts = 0;
     PackSlots(c, request_ids, batch, &tc, &ts);
-    std::memcpy(QPtr(c), queries, size_t(batch) * c->ept * 4);
+    if (queries != QPtr(c)) std::memcpy(QPtr(c), queries, size_t(batch) * c->ept * 4);
     H2D(c, c->d_in, c->h_in, c->in_q_off + size_t(batch) * c->ept * 4);
     RunHostStep(c, batch, tc, ts, output_mode, timing, outputs, scores, selected, out_timing);
   });

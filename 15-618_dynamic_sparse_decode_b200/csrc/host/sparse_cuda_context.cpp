@@ -46,9 +46,9 @@ SparseCudaContext::SparseCudaContext(const PagedKvCache& cache, const ModelConfi
     dsd_ctx_destroy(ctx_);
     throw;
   }
-  const std::size_t mb = static_cast<std::size_t>(std::max(1, max_batch_size));
-  queries_.reserve(mb * elements_per_token_);
-  outputs_.resize(mb * elements_per_token_);
+  // queries are packed straight into the context's pinned staging and
+  // outputs read from it: no extra host copy per step
+  ThrowIf(dsd_step_host_buffers(ctx_, &host_queries_, &host_outputs_));
 }
 
 SparseCudaContext::~SparseCudaContext() {
@@ -92,6 +92,8 @@ SparseBatchCudaResult SparseCudaContext::Run(const std::vector<const RequestStat
   const bool timed = options.timing_mode == SparseBatchTimingMode::kKernelEvents;
   const int B = static_cast<int>(requests.size());
   const int ept = elements_per_token_;
+  if (B > max_batch_size_)
+    throw std::invalid_argument("request batch exceeds sparse CUDA context capacity");
   const auto wall0 = std::chrono::steady_clock::now();
 
   double* prep = timed ? &result.runtime_overheads.time_prepare_sparse_layout_ms : nullptr;
@@ -99,7 +101,6 @@ SparseBatchCudaResult SparseCudaContext::Run(const std::vector<const RequestStat
   int total_cand = 0;
   {
     ScopedStageTimer t(prep);
-    queries_.clear();
     offsets_.assign(1, 0);
     ids_.clear();
     request_ids_.clear();
@@ -108,7 +109,7 @@ SparseBatchCudaResult SparseCudaContext::Run(const std::vector<const RequestStat
       if (!q) throw std::invalid_argument("request pointer must be non-null");
       if (static_cast<int>(q->query.size()) != ept)
         throw std::invalid_argument("query length does not match model config");
-      queries_.insert(queries_.end(), q->query.begin(), q->query.end());
+      std::copy(q->query.begin(), q->query.end(), host_queries_ + static_cast<std::size_t>(r) * ept);
       int n;
       if (tables) {
         request_ids_.push_back(q->request_id);
@@ -133,16 +134,15 @@ SparseBatchCudaResult SparseCudaContext::Run(const std::vector<const RequestStat
 
   const int mode = options.output_mode == SparseBatchOutputMode::kNoOutputs ? DSD_OUTPUT_NONE
                    : debug ? DSD_OUTPUT_DEBUG : DSD_OUTPUT_OUTPUTS;
-  outputs_.resize(static_cast<std::size_t>(B) * ept);
   scores_.resize(static_cast<std::size_t>(std::max(1, total_cand)));
   selected_.resize(static_cast<std::size_t>(std::max(1, total_sel)));
   dsd_step_timing st{};
   if (tables) {
-    ThrowIf(dsd_decode_step(ctx_, request_ids_.data(), B, queries_.data(), mode, timed ? 1 : 0,
-                            outputs_.data(), scores_.data(), selected_.data(), &st));
+    ThrowIf(dsd_decode_step(ctx_, request_ids_.data(), B, host_queries_, mode, timed ? 1 : 0,
+                            host_outputs_, scores_.data(), selected_.data(), &st));
   } else {
-    ThrowIf(dsd_decode_batch(ctx_, B, queries_.data(), offsets_.data(), ids_.data(), mode,
-                             timed ? 1 : 0, outputs_.data(), scores_.data(), selected_.data(), &st));
+    ThrowIf(dsd_decode_batch(ctx_, B, host_queries_, offsets_.data(), ids_.data(), mode,
+                             timed ? 1 : 0, host_outputs_, scores_.data(), selected_.data(), &st));
   }
   if (timed) {
     result.aggregate_timings.page_scoring_ms = st.score_ms;
@@ -171,8 +171,8 @@ SparseBatchCudaResult SparseCudaContext::Run(const std::vector<const RequestStat
       one.selected_page_ids.assign(selected_.begin() + sel_off[static_cast<std::size_t>(r)],
                                    selected_.begin() + sel_off[static_cast<std::size_t>(r) + 1]);
     }
-    one.output.output.assign(outputs_.begin() + static_cast<std::ptrdiff_t>(r) * ept,
-                             outputs_.begin() + static_cast<std::ptrdiff_t>(r + 1) * ept);
+    one.output.output.assign(host_outputs_ + static_cast<std::ptrdiff_t>(r) * ept,
+                             host_outputs_ + static_cast<std::ptrdiff_t>(r + 1) * ept);
     result.per_request.push_back(std::move(one));
   }
   if (debug && tables) {

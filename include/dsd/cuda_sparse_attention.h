@@ -116,9 +116,10 @@ class SparseCudaContext {
   dsd_ctx* ctx_ = nullptr;
   std::unique_ptr<DevicePagePool> pool_;
   std::vector<const RequestState*> ptr_scratch_;
-  std::vector<float> queries_;
+  float* host_queries_ = nullptr;   // pinned step staging owned by the context
+  float* host_outputs_ = nullptr;
   std::vector<int> offsets_, ids_, request_ids_, selected_;
-  std::vector<float> outputs_, scores_;
+  std::vector<float> scores_;
 };
 
 SparseDecodeResult SparseDecodeCuda(const PagedKvCache& cache, const RequestState& request,

@@ -51,6 +51,9 @@ class PagedKvCache {
                                             bool force_new_page);
   AppendTokenResult AppendTokenMetadataOnly(int request_id, bool force_new_page);
 
+  // Frees the request's pages (LIFO reuse).  Their raw PageSummaryPool()
+  // rows are left as they were; a free page reads as zeros through
+  // CopyPageSummary / BuildPageSummary and is cleared when reallocated.
   std::vector<PageId> ReleaseRequest(int request_id);
   void Reset();
 

@@ -96,6 +96,11 @@ int dsd_ctx_device_pointers(dsd_ctx* ctx, float** keys, float** values, float** 
                             int32_t** token_counts);
 /* The CUDA stream every call of this context is ordered on (cudaStream_t). */
 void* dsd_ctx_stream(dsd_ctx* ctx);
+/* The context's pinned per-step staging: queries [max_batch][H*D] and outputs
+ * [max_batch][H*D].  Passing these pointers as `queries` / `outputs` to
+ * dsd_decode_batch / dsd_decode_step skips one host copy each way.  Valid
+ * until the context is destroyed; the next step overwrites them. */
+int dsd_step_host_buffers(dsd_ctx* ctx, float** queries, float** outputs);
 
 /* DevicePagePool::Reset (src/device_page_pool.cpp:286-302): zero counts, live
  * flags and summaries; drop every request page table. */
