@@ -278,7 +278,7 @@ void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool cap
   const int target_units = 8 * c->num_sms;
   if (timed) RecordEvent(c, 0, capturing);
   dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, c->stream>>>(plan, c->cfg.top_k_pages,
-                                                             target_units);
+                                                             target_units, c->num_sms);
   dsdk::score_kernel<<<c->num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, c->stream>>>(
       plan, d_q, c->summaries, c->ept, c->scale, c->d_scores);
   if (timed) RecordEvent(c, 1, capturing);
@@ -1237,7 +1237,7 @@ extern "C" int dsd_decode_batch_noalloc(int device, const dsd_model_config* conf
                           cudaMemcpyHostToDevice, s), "offsets copy");
     const int target = std::min(kNaMaxUnitsTarget, 2 * nd.num_sms);
     const float scale = 1.0f / std::sqrt(static_cast<float>(D));
-    dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, s>>>(plan, cfg.top_k_pages, target);
+    dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, s>>>(plan, cfg.top_k_pages, target, nd.num_sms);
     dsdk::score_kernel<<<nd.num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, s>>>(
         plan, d_queries, d_summaries, ept, scale, scores);
     dsdk::select_kernel<<<std::min(batch, 2 * nd.num_sms), dsdk::kSelectThreads, 0, s>>>(

@@ -71,7 +71,7 @@ struct StepPlan {
   int* sel_off;            // [B+1]
   int* tile_off;           // [B+1]
   int* unit_off;           // [B+1]
-  int* misc;               // [0] pages per attention unit
+  int* misc;               // [0] pages per attention unit, [1] score tile size
   int* status;             // error bits
 };
 
@@ -192,7 +192,7 @@ __device__ __forceinline__ void block_exclusive_scan(int (&v)[N], int (&total)[N
 // request list: candidate counts (CSR offsets or page-table lengths),
 // selected counts min(k, n), score tiles and split-K attention units.
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(StepPlan plan, int top_k,
-                                                            int target_units) {
+                                                            int target_units, int score_grid) {
   const int B = plan.hdr[0];
   const int mode = plan.hdr[1];
   const int r = threadIdx.x;
@@ -209,20 +209,44 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(StepPlan plan, int t
     if (n < 0) { n = 0; atomicOr(plan.status, kStatusBadInput); }
   }
   const int ksel = max(0, min(top_k, n));
-  int v[3] = {n, ksel, (n + kScoreTile - 1) / kScoreTile};
-  int tot[3];
-  block_exclusive_scan<3>(v, tot);
+  int v[2] = {n, ksel};
+  int tot[2];
+  block_exclusive_scan<2>(v, tot);
+  // Score tile size: the smallest ts <= kScoreTile whose tile count fits a
+  // whole number of waves over the score grid, so every CTA runs the same
+  // number of (slightly shorter) tiles instead of a ragged last wave.
+  __shared__ int s_count;
+  const int waves = max(1, (tot[0] + kScoreTile * score_grid - 1) / (kScoreTile * score_grid));
+  const int target_tiles = waves * score_grid;
+  int ts = max(1, min(kScoreTile, (tot[0] + target_tiles - 1) / max(1, target_tiles)));
+  for (; ts < kScoreTile; ++ts) {
+    if (threadIdx.x == 0) s_count = 0;
+    __syncthreads();
+    const int c = (n + ts - 1) / ts;
+    int wsum = c;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+    if ((threadIdx.x & 31) == 0 && wsum) atomicAdd(&s_count, wsum);
+    __syncthreads();
+    const int count = s_count;
+    __syncthreads();
+    if (count <= target_tiles) break;
+  }
+  int t1[1] = {(n + ts - 1) / ts};
+  int ttot[1];
+  block_exclusive_scan<1>(t1, ttot);
   if (r < B) {
     plan.n_cand[r] = n;
     plan.id_base[r] = base;
     plan.score_off[r] = v[0];
     plan.sel_off[r] = v[1];
-    plan.tile_off[r] = v[2];
+    plan.tile_off[r] = t1[0];
   }
   if (r == 0) {
     plan.score_off[B] = tot[0];
     plan.sel_off[B] = tot[1];
-    plan.tile_off[B] = tot[2];
+    plan.tile_off[B] = ttot[0];
+    plan.misc[1] = ts;
   }
   // pages per attention unit: enough units to fill the GPU, at most 16 pages
   int ppu = (tot[1] + target_units - 1) / max(1, target_units);
@@ -258,14 +282,16 @@ __device__ __forceinline__ void cp_async_wait() {
 // kScoreChunk floats per row per stage, filled by all threads with coalesced
 // 16-byte cp.async copies (one warp moves two 256 B row chunks per
 // instruction); row kScoreTile of every stage holds the query chunk.
-// Thread t always copies rows (t>>4) + 8j, column t&15, so it keeps the
-// page ids of the tile it is loading in registers.
+// Thread t always copies rows t/kCols + kRowStep*j, column t%kCols, so it
+// keeps the page offsets of the tile it is loading in registers.
 __global__ void __launch_bounds__(kScoreThreads, 1) score_kernel(
     StepPlan plan, const float* __restrict__ queries, const float* __restrict__ summaries,
     int ept, float scale, float* __restrict__ scores) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   float* stage_base = reinterpret_cast<float*>(smem_raw);
-  constexpr int kRowsPerThread = (kScoreRows + 7) / 8;   // 17
+  constexpr int kCols = kScoreChunk / 4;                  // float4 columns per row chunk
+  constexpr int kRowStep = kScoreThreads / kCols;         // rows one pass of the CTA covers
+  constexpr int kRowsPerThread = (kScoreRows + kRowStep - 1) / kRowStep;
   constexpr int kStageFloats = kScoreRows * kScoreRowStride;
 
   const int tid = threadIdx.x;
@@ -273,9 +299,10 @@ __global__ void __launch_bounds__(kScoreThreads, 1) score_kernel(
   const int mode = plan.hdr[1];
   const int* ids_src = mode == 0 ? plan.cand_ids : plan.table;
   const int total_tiles = plan.tile_off[B];
+  const int ts = plan.misc[1];
   const int nchunks = (ept + kScoreChunk - 1) / kScoreChunk;
-  const int col = tid & 15;
-  const int row0 = tid >> 4;
+  const int col = tid % kCols;
+  const int row0 = tid / kCols;
 
   // ---- loader state (runs kScoreStages-1 chunks ahead of the compute)
   int ld_tile = blockIdx.x, ld_ch = 0, ld_slot = 0, ld_nvalid = 0;
@@ -284,13 +311,13 @@ __global__ void __launch_bounds__(kScoreThreads, 1) score_kernel(
   auto load_tile = [&]() {
     if (ld_tile >= total_tiles) return;
     const int r = upper_segment(plan.tile_off, B, ld_tile);
-    const int c0 = (ld_tile - plan.tile_off[r]) * kScoreTile;
-    ld_nvalid = min(kScoreTile, plan.n_cand[r] - c0);
+    const int c0 = (ld_tile - plan.tile_off[r]) * ts;
+    ld_nvalid = min(ts, plan.n_cand[r] - c0);
     ld_q = queries + size_t(r) * ept;
     const int* ids = ids_src + plan.id_base[r] + c0;
 #pragma unroll
     for (int j = 0; j < kRowsPerThread; ++j) {
-      const int row = row0 + 8 * j;
+      const int row = row0 + kRowStep * j;
       ld_off[j] = row < ld_nvalid ? size_t(__ldg(ids + row)) * ept : 0;
     }
   };
@@ -302,7 +329,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1) score_kernel(
         const size_t coff = size_t(ld_ch) * kScoreChunk + col * 4;
 #pragma unroll
         for (int j = 0; j < kRowsPerThread; ++j) {
-          const int row = row0 + 8 * j;
+          const int row = row0 + kRowStep * j;
           if (row < ld_nvalid) {
             cp_async16(st + row * kScoreRowStride + col * 4, summaries + ld_off[j] + coff);
           } else if (row == kScoreTile) {
@@ -327,8 +354,8 @@ __global__ void __launch_bounds__(kScoreThreads, 1) score_kernel(
   int slot = 0;
   for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
     const int r = upper_segment(plan.tile_off, B, tile);
-    const int c0 = (tile - plan.tile_off[r]) * kScoreTile;
-    const int nvalid = min(kScoreTile, plan.n_cand[r] - c0);
+    const int c0 = (tile - plan.tile_off[r]) * ts;
+    const int nvalid = min(ts, plan.n_cand[r] - c0);
     float acc = 0.0f;
     for (int ch = 0; ch < nchunks; ++ch) {
       cp_async_wait<kScoreStages - 2>();
