@@ -330,10 +330,34 @@ void ReadTiming(dsd_ctx* c, dsd_step_timing* t) {
   Check(cudaEventElapsedTime(&t->total_ms, c->ev[0], c->ev[3]), "event time");
 }
 
+// True for page-locked host memory (cudaMallocHost / cudaHostRegister):
+// such buffers are DMA'd directly, without the staging copy.
+bool IsPinnedHost(const void* p) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost;
+}
+
 int* HdrPtr(dsd_ctx* c) { return reinterpret_cast<int*>(c->h_in); }
 int* ReqPtr(dsd_ctx* c) { return reinterpret_cast<int*>(c->h_in + c->in_req_off); }
 float* QPtr(dsd_ctx* c) { return reinterpret_cast<float*>(c->h_in + c->in_q_off); }
 int* IdsPtr(dsd_ctx* c) { return reinterpret_cast<int*>(c->h_in + c->in_ids_off); }
+
+// Uploads the step header, request list and queries.  Pinned caller queries
+// go straight to the device; pageable ones through the pinned staging.
+void UploadQueries(dsd_ctx* c, const float* queries, int batch) {
+  const size_t qbytes = size_t(batch) * c->ept * 4;
+  if (queries != QPtr(c) && IsPinnedHost(queries)) {
+    H2D(c, c->d_in, c->h_in, c->in_q_off);
+    H2D(c, c->d_in + c->in_q_off, queries, qbytes);
+    return;
+  }
+  if (queries != QPtr(c)) std::memcpy(QPtr(c), queries, qbytes);
+  H2D(c, c->d_in, c->h_in, c->in_q_off + qbytes);
+}
 
 // Common tail of a host-facing step: launch, copy results back, unpack.
 void RunHostStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int output_mode,
@@ -342,7 +366,9 @@ void RunHostStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int outpu
   LaunchStepGraph(c, reinterpret_cast<const float*>(c->d_in + c->in_q_off), c->d_outputs,
                   timing != 0);
   const size_t out_bytes = size_t(batch) * c->ept * sizeof(float);
-  if (output_mode != DSD_OUTPUT_NONE && outputs) D2H(c, c->h_outputs, c->d_outputs, out_bytes);
+  const bool direct_out = outputs && outputs != c->h_outputs && IsPinnedHost(outputs);
+  if (output_mode != DSD_OUTPUT_NONE && outputs)
+    D2H(c, direct_out ? outputs : c->h_outputs, c->d_outputs, out_bytes);
   if (output_mode == DSD_OUTPUT_DEBUG) {
     if (scores && total_cand > 0)
       D2H(c, c->h_scores, c->d_scores, size_t(total_cand) * sizeof(float));
@@ -351,7 +377,7 @@ void RunHostStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int outpu
   }
   CheckStatus(c);  // synchronises the stream
   if (timing) ReadTiming(c, out_timing);
-  if (output_mode != DSD_OUTPUT_NONE && outputs && outputs != c->h_outputs)
+  if (output_mode != DSD_OUTPUT_NONE && outputs && outputs != c->h_outputs && !direct_out)
     std::memcpy(outputs, c->h_outputs, out_bytes);
   if (output_mode == DSD_OUTPUT_DEBUG) {
     if (scores && total_cand > 0)
@@ -942,9 +968,8 @@ int dsd_decode_batch(dsd_ctx* c, int batch, const float* queries, const int32_t*
     hdr[0] = batch;
     hdr[1] = 0;
     std::memcpy(ReqPtr(c), cand_offsets, size_t(batch + 1) * 4);
-    if (queries != QPtr(c)) std::memcpy(QPtr(c), queries, size_t(batch) * c->ept * 4);
     std::memcpy(IdsPtr(c), cand_ids, size_t(total_cand) * 4);
-    H2D(c, c->d_in, c->h_in, c->in_q_off + size_t(batch) * c->ept * 4);
+    UploadQueries(c, queries, batch);
     if (total_cand > 0) H2D(c, c->d_in + c->in_ids_off, IdsPtr(c), size_t(total_cand) * 4);
     RunHostStep(c, batch, total_cand, total_sel, output_mode, timing, outputs, scores, selected,
                 out_timing);
@@ -1050,8 +1075,7 @@ int dsd_decode_step(dsd_ctx* c, const int32_t* request_ids, int batch, const flo
     SetDevice(c);
     int tc = 0, ts = 0;
     PackSlots(c, request_ids, batch, &tc, &ts);
-    if (queries != QPtr(c)) std::memcpy(QPtr(c), queries, size_t(batch) * c->ept * 4);
-    H2D(c, c->d_in, c->h_in, c->in_q_off + size_t(batch) * c->ept * 4);
+    UploadQueries(c, queries, batch);
     RunHostStep(c, batch, tc, ts, output_mode, timing, outputs, scores, selected, out_timing);
   });
 }

@@ -219,3 +219,22 @@ def test_bound_graph_step_matches_host_step(dsd, orc):
         t = ctx.decode_bound_timed(dq.data_ptr(), do.data_ptr())
         assert np.array_equal(do.cpu().numpy(), host["outputs"])
         assert t["score_ms"] > 0 and t["attention_ms"] > 0
+
+
+def test_pinned_host_buffers_match_pageable(dsd, orc):
+    """Pinned caller buffers are DMA'd directly; results equal the staged path."""
+    torch = pytest.importorskip("torch")
+    b = orc.synthetic_batch(32, 128, 16, 8, 8, 300, 900, 23)
+    with make_ctx(dsd, b, tables=True) as ctx:
+        ctx.upload_pool(b.key_pool, b.value_pool, b.token_counts)
+        for r in range(b.batch):
+            ctx.set_request_pages(r, b.cand_ids[b.cand_offsets[r]:b.cand_offsets[r + 1]])
+        ref = ctx.decode_step(np.arange(b.batch), b.queries, output_mode=dsd.OUTPUT_OUTPUTS)
+        q_pin = torch.empty(b.queries.shape, dtype=torch.float32, pin_memory=True).numpy()
+        q_pin[:] = b.queries
+        o_pin = torch.zeros(b.queries.shape, dtype=torch.float32, pin_memory=True).numpy()
+        got = ctx.decode_step(np.arange(b.batch), q_pin, output_mode=dsd.OUTPUT_OUTPUTS, out=o_pin)
+        assert got["outputs"] is o_pin
+        assert np.array_equal(o_pin, ref["outputs"])
+        res = ctx.decode_batch(q_pin, b.cand_offsets, b.cand_ids)
+        check_against_oracle(orc, b, res, 1e-4)
