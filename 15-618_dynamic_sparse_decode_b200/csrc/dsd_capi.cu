@@ -159,7 +159,8 @@ struct dsd_ctx {
   // pool
   float* k_pool = nullptr;
   float* v_pool = nullptr;
-  float* summaries = nullptr;
+  float* summaries = nullptr;     // chunk-major in 128-page groups (see summary_off)
+  size_t summary_floats = 0;
   int* token_counts = nullptr;
   uint8_t* live = nullptr;
   std::vector<int> host_counts;  // mirror of token_counts for validation
@@ -278,8 +279,8 @@ void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool cap
   const int target_units = 8 * c->num_sms;
   if (timed) RecordEvent(c, 0, capturing);
   dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, c->stream>>>(plan, c->cfg.top_k_pages,
-                                                             target_units, c->num_sms);
-  dsdk::score_kernel<<<c->num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, c->stream>>>(
+                                                             target_units, 2 * c->num_sms);
+  dsdk::score_kernel<<<2 * c->num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, c->stream>>>(
       plan, d_q, c->summaries, c->ept, c->scale, c->d_scores);
   if (timed) RecordEvent(c, 1, capturing);
   const int sel_grid = std::max(1, std::min(c->opt.max_batch, 2 * c->num_sms));
@@ -509,10 +510,12 @@ int dsd_ctx_create(int device, const dsd_model_config* config, const dsd_ctx_opt
       const size_t cap = size_t(opt.capacity_pages);
       c->k_pool = DeviceAlloc<float>(cap * cfg.page_size * ept, "key pool");
       c->v_pool = DeviceAlloc<float>(cap * cfg.page_size * ept, "value pool");
-      c->summaries = DeviceAlloc<float>(cap * ept, "page summaries");
+      c->summary_floats = (cap + 127) / 128 * dsdk::summary_group_floats(ept);
+      c->summaries = DeviceAlloc<float>(c->summary_floats, "page summaries");
       c->token_counts = DeviceAlloc<int>(cap, "token counts");
       c->live = DeviceAlloc<uint8_t>(cap, "live mask");
-      Check(cudaMemsetAsync(c->summaries, 0, std::max<size_t>(1, cap * ept) * 4, c->stream), "memset");
+      Check(cudaMemsetAsync(c->summaries, 0, std::max<size_t>(1, c->summary_floats) * 4, c->stream),
+            "memset");
       Check(cudaMemsetAsync(c->token_counts, 0, std::max<size_t>(1, cap) * 4, c->stream), "memset");
       Check(cudaMemsetAsync(c->live, 0, std::max<size_t>(1, cap), c->stream), "memset");
       c->host_counts.assign(cap, 0);
@@ -628,7 +631,8 @@ int dsd_pool_reset(dsd_ctx* c) {
     if (!c) Fail(DSD_EINVAL, "null context");
     SetDevice(c);
     const size_t cap = size_t(c->opt.capacity_pages);
-    Check(cudaMemsetAsync(c->summaries, 0, std::max<size_t>(1, cap * c->ept) * 4, c->stream), "memset");
+    Check(cudaMemsetAsync(c->summaries, 0, std::max<size_t>(1, c->summary_floats) * 4, c->stream),
+          "memset");
     Check(cudaMemsetAsync(c->token_counts, 0, std::max<size_t>(1, cap) * 4, c->stream), "memset");
     Check(cudaMemsetAsync(c->live, 0, std::max<size_t>(1, cap), c->stream), "memset");
     std::fill(c->host_counts.begin(), c->host_counts.end(), 0);
@@ -908,7 +912,15 @@ int dsd_download_page(dsd_ctx* c, int page_id, float* keys, float* values, float
     const size_t pf = size_t(c->cfg.page_size) * c->ept;
     if (keys) D2H(c, keys, c->k_pool + size_t(page_id) * pf, pf * 4);
     if (values) D2H(c, values, c->v_pool + size_t(page_id) * pf, pf * 4);
-    if (summary) D2H(c, summary, c->summaries + size_t(page_id) * c->ept, size_t(c->ept) * 4);
+    if (summary) {
+      // gather the page's NC chunks of CW floats (stride 128*CW) into one row
+      const int cw = dsdk::summary_chunk(c->ept);
+      Check(cudaMemcpy2DAsync(summary, size_t(cw) * 4,
+                              c->summaries + dsdk::summary_row_base(page_id, c->ept),
+                              size_t(128) * cw * 4, size_t(cw) * 4, size_t(c->ept / cw),
+                              cudaMemcpyDeviceToHost, c->stream), "summary download");
+      CountD2H(c, size_t(c->ept) * 4);
+    }
     if (token_count) D2H(c, token_count, c->token_counts + page_id, 4);
     Sync(c);
   });
@@ -1261,8 +1273,8 @@ extern "C" int dsd_decode_batch_noalloc(int device, const dsd_model_config* conf
                           cudaMemcpyHostToDevice, s), "offsets copy");
     const int target = std::min(kNaMaxUnitsTarget, 2 * nd.num_sms);
     const float scale = 1.0f / std::sqrt(static_cast<float>(D));
-    dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, s>>>(plan, cfg.top_k_pages, target, nd.num_sms);
-    dsdk::score_kernel<<<nd.num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, s>>>(
+    dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, s>>>(plan, cfg.top_k_pages, target, 2 * nd.num_sms);
+    dsdk::score_kernel<<<2 * nd.num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, s>>>(
         plan, d_queries, d_summaries, ept, scale, scores);
     dsdk::select_kernel<<<std::min(batch, 2 * nd.num_sms), dsdk::kSelectThreads, 0, s>>>(
         plan, scores, selected);

@@ -34,7 +34,7 @@ constexpr int kPlanThreads = 1024;
 constexpr int kScoreTile = 128;
 constexpr int kScoreChunk = 64;                     // floats of a summary row per stage
 constexpr int kScoreRowStride = kScoreChunk + 4;    // +16 B: conflict-free float4 rows
-constexpr int kScoreStages = 6;
+constexpr int kScoreStages = 3;
 constexpr int kScoreThreads = kScoreTile;
 constexpr int kScoreRows = kScoreTile + 1;          // + the query chunk
 constexpr size_t kScoreSmem = size_t(kScoreStages) * kScoreRows * kScoreRowStride * sizeof(float);
@@ -143,6 +143,29 @@ __device__ __forceinline__ int upper_segment(const int* offs, int n, int x) {
     if (__ldg(offs + mid) <= x) lo = mid; else hi = mid - 1;
   }
   return lo;
+}
+
+// ------------------------------------------------------------------ summary layout
+//
+// Page summaries are stored chunk-major inside groups of 128 pages:
+//   element e of page p lives at ((p/128 * NC + e/CW) * 128 + p%128) * CW + e%CW
+// with CW = min(64, largest power of two dividing H*D) and NC = H*D / CW.
+// A score tile of consecutive page ids then reads, per stage, one contiguous
+// run of 128 * CW floats instead of 128 scattered row pieces.
+__host__ __device__ __forceinline__ int summary_chunk(int ept) {
+  const int low = ept & -ept;
+  return low < 64 ? low : 64;
+}
+__host__ __device__ __forceinline__ size_t summary_group_floats(int ept) {
+  return size_t(128) * ept;
+}
+// offset of (page, chunk 0, element 0); chunk c adds c * 128 * CW
+__host__ __device__ __forceinline__ size_t summary_row_base(int page, int ept) {
+  return size_t(page >> 7) * summary_group_floats(ept) + size_t(page & 127) * summary_chunk(ept);
+}
+__host__ __device__ __forceinline__ size_t summary_off(int page, int e, int ept) {
+  const int cw = summary_chunk(ept);
+  return summary_row_base(page, ept) + size_t(e / cw) * 128 * cw + (e % cw);
 }
 
 // ------------------------------------------------------------------ plan
@@ -284,7 +307,7 @@ __device__ __forceinline__ void cp_async_wait() {
 // instruction); row kScoreTile of every stage holds the query chunk.
 // Thread t always copies rows t/kCols + kRowStep*j, column t%kCols, so it
 // keeps the page offsets of the tile it is loading in registers.
-__global__ void __launch_bounds__(kScoreThreads, 1) score_kernel(
+__global__ void __launch_bounds__(kScoreThreads, 2) score_kernel(
     StepPlan plan, const float* __restrict__ queries, const float* __restrict__ summaries,
     int ept, float scale, float* __restrict__ scores) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -300,7 +323,9 @@ __global__ void __launch_bounds__(kScoreThreads, 1) score_kernel(
   const int* ids_src = mode == 0 ? plan.cand_ids : plan.table;
   const int total_tiles = plan.tile_off[B];
   const int ts = plan.misc[1];
-  const int nchunks = (ept + kScoreChunk - 1) / kScoreChunk;
+  const int cw = summary_chunk(ept);          // floats of a page's summary per stage
+  const int nchunks = ept / cw;
+  const size_t chunk_stride = size_t(128) * cw;
   const int col = tid % kCols;
   const int row0 = tid / kCols;
 
@@ -318,22 +343,23 @@ __global__ void __launch_bounds__(kScoreThreads, 1) score_kernel(
 #pragma unroll
     for (int j = 0; j < kRowsPerThread; ++j) {
       const int row = row0 + kRowStep * j;
-      ld_off[j] = row < ld_nvalid ? size_t(__ldg(ids + row)) * ept : 0;
+      ld_off[j] = row < ld_nvalid ? summary_row_base(__ldg(ids + row), ept) : 0;
     }
   };
   auto issue = [&]() {
     if (ld_tile < total_tiles) {
-      const int len = min(kScoreChunk, ept - ld_ch * kScoreChunk);
+      const int len = cw;
       float* st = stage_base + size_t(ld_slot) * kStageFloats;
       if (col * 4 < len) {
-        const size_t coff = size_t(ld_ch) * kScoreChunk + col * 4;
+        const size_t coff = size_t(ld_ch) * chunk_stride + col * 4;
+        const size_t qoff = size_t(ld_ch) * cw + col * 4;
 #pragma unroll
         for (int j = 0; j < kRowsPerThread; ++j) {
           const int row = row0 + kRowStep * j;
           if (row < ld_nvalid) {
             cp_async16(st + row * kScoreRowStride + col * 4, summaries + ld_off[j] + coff);
           } else if (row == kScoreTile) {
-            cp_async16(st + row * kScoreRowStride + col * 4, ld_q + coff);
+            cp_async16(st + row * kScoreRowStride + col * 4, ld_q + qoff);
           }
         }
       }
@@ -361,7 +387,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1) score_kernel(
       cp_async_wait<kScoreStages - 2>();
       __syncthreads();   // chunk `slot` landed for all threads; slot-1 is free again
       issue();
-      const int len = min(kScoreChunk, ept - ch * kScoreChunk);
+      const int len = cw;
       const float* st = stage_base + size_t(slot) * kStageFloats;
       if (tid < nvalid) {
         const float4* srow = reinterpret_cast<const float4*>(st + tid * kScoreRowStride);
@@ -833,7 +859,7 @@ __global__ void upload_pages_kernel(const int* __restrict__ page_ids,
       out = make_float4(__fmul_rn(sum.x, inv), __fmul_rn(sum.y, inv), __fmul_rn(sum.z, inv),
                         __fmul_rn(sum.w, inv));
     }
-    reinterpret_cast<float4*>(summaries + size_t(page) * ept)[j] = out;
+    *reinterpret_cast<float4*>(summaries + summary_off(page, 4 * j, ept)) = out;
   }
   if (blockIdx.y == 0 && threadIdx.x == 0) {
     token_counts[page] = n;
@@ -847,7 +873,7 @@ __global__ void set_summaries_kernel(const int* __restrict__ page_ids,
   const int i = blockIdx.x;
   const int page = page_ids[i];
   for (int e = threadIdx.x; e < ept; e += blockDim.x)
-    summaries[size_t(page) * ept + e] = staged[size_t(i) * ept + e];
+    summaries[summary_off(page, e, ept)] = staged[size_t(i) * ept + e];
 }
 
 // Token append.  One block per distinct page; its tokens (token_first[i] ..
@@ -864,7 +890,8 @@ __global__ void append_tokens_kernel(const int* __restrict__ group_page,
                                      uint8_t* __restrict__ live) {
   const int gidx = blockIdx.x;
   const int page = group_page[gidx];
-  float* summ = summaries + size_t(page) * ept;
+  const size_t sbase = summary_row_base(page, ept);
+  const int scw = summary_chunk(ept);
   int last = -1;
   for (int i = token_first[gidx]; i < token_first[gidx + 1]; ++i) {
     const int off = token_offset[i];
@@ -876,8 +903,9 @@ __global__ void append_tokens_kernel(const int* __restrict__ group_page,
       const float k = staged_k[size_t(i) * ept + e];
       dk[e] = k;
       dv[e] = staged_v[size_t(i) * ept + e];
-      const float s = off == 0 ? 0.0f : summ[e];
-      summ[e] = __fdiv_rn(__fadd_rn(__fmul_rn(s, old_c), k), new_c);
+      float& slot = summaries[sbase + size_t(e / scw) * 128 * scw + (e % scw)];
+      const float s = off == 0 ? 0.0f : slot;
+      slot = __fdiv_rn(__fadd_rn(__fmul_rn(s, old_c), k), new_c);
     }
     last = max(last, off);
   }
@@ -908,7 +936,7 @@ __global__ void free_pages_kernel(const int* __restrict__ page_ids, int ept,
                                   float* __restrict__ summaries, int* __restrict__ token_counts,
                                   uint8_t* __restrict__ live) {
   const int page = page_ids[blockIdx.x];
-  for (int e = threadIdx.x; e < ept; e += blockDim.x) summaries[size_t(page) * ept + e] = 0.0f;
+  for (int e = threadIdx.x; e < ept; e += blockDim.x) summaries[summary_off(page, e, ept)] = 0.0f;
   if (threadIdx.x == 0) {
     token_counts[page] = 0;
     live[page] = 0;
@@ -968,7 +996,7 @@ __global__ void prefill_synthetic_kernel(const int* __restrict__ page_ids,
       value_pool[(size_t(page) * page_size + t) * ept + e] = v;
       sum = __fadd_rn(sum, k);
     }
-    summaries[size_t(page) * ept + e] =
+    summaries[summary_off(page, e, ept)] =
         n > 0 ? __fmul_rn(sum, __fdiv_rn(1.0f, static_cast<float>(n))) : 0.0f;
   }
   if (threadIdx.x == 0) {
@@ -989,7 +1017,8 @@ __global__ void append_synthetic_kernel(const int* __restrict__ group_page,
                                         uint8_t* __restrict__ live) {
   const int gidx = blockIdx.x;
   const int page = group_page[gidx];
-  float* summ = summaries + size_t(page) * ept;
+  const size_t sbase = summary_row_base(page, ept);
+  const int scw = summary_chunk(ept);
   int last = -1;
   for (int i = token_first[gidx]; i < token_first[gidx + 1]; ++i) {
     const int off = token_offset[i];
@@ -999,8 +1028,9 @@ __global__ void append_synthetic_kernel(const int* __restrict__ group_page,
       const float k = decode_value(reqs[i], steps[i], e, 1);
       key_pool[(size_t(page) * page_size + off) * ept + e] = k;
       value_pool[(size_t(page) * page_size + off) * ept + e] = decode_value(reqs[i], steps[i], e, 2);
-      const float s = off == 0 ? 0.0f : summ[e];
-      summ[e] = __fdiv_rn(__fadd_rn(__fmul_rn(s, old_c), k), new_c);
+      float& slot = summaries[sbase + size_t(e / scw) * 128 * scw + (e % scw)];
+      const float s = off == 0 ? 0.0f : slot;
+      slot = __fdiv_rn(__fadd_rn(__fmul_rn(s, old_c), k), new_c);
     }
     last = max(last, off);
   }
@@ -1061,7 +1091,7 @@ __global__ void generate_normal_kernel(const int* __restrict__ page_ids,
       value_pool[(size_t(page) * page_size + t) * ept + e] = normal_value(vmix, idx);
       sum = __fadd_rn(sum, k);
     }
-    summaries[size_t(page) * ept + e] =
+    summaries[summary_off(page, e, ept)] =
         n > 0 ? __fmul_rn(sum, __fdiv_rn(1.0f, static_cast<float>(n))) : 0.0f;
   }
   if (blockIdx.y == 0 && threadIdx.x == 0) {

@@ -1,6 +1,7 @@
 // GPU-resident page pool (drop-in for include/dsd/device_page_pool.h:17-140)
 // over the C ABI (include/dsd_b200.h).  Layout in HBM: page-major K and V
-// [capacity][page_size][H*D] fp32, summaries [capacity][H*D], token counts,
+// [capacity][page_size][H*D] fp32, summaries chunk-major in 128-page groups
+// (see include/dsd_b200.h), token counts,
 // live flags.  Page offsets are derived (page * page_size * H*D), so the
 // reference's per-page offset tables do not exist: page_k/v_offsets_device()
 // return nullptr.

@@ -14,7 +14,9 @@
  *
  * Data layout in HBM (one context = one GPU):
  *   keys, values  float [capacity_pages][page_size][H*D]   page-major, 16 B aligned rows
- *   summaries     float [capacity_pages][H*D]              mean key of the page
+ *   summaries     mean key of each page, chunk-major in groups of 128 pages:
+ *                 element e of page p at ((p/128*NC + e/CW)*128 + p%128)*CW + e%CW,
+ *                 CW = min(64, largest power of two dividing H*D), NC = H*D/CW
  *   token_counts  int32 [capacity_pages]; live  uint8 [capacity_pages]
  *   request page tables int32 [max_requests][max_pages_per_request] (+ counts)
  */
@@ -218,9 +220,10 @@ int dsd_kernels_per_step(void);
  * pages (sum of min(k, n_r)) <= 8192, num_heads*head_dim <= 4096, top_k <= 4096;
  * larger sizes are rejected with DSD_EINVAL.
  *   cand_offsets  HOST array [batch+1] (validated here, copied to the device)
- *   d_cand_ids, d_queries [batch][H*D], d_summaries [cap][H*D],
+ *   d_cand_ids, d_queries [batch][H*D], d_summaries (pool summary layout),
  *   d_keys/d_values [cap][page_size][H*D], d_token_counts [cap], d_outputs
- *   [batch][H*D]: device pointers, float arrays 16-byte aligned.
+ *   [batch][H*D]: device pointers, float arrays 16-byte aligned; d_summaries in the
+ *   pool's summary layout above (e.g. the pointer dsd_ctx_device_pointers returns).
  * Page ids are not range-checked (they live on the device).  Work is queued on
  * `stream` (a cudaStream_t, NULL = default stream) and the call waits for it.
  * The first call on a device looks up the array's device address and sets
