@@ -284,8 +284,8 @@ void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool cap
       plan, d_q, c->summaries, c->ept, c->scale, c->d_scores);
   if (timed) RecordEvent(c, 1, capturing);
   const int sel_grid = std::max(1, std::min(c->opt.max_batch, 2 * c->num_sms));
-  dsdk::select_kernel<<<sel_grid, dsdk::kSelectThreads, 0, c->stream>>>(plan, c->d_scores,
-                                                                         c->d_selected);
+  dsdk::select_kernel<<<sel_grid, dsdk::kSelectThreads, dsdk::kSelectSmem, c->stream>>>(
+      plan, c->d_scores, c->d_selected);
   if (timed) RecordEvent(c, 2, capturing);
   const int H = c->cfg.num_heads, D = c->cfg.head_dim, P = c->cfg.page_size;
   LaunchAttn(c->attn, c->num_sms, c->stream, plan, d_q, c->k_pool, c->v_pool, c->token_counts,
@@ -573,6 +573,8 @@ int dsd_ctx_create(int device, const dsd_model_config* config, const dsd_ctx_opt
       Check(cudaFuncSetAttribute(dsdk::score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)dsdk::kScoreSmem), "smem attribute");
       SetAllAttnAttributes(c->attn.smem);
+      Check(cudaFuncSetAttribute(dsdk::select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 int(dsdk::kSelectSmem)), "smem attribute");
       Sync(c);
     } catch (...) {
       dsd_ctx_destroy(c);
@@ -1199,6 +1201,8 @@ NaDevice& NaSetup(int device) {
   const size_t max_attn = size_t(dsdk::kAttnStages) * dsdk::kAttnStageFloats * 4 +
                           dsdk::kAttnStages * 8;
   SetAllAttnAttributes(max_attn);
+  Check(cudaFuncSetAttribute(dsdk::select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(dsdk::kSelectSmem)), "smem attribute");
   d.scratch = static_cast<int*>(p);
   d.ready = true;
   return d;
@@ -1276,8 +1280,8 @@ extern "C" int dsd_decode_batch_noalloc(int device, const dsd_model_config* conf
     dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, s>>>(plan, cfg.top_k_pages, target, 2 * nd.num_sms);
     dsdk::score_kernel<<<2 * nd.num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, s>>>(
         plan, d_queries, d_summaries, ept, scale, scores);
-    dsdk::select_kernel<<<std::min(batch, 2 * nd.num_sms), dsdk::kSelectThreads, 0, s>>>(
-        plan, scores, selected);
+    dsdk::select_kernel<<<std::min(batch, 2 * nd.num_sms), dsdk::kSelectThreads,
+                          dsdk::kSelectSmem, s>>>(plan, scores, selected);
     const AttnShape ash = MakeAttnShape(cfg.num_heads, D, cfg.page_size);
     LaunchAttn(ash, nd.num_sms, s, plan, d_queries, d_keys, d_values, d_token_counts, selected,
                part_acc, part_ml, cfg.num_heads, D, cfg.page_size, scale);

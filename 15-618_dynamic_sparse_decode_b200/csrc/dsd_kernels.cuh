@@ -47,6 +47,8 @@ constexpr int kAttnMaxTokensPerStage = 8;           // logits held in registers 
 
 constexpr int kSelectThreads = 512;
 constexpr int kSelectMaxK = 4096;                   // selected pages per request
+constexpr int kSelectSmemKeys = 8192;               // candidates staged in shared memory
+constexpr size_t kSelectSmem = size_t(kSelectMaxK + kSelectSmemKeys) * 8;   // 96 KiB
 
 // status bits written by kernels (read by the host after the step)
 constexpr int kStatusTimeout = 1;
@@ -432,16 +434,23 @@ __device__ __forceinline__ unsigned long long page_key(float score, int page) {
   return (static_cast<unsigned long long>(b) << 32) | static_cast<uint32_t>(~page);
 }
 
-// One CTA per request (grid-stride).  Radix select (8 passes of 8 bits, MSB
-// first) finds the k-th largest key; the k winners are gathered into shared
-// memory, bitonic-sorted descending and written as page ids.
+// One CTA per request (grid-stride).  The request's candidate keys are
+// staged in shared memory (when n <= kSelectSmemKeys; otherwise every pass
+// re-reads them from global memory).  A radix select, 8 bits per pass from
+// the most significant byte, narrows the prefix of the k-th largest key and
+// stops as soon as every key sharing the prefix is a winner.  Keys above the
+// threshold (then the ones equal to it, for duplicated ids) are gathered,
+// bitonic-sorted descending and written as page ids.
 __global__ void __launch_bounds__(kSelectThreads) select_kernel(StepPlan plan,
                                                                 const float* __restrict__ scores,
                                                                 int* __restrict__ selected) {
-  __shared__ unsigned long long keys[kSelectMaxK];
+  extern __shared__ __align__(16) unsigned long long sel_smem[];
+  unsigned long long* keys = sel_smem;                      // winners [kSelectMaxK]
+  unsigned long long* all = sel_smem + kSelectMaxK;         // candidates [kSelectSmemKeys]
   __shared__ int hist[256];
   __shared__ unsigned long long s_prefix;
   __shared__ int s_remaining;
+  __shared__ int s_done;
   __shared__ int s_count_gt;
   __shared__ int s_count_eq;
 
@@ -460,11 +469,17 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(StepPlan plan,
     }
     const float* sc = scores + plan.score_off[r];
     const int* ids = ids_src + plan.id_base[r];
+    const bool staged = n <= kSelectSmemKeys;
+    if (staged) {
+      for (int i = tid; i < n; i += blockDim.x) all[i] = page_key(sc[i], __ldg(ids + i));
+    }
+    auto key_at = [&](int i) -> unsigned long long {
+      return staged ? all[i] : page_key(sc[i], __ldg(ids + i));
+    };
 
-    unsigned long long threshold = 0;  // keys >= threshold are candidates for selection
+    unsigned long long threshold = 0;  // keys >= threshold are the winners
     if (k < n) {
-      // ---- radix select of the k-th largest key
-      if (tid == 0) { s_prefix = 0; s_remaining = k; }
+      if (tid == 0) { s_prefix = 0; s_remaining = k; s_done = 0; }
       unsigned long long mask = 0;
       for (int pass = 0; pass < 8; ++pass) {
         const int shift = 56 - 8 * pass;
@@ -472,12 +487,12 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(StepPlan plan,
         __syncthreads();
         const unsigned long long prefix = s_prefix;
         for (int i = tid; i < n; i += blockDim.x) {
-          const unsigned long long key = page_key(sc[i], __ldg(ids + i));
+          const unsigned long long key = key_at(i);
           if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xff], 1);
         }
         __syncthreads();
         if (tid < 32) {
-          // find the digit (from 255 down) where the cumulative count reaches `remaining`
+          // the digit (from 255 down) where the cumulative count reaches `remaining`
           const int rem = s_remaining;
           int cnt[8];
           int local = 0;
@@ -501,6 +516,9 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(StepPlan plan,
                 const int digit = 255 - (tid * 8 + j);
                 s_prefix = prefix | (static_cast<unsigned long long>(digit) << shift);
                 s_remaining = rem - acc;
+                // every key with this prefix is a winner: the prefix itself
+                // (lower bits zero) is a valid threshold
+                if (acc + cnt[j] == rem) s_done = 1;
                 break;
               }
               acc += cnt[j];
@@ -509,15 +527,16 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(StepPlan plan,
         }
         __syncthreads();
         mask |= 0xffULL << shift;
+        if (s_done) break;
       }
-      threshold = s_prefix;  // the exact k-th largest key
+      threshold = s_prefix;
     }
 
     // ---- gather keys > threshold, then fill with keys == threshold
     if (tid == 0) { s_count_gt = 0; s_count_eq = 0; }
     __syncthreads();
     for (int i = tid; i < n; i += blockDim.x) {
-      const unsigned long long key = page_key(sc[i], __ldg(ids + i));
+      const unsigned long long key = key_at(i);
       if (key > threshold || k == n) {
         const int pos = atomicAdd(&s_count_gt, 1);
         if (pos < k) keys[pos] = key;
@@ -527,7 +546,7 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(StepPlan plan,
     const int gt = min(s_count_gt, k);
     if (gt < k) {
       for (int i = tid; i < n; i += blockDim.x) {
-        const unsigned long long key = page_key(sc[i], __ldg(ids + i));
+        const unsigned long long key = key_at(i);
         if (key == threshold) {
           const int pos = gt + atomicAdd(&s_count_eq, 1);
           if (pos < k) keys[pos] = key;
