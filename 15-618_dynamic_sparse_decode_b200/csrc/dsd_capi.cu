@@ -12,6 +12,7 @@
 #include <cstdint>
 #include <cstring>
 #include <mutex>
+#include <thread>
 #include <stdexcept>
 #include <string>
 #include <unordered_map>
@@ -193,6 +194,15 @@ struct dsd_ctx {
   unsigned char* d_stage = nullptr;
   size_t d_stage_bytes = 0;
 
+  // bulk host->device uploads: per worker two pinned chunks, a copy stream
+  // and an event per chunk (created on first large pageable upload)
+  struct Uploader {
+    cudaStream_t stream = nullptr;
+    unsigned char* pinned[2] = {nullptr, nullptr};
+    cudaEvent_t done[2] = {nullptr, nullptr};
+  };
+  std::vector<Uploader> uploaders;
+
   // bound (device-resident) steps
   int bound_batch = -1;
   // captured steps, keyed by (queries, outputs, timed); the plan inside a
@@ -246,6 +256,77 @@ void EnsureStage(dsd_ctx* c, size_t bytes) {
   c->d_stage_bytes = 0;
   c->d_stage = DeviceAlloc<unsigned char>(bytes, "staging buffer");
   c->d_stage_bytes = bytes;
+}
+
+bool IsPinnedHost(const void* p);
+bool IsPinnedHostPtr(const void* p) { return IsPinnedHost(p); }
+
+constexpr size_t kUploadChunk = size_t(16) << 20;   // bytes per pinned chunk
+constexpr int kUploadWorkers = 4;
+
+// Host -> device copy of a large pageable buffer: kUploadWorkers threads each
+// copy 16 MiB chunks into their two pinned buffers and DMA them on their own
+// stream, so host copies and PCIe transfers overlap.  The context stream
+// then waits for every worker stream.  Pinned or small sources go directly.
+void BulkH2D(dsd_ctx* c, void* dst, const void* src, size_t bytes) {
+  if (bytes == 0) return;
+  if (bytes < 2 * kUploadChunk || IsPinnedHostPtr(src)) {
+    H2D(c, dst, src, bytes);
+    return;
+  }
+  if (c->uploaders.empty()) {
+    c->uploaders.resize(kUploadWorkers);
+    for (auto& u : c->uploaders) {
+      Check(cudaStreamCreateWithFlags(&u.stream, cudaStreamNonBlocking), "upload stream");
+      for (int b = 0; b < 2; ++b) {
+        u.pinned[b] = PinnedAlloc<unsigned char>(kUploadChunk, "upload staging");
+        Check(cudaEventCreateWithFlags(&u.done[b], cudaEventDisableTiming), "upload event");
+      }
+    }
+  }
+  // the destination may still be read by earlier work on the context stream
+  cudaEvent_t ready;
+  Check(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming), "event");
+  Check(cudaEventRecord(ready, c->stream), "event record");
+  const size_t nchunks = (bytes + kUploadChunk - 1) / kUploadChunk;
+  std::vector<std::string> errors(c->uploaders.size());
+  std::vector<std::thread> pool;
+  for (size_t w = 0; w < c->uploaders.size(); ++w) {
+    pool.emplace_back([&, w]() {
+      auto& u = c->uploaders[w];
+      if (cudaSetDevice(c->device) != cudaSuccess ||
+          cudaStreamWaitEvent(u.stream, ready, 0) != cudaSuccess) {
+        errors[w] = "upload worker setup failed";
+        return;
+      }
+      int b = 0;
+      for (size_t i = w; i < nchunks; i += c->uploaders.size(), b ^= 1) {
+        const size_t off = i * kUploadChunk;
+        const size_t len = std::min(kUploadChunk, bytes - off);
+        if (cudaEventSynchronize(u.done[b]) != cudaSuccess) {
+          errors[w] = "upload event wait failed";
+          return;
+        }
+        std::memcpy(u.pinned[b], static_cast<const unsigned char*>(src) + off, len);
+        if (cudaMemcpyAsync(static_cast<unsigned char*>(dst) + off, u.pinned[b], len,
+                            cudaMemcpyHostToDevice, u.stream) != cudaSuccess ||
+            cudaEventRecord(u.done[b], u.stream) != cudaSuccess) {
+          errors[w] = "upload copy failed";
+          return;
+        }
+      }
+    });
+  }
+  for (auto& t : pool) t.join();
+  cudaEventDestroy(ready);
+  for (const auto& e : errors)
+    if (!e.empty()) Fail(DSD_ECUDA, e);
+  for (auto& u : c->uploaders)
+    for (int b = 0; b < 2; ++b)
+      Check(cudaStreamWaitEvent(c->stream, u.done[b], 0), "upload join");
+  c->stats.h2d_bytes += bytes;
+  c->stats.h2d_calls += nchunks;
+  c->stats.h2d_large_calls += nchunks;
 }
 
 void ValidatePage(const dsd_ctx* c, int page) {
@@ -592,6 +673,14 @@ int dsd_ctx_destroy(dsd_ctx* c) {
     if (g.exec) cudaGraphExecDestroy(g.exec);
     if (g.graph) cudaGraphDestroy(g.graph);
   }
+  for (auto& u : c->uploaders) {
+    if (u.stream) cudaStreamSynchronize(u.stream);
+    for (int b = 0; b < 2; ++b) {
+      if (u.pinned[b]) cudaFreeHost(u.pinned[b]);
+      if (u.done[b]) cudaEventDestroy(u.done[b]);
+    }
+    if (u.stream) cudaStreamDestroy(u.stream);
+  }
   void* dev[] = {c->k_pool, c->v_pool, c->summaries, c->token_counts, c->live, c->table,
                  c->table_n, c->d_in, c->d_scores, c->d_selected, c->d_outputs, c->d_part_acc,
                  c->d_part_ml, c->d_planbuf, c->d_status, c->d_stage};
@@ -694,8 +783,8 @@ int dsd_pool_upload_pages(dsd_ctx* c, const int32_t* page_ids, const int32_t* to
       }
       const size_t meta_bytes = meta.size() * sizeof(long long);
       EnsureStage(c, meta_off + meta_bytes);
-      H2D(c, c->d_stage, keys + tok0 * c->ept, payload);
-      H2D(c, c->d_stage + payload, values + tok0 * c->ept, payload);
+      BulkH2D(c, c->d_stage, keys + tok0 * c->ept, payload);
+      BulkH2D(c, c->d_stage + payload, values + tok0 * c->ept, payload);
       H2D(c, c->d_stage + meta_off, meta.data(), meta_bytes);
       const long long* d_off = reinterpret_cast<const long long*>(c->d_stage + meta_off);
       const int* d_ids = reinterpret_cast<const int*>(d_off + np);
