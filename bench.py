@@ -352,7 +352,7 @@ CONTINUOUS = {
                     desc="config4: 128 req, max_active 32/GPU, arrival [0,64], prompt 1024-4096, "
                          "decode 16-64, H32 D128 P16 k8, direct GPU upload, preadmit, "
                          "precompute, GPU synthetic append, lazy release",
-                    published=36236.393529),
+                    published=36236.393529, repeats=5),
     # box-scale serving, synthetic GPU prefill and append
     "config5": dict(argv=[2048, 128, 512, 8192, 32768, 64, 256, 11, 32, 128, 32, 32, 2, 0, 0, 1, 0, 1, 0, 0, 1, 1],
                     desc="config5: 2048 req, max_active 128/GPU, arrival [0,512], prompt 8192-32768, "
@@ -371,7 +371,7 @@ def run_continuous(args):
         dist.barrier()
     spec = CONTINUOUS[args.workload]
     exe = os.path.join(ROOT, "15-618_dynamic_sparse_decode_b200", "bin", "dsd_continuous_bench")
-    argv = [str(x) for x in spec["argv"]] + [str(world), str(rank)]
+    argv = [str(x) for x in spec["argv"]] + [str(world), str(rank), str(spec.get("repeats", 1))]
     env = dict(os.environ, CUDA_VISIBLE_DEVICES=str(local))
     out = subprocess.run([exe, *argv], capture_output=True, text=True, env=env)
     if out.returncode != 0:
