@@ -93,6 +93,7 @@ SIGNATURES = [
     ("dsd_decode_bound_timed", ctypes.c_int, [_VP, _VP, _VP, ctypes.POINTER(StepTiming)]),
     ("dsd_read_step_timing", ctypes.c_int, [_VP, ctypes.POINTER(StepTiming)]),
     ("dsd_kernels_per_step", ctypes.c_int, []),
+    ("dsd_selftest_bounded_wait", ctypes.c_int, [_VP, ctypes.c_int64]),
     ("dsd_decode_batch_noalloc", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ModelConfig),
                                                 ctypes.c_int, _I32P, _VP, _VP, _VP, _VP, _VP,
                                                 _VP, _VP, _VP]),

@@ -550,6 +550,18 @@ int dsd_available(void) {
 
 int dsd_kernels_per_step(void) { return 5; }
 
+int dsd_selftest_bounded_wait(dsd_ctx* c, int64_t budget_cycles) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    if (budget_cycles <= 0 || budget_cycles > (int64_t(1) << 32))
+      Fail(DSD_EINVAL, "budget must be in (0, 2^32] cycles");
+    SetDevice(c);
+    dsdk::bounded_wait_probe_kernel<<<1, 32, 0, c->stream>>>(c->d_status, budget_cycles);
+    Check(cudaGetLastError(), "probe launch");
+    CheckStatus(c);  // DSD_ETIMEOUT when the wait gave up, as it must
+  });
+}
+
 int dsd_ctx_create(int device, const dsd_model_config* config, const dsd_ctx_options* options,
                    dsd_ctx** out) {
   return Guard([&]() {

@@ -115,16 +115,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Waits for the barrier phase with a cycle budget; on expiry sets the
 // timeout bit in *status and returns false (the caller then stops issuing work).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status,
+                                          long long budget = kWaitBudgetCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long start = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - start > kWaitBudgetCycles) {
+    if (clock64() - start > budget) {
       atomicOr(status, kStatusTimeout);
       return false;
     }
   }
   return true;
+}
+
+// Self-test of the bounded wait: one thread waits on a barrier phase that
+// nothing completes (no copy is issued, no thread arrives) with a small
+// budget.  The wait gives up, sets the timeout bit and the kernel returns.
+__global__ void bounded_wait_probe_kernel(int* status, long long budget) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    mbar_wait(&bar, 0, status, budget);
+  }
 }
 
 // 1-D bulk copy global -> shared (TMA), completion counted on `bar` in bytes.

@@ -208,6 +208,12 @@ int dsd_read_step_timing(dsd_ctx* ctx, dsd_step_timing* out_timing);
 /* Number of kernels one decode step launches (for launch accounting). */
 int dsd_kernels_per_step(void);
 
+/* Failure-detection self-test: launches a kernel whose single wait (on a
+ * shared-memory barrier that nothing completes) uses the same bounded-wait
+ * routine as the decode kernels, with `budget_cycles` instead of ~2^31.
+ * Returns DSD_ETIMEOUT after the wait gives up; the context stays usable. */
+int dsd_selftest_bounded_wait(dsd_ctx* ctx, int64_t budget_cycles);
+
 /* Allocation-free decode step.  No counterpart in the reference: it exists
  * for callers that must not allocate device memory at all -- code running
  * under a host framework that owns every allocation (a custom caching

@@ -394,4 +394,44 @@ void orc_normal_fill(std::uint64_t seed, int kind, std::uint64_t first_index, lo
     out[i] = orc_normal_value(seed, kind, first_index + static_cast<std::uint64_t>(i));
 }
 
+// SyntheticPromptValue / SyntheticDecodeValue of the reference's GPU
+// admission mode 2 (src/device_page_pool.cpp:102-138): boost-style hash
+// combine of the indices, 32-bit finaliser, (x % 2001 - 1000) / 1000.
+static std::uint32_t HashCombine(std::uint32_t x, int v, std::uint32_t salt) {
+  return x ^ (static_cast<std::uint32_t>(v + static_cast<int>(salt)) + (x << 6) + (x >> 2));
+}
+static float HashUnit(std::uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return static_cast<float>(static_cast<int>(x % 2001u) - 1000) / 1000.0f;
+}
+
+// tokens [0, n) of prompt page `page_idx` of `request`, stream 1 = key, 2 = value
+void orc_synthetic_prompt_fill(int request, int page_idx, int n, int ept, int stream, float* out) {
+  for (int t = 0; t < n; ++t)
+    for (int e = 0; e < ept; ++e) {
+      std::uint32_t x = 0x9e3779b9u;
+      x = HashCombine(x, request, 0x85ebca6bu);
+      x = HashCombine(x, page_idx, 0xc2b2ae35u);
+      x = HashCombine(x, t, 0x27d4eb2fu);
+      x = HashCombine(x, e, 0x165667b1u);
+      x = HashCombine(x, stream, 0xd3a2646cu);
+      out[static_cast<long long>(t) * ept + e] = HashUnit(x);
+    }
+}
+
+void orc_synthetic_decode_fill(int request, int step, int ept, int stream, float* out) {
+  for (int e = 0; e < ept; ++e) {
+    std::uint32_t x = 0x9e3779b9u;
+    x = HashCombine(x, request, 0x85ebca6bu);
+    x = HashCombine(x, step, 0xc2b2ae35u);
+    x = HashCombine(x, e, 0x165667b1u);
+    x = HashCombine(x, stream, 0xd3a2646cu);
+    out[e] = HashUnit(x);
+  }
+}
+
 }  // extern "C"

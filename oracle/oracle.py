@@ -60,6 +60,8 @@ def lib():
         L.orc_normal_value.restype = ctypes.c_float
         L.orc_normal_fill.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_uint64,
                                       ctypes.c_longlong, _F]
+        L.orc_synthetic_prompt_fill.argtypes = [ctypes.c_int] * 5 + [_F]
+        L.orc_synthetic_decode_fill.argtypes = [ctypes.c_int] * 4 + [_F]
         _lib = L
     return _lib
 
@@ -188,6 +190,18 @@ def running_mean_append(summary: np.ndarray, key: np.ndarray, old_count: int) ->
 def deterministic_token_vector(count, request_id, decode_step, stream) -> np.ndarray:
     out = np.zeros(count, np.float32)
     lib().orc_deterministic_token_vector(count, request_id, decode_step, stream, fp(out))
+    return out
+
+
+def synthetic_prompt(request, page_idx, n, ept, stream) -> np.ndarray:
+    out = np.zeros((n, ept), np.float32)
+    lib().orc_synthetic_prompt_fill(request, page_idx, n, ept, stream, fp(out))
+    return out
+
+
+def synthetic_decode(request, step, ept, stream) -> np.ndarray:
+    out = np.zeros(ept, np.float32)
+    lib().orc_synthetic_decode_fill(request, step, ept, stream, fp(out))
     return out
 
 
