@@ -88,6 +88,9 @@ SIGNATURES = [
     ("dsd_decode_step", ctypes.c_int, [_VP, _I32P, ctypes.c_int, _F32P, ctypes.c_int,
                                        ctypes.c_int, _F32P, _F32P, _I32P,
                                        ctypes.POINTER(StepTiming)]),
+    ("dsd_decode_step_begin", ctypes.c_int, [_VP, _I32P, ctypes.c_int, _F32P, ctypes.c_int,
+                                             ctypes.c_int]),
+    ("dsd_decode_step_end", ctypes.c_int, [_VP, _F32P, _F32P, _I32P, ctypes.POINTER(StepTiming)]),
     ("dsd_bind_requests", ctypes.c_int, [_VP, _I32P, ctypes.c_int]),
     ("dsd_decode_bound", ctypes.c_int, [_VP, _VP, _VP]),
     ("dsd_decode_bound_timed", ctypes.c_int, [_VP, _VP, _VP, ctypes.POINTER(StepTiming)]),
@@ -350,6 +353,20 @@ class SparseDecodeContext:
                     scores=None if scores is None else scores[: int(n.sum())],
                     selected=None if sel is None else sel[:total_sel],
                     timing={n_: getattr(t, n_) for n_, _ in StepTiming._fields_})
+
+    def decode_step_begin(self, request_ids, queries, output_mode=OUTPUT_OUTPUTS):
+        req, q = _i32(request_ids), _f32(queries)
+        self._pending = (len(req), output_mode,
+                         np.array([self.request_num_pages(int(r)) for r in req]))
+        _check(self.lib.dsd_decode_step_begin(self.h, _ip(req), len(req), _fp(q), output_mode, 0))
+
+    def decode_step_end(self):
+        B, mode, n = self._pending
+        total_sel = int(np.minimum(n, self.cfg.top_k_pages).sum())
+        out, scores, sel = self._results(B, int(n.sum()), total_sel, mode)
+        _check(self.lib.dsd_decode_step_end(self.h, _fp(out), _fp(scores), _ip(sel), None))
+        return dict(outputs=out, scores=None if scores is None else scores[: int(n.sum())],
+                    selected=None if sel is None else sel[:total_sel])
 
     def bind_requests(self, request_ids):
         req = _i32(request_ids)

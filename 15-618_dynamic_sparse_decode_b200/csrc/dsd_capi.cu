@@ -218,6 +218,12 @@ struct dsd_ctx {
   std::vector<StepGraph> graphs;
 
   dsd_transfer_stats stats{};
+
+  // a step queued by dsd_decode_step_begin, finished by dsd_decode_step_end
+  struct PendingStep {
+    bool active = false;
+    int batch = 0, total_cand = 0, total_sel = 0, output_mode = 0, timing = 0;
+  } pending;
 };
 
 namespace {
@@ -466,6 +472,48 @@ void RunHostStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int outpu
       std::memcpy(scores, c->h_scores, size_t(total_cand) * sizeof(float));
     if (selected && total_sel > 0)
       std::memcpy(selected, c->h_selected, size_t(total_sel) * sizeof(int));
+  }
+}
+
+// Queues the step and its result copies into the pinned staging; records
+// ev[4] when everything (status word included) has landed on the host.
+void EnqueueStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int output_mode,
+                 int timing) {
+  LaunchStepGraph(c, reinterpret_cast<const float*>(c->d_in + c->in_q_off), c->d_outputs,
+                  timing != 0);
+  if (output_mode != DSD_OUTPUT_NONE)
+    D2H(c, c->h_outputs, c->d_outputs, size_t(batch) * c->ept * sizeof(float));
+  if (output_mode == DSD_OUTPUT_DEBUG) {
+    if (total_cand > 0) D2H(c, c->h_scores, c->d_scores, size_t(total_cand) * sizeof(float));
+    if (total_sel > 0) D2H(c, c->h_selected, c->d_selected, size_t(total_sel) * sizeof(int));
+  }
+  Check(cudaMemcpyAsync(c->h_status, c->d_status, sizeof(int), cudaMemcpyDeviceToHost, c->stream),
+        "status read");
+  Check(cudaEventRecord(c->ev[4], c->stream), "event record");
+  c->pending = dsd_ctx::PendingStep{true, batch, total_cand, total_sel, output_mode, timing};
+}
+
+void FinishStep(dsd_ctx* c, float* outputs, float* scores, int32_t* selected,
+                dsd_step_timing* out_timing) {
+  if (!c->pending.active) Fail(DSD_EINVAL, "no decode step is pending");
+  const auto p = c->pending;
+  c->pending.active = false;
+  Check(cudaEventSynchronize(c->ev[4]), "step wait");
+  const int st = *c->h_status;
+  if (st != 0) {
+    Check(cudaMemsetAsync(c->d_status, 0, sizeof(int), c->stream), "status clear");
+    Sync(c);
+    if (st & dsdk::kStatusTimeout) Fail(DSD_ETIMEOUT, "a device-side wait exceeded its budget");
+    Fail(DSD_EINVAL, "device kernels rejected the step input (status " + std::to_string(st) + ")");
+  }
+  if (p.timing) ReadTiming(c, out_timing);
+  if (p.output_mode != DSD_OUTPUT_NONE && outputs && outputs != c->h_outputs)
+    std::memcpy(outputs, c->h_outputs, size_t(p.batch) * c->ept * sizeof(float));
+  if (p.output_mode == DSD_OUTPUT_DEBUG) {
+    if (scores && p.total_cand > 0)
+      std::memcpy(scores, c->h_scores, size_t(p.total_cand) * sizeof(float));
+    if (selected && p.total_sel > 0)
+      std::memcpy(selected, c->h_selected, size_t(p.total_sel) * sizeof(int));
   }
 }
 
@@ -1192,6 +1240,32 @@ int dsd_decode_step(dsd_ctx* c, const int32_t* request_ids, int batch, const flo
     PackSlots(c, request_ids, batch, &tc, &ts);
     UploadQueries(c, queries, batch);
     RunHostStep(c, batch, tc, ts, output_mode, timing, outputs, scores, selected, out_timing);
+  });
+}
+
+int dsd_decode_step_begin(dsd_ctx* c, const int32_t* request_ids, int batch,
+                          const float* queries, int output_mode, int timing) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    RequireTables(c);
+    if (c->pending.active) Fail(DSD_EINVAL, "a decode step is already pending");
+    if (batch <= 0) Fail(DSD_EINVAL, "empty batch");
+    if (!queries || !request_ids) Fail(DSD_EINVAL, "null step input");
+    SetDevice(c);
+    int tc = 0, ts = 0;
+    PackSlots(c, request_ids, batch, &tc, &ts);
+    UploadQueries(c, queries, batch);
+    EnqueueStep(c, batch, tc, ts, output_mode, timing);
+  });
+}
+
+int dsd_decode_step_end(dsd_ctx* c, float* outputs, float* scores, int32_t* selected,
+                        dsd_step_timing* out_timing) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    if (out_timing) *out_timing = dsd_step_timing{};
+    SetDevice(c);
+    FinishStep(c, outputs, scores, selected, out_timing);
   });
 }
 

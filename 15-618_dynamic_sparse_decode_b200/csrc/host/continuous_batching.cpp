@@ -341,12 +341,24 @@ ContinuousBatchStats RunContinuousSparseDecode(const ModelConfig& config,
     const auto s0 = Clock::now();
     batch.clear();
     for (const auto& a : active) batch.push_back(&a.state);
-    const auto out = tables ? ctx.RunStep(batch, run_opts) : ctx.RunBatch(batch, run_opts);
-    const double ms = Ms(s0, Clock::now());
-    stats.run_batch_wall_ms += ms;
-    step_ms.push_back(ms);
-    Add(&timings_sum, out.aggregate_timings);
-    Add(&overhead_sum, out.runtime_overheads);
+    // With device page tables the step is queued asynchronously: the host
+    // bookkeeping of this step's token appends (and their uploads, ordered
+    // after the step on the same stream) overlaps the GPU work.
+    SparseBatchCudaResult out;
+    if (tables) {
+      ctx.BeginStep(batch, run_opts);
+    } else {
+      out = ctx.RunBatch(batch, run_opts);
+    }
+    auto finish_step = [&]() {
+      if (tables) out = ctx.FinishStep();
+      const double ms = Ms(s0, Clock::now());
+      stats.run_batch_wall_ms += ms;
+      step_ms.push_back(ms);
+      Add(&timings_sum, out.aggregate_timings);
+      Add(&overhead_sum, out.runtime_overheads);
+    };
+    if (!tables) finish_step();
     ++nonempty;
     active_sum += static_cast<int>(active.size());
 
@@ -428,6 +440,7 @@ ContinuousBatchStats RunContinuousSparseDecode(const ModelConfig& config,
         for (const auto& np : new_pages) ctx.AppendRequestPages(np.first, {np.second});
     }
     stats.append_sync_ms += Ms(a0, Clock::now());
+    if (tables) finish_step();
 
     std::vector<PageId> released;
     active.erase(std::remove_if(active.begin(), active.end(),

@@ -73,6 +73,13 @@ class SparseCudaContext {
   SparseBatchCudaResult RunStep(const std::vector<const RequestState*>& requests,
                                 SparseRunBatchOptions options);
 
+  // RunStep split in two: BeginStep uploads the queries and queues the step;
+  // host work and further uploads on this context (appends, frees) may
+  // follow before FinishStep waits for the results.  `requests` must stay
+  // alive until FinishStep.
+  void BeginStep(const std::vector<const RequestState*>& requests, SparseRunBatchOptions options);
+  SparseBatchCudaResult FinishStep();
+
   void SyncPageFromCache(const PagedKvCache& cache, PageId page_id);
   void SyncPagesFromCache(const PagedKvCache& cache, const std::vector<PageId>& page_ids);
   void SyncPromptDirect(const PagedKvCache& cache, const std::vector<PageId>& page_ids,
@@ -120,6 +127,12 @@ class SparseCudaContext {
   float* host_outputs_ = nullptr;
   std::vector<int> offsets_, ids_, request_ids_, selected_;
   std::vector<float> scores_;
+  // pending BeginStep
+  std::vector<const RequestState*> pending_requests_;
+  std::vector<int> pending_sel_off_;
+  SparseRunBatchOptions pending_options_;
+  double pending_prep_ms_ = 0.0;
+  bool pending_ = false;
 };
 
 SparseDecodeResult SparseDecodeCuda(const PagedKvCache& cache, const RequestState& request,

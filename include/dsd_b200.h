@@ -192,6 +192,17 @@ int dsd_decode_step(dsd_ctx* ctx, const int32_t* request_ids, int batch, const f
                     int output_mode, int timing, float* outputs, float* scores,
                     int32_t* selected, dsd_step_timing* out_timing);
 
+/* The same step split in two, so the caller's host work overlaps the GPU:
+ * begin uploads the queries and queues the step and its result copies;
+ * end waits and returns the results (copied out of the context's pinned
+ * staging, see dsd_step_host_buffers).  Work the caller queues on this
+ * context between the two (token appends, frees) runs after the step on
+ * the GPU.  One step may be pending at a time. */
+int dsd_decode_step_begin(dsd_ctx* ctx, const int32_t* request_ids, int batch,
+                          const float* queries, int output_mode, int timing);
+int dsd_decode_step_end(dsd_ctx* ctx, float* outputs, float* scores, int32_t* selected,
+                        dsd_step_timing* out_timing);
+
 /* Device-resident variant: bind a request set once, then run steps whose
  * queries and outputs already live in HBM ([batch][H*D] each).  The step is
  * replayed from a CUDA graph; nothing crosses PCIe. */

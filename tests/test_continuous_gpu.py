@@ -62,7 +62,8 @@ class HostMirror:
         return ids
 
 
-def run_continuous(dsd, H, D, P, K, n_req, max_active, window, pmin, pmax, dmin, dmax, seed):
+def run_continuous(dsd, H, D, P, K, n_req, max_active, window, pmin, pmax, dmin, dmax, seed,
+                   split_step=False):
     E = H * D
     w = o.continuous_workload(H, D, n_req, window, pmin, pmax, dmin, dmax, seed)
     ids, arr, pt, ds = w["request_ids"], w["arrival_steps"], w["prompt_tokens"], w["decode_steps"]
@@ -111,15 +112,21 @@ def run_continuous(dsd, H, D, P, K, n_req, max_active, window, pmin, pmax, dmin,
             continue
         rids = np.array([a["rid"] for a in active], np.int32)
         q = np.stack([a["query"] for a in active])
-        res = ctx.decode_step(rids, q, output_mode=dsd.OUTPUT_DEBUG)
+        if split_step:
+            ctx.decode_step_begin(rids, q, output_mode=dsd.OUTPUT_DEBUG)
+        else:
+            res = ctx.decode_step(rids, q, output_mode=dsd.OUTPUT_DEBUG)
         cand = [np.array(host.pages[a["rid"]], np.int32) for a in active]
         b = o.Batch(H, D, P, K, host.kp, host.vp, host.summ, host.tc, q,
                     np.concatenate([[0], np.cumsum([len(c) for c in cand])]).astype(np.int32),
                     np.concatenate(cand))
         sel, so, out, scores = o.sparse_decode(b)
-        assert np.array_equal(res["scores"].view(np.uint32), scores.view(np.uint32)), step
-        assert np.array_equal(res["selected"], sel), step
-        assert float(np.abs(res["outputs"] - out).max()) <= 1e-4, step
+        if split_step:
+            pending_check = (sel, out, scores)
+        else:
+            assert np.array_equal(res["scores"].view(np.uint32), scores.view(np.uint32)), step
+            assert np.array_equal(res["selected"], sel), step
+            assert float(np.abs(res["outputs"] - out).max()) <= 1e-4, step
         checked += 1
         # append this step's token (the last step's token is never uploaded)
         up_p, up_o, up_r, up_k, up_v = [], [], [], [], []
@@ -135,6 +142,13 @@ def run_continuous(dsd, H, D, P, K, n_req, max_active, window, pmin, pmax, dmin,
             a["remaining"] -= 1
         if up_p:
             ctx.append_tokens(up_p, up_o, np.stack(up_k), np.stack(up_v), request_ids=up_r)
+        if split_step:
+            # the appends were queued while the step was pending: it must not see them
+            res = ctx.decode_step_end()
+            sel, out, scores = pending_check
+            assert np.array_equal(res["scores"].view(np.uint32), scores.view(np.uint32)), step
+            assert np.array_equal(res["selected"], sel), step
+            assert float(np.abs(res["outputs"] - out).max()) <= 1e-4, step
         for a in [a for a in active if a["remaining"] == 0]:
             ctx.release_request(a["rid"], free_pages=True)
             host.release(a["rid"])
@@ -144,8 +158,9 @@ def run_continuous(dsd, H, D, P, K, n_req, max_active, window, pmin, pmax, dmin,
     return checked
 
 
-def test_continuous_small_shapes(dsd):
-    assert run_continuous(dsd, 4, 16, 8, 3, 10, 4, 6, 20, 60, 3, 10, 7) > 5
+@pytest.mark.parametrize("split_step", [False, True], ids=["sync_step", "begin_end_step"])
+def test_continuous_small_shapes(dsd, split_step):
+    assert run_continuous(dsd, 4, 16, 8, 3, 10, 4, 6, 20, 60, 3, 10, 7, split_step) > 5
 
 
 def test_continuous_config4_shape(dsd):
