@@ -1009,6 +1009,8 @@ __device__ __forceinline__ float decode_value(int request, int step, int element
 }
 
 // Synthetic prefill: page i is page_idx i of `request`; summary by AppendPage's formula.
+// The key (stream 1) and value (stream 2) hashes share every combine step but
+// the last, so the shared prefix is computed once per element and token.
 __global__ void prefill_synthetic_kernel(const int* __restrict__ page_ids,
                                          const int* __restrict__ counts, int request, int ept,
                                          int page_size, float* __restrict__ key_pool,
@@ -1019,11 +1021,16 @@ __global__ void prefill_synthetic_kernel(const int* __restrict__ page_ids,
   const int i = blockIdx.x;
   const int page = page_ids[i];
   const int n = counts[i];
+  uint32_t xr = 0x9e3779b9u;
+  xr = combine_hash(xr, request, 0x85ebca6bu);
+  xr = combine_hash(xr, i, 0xc2b2ae35u);
   for (int e = threadIdx.x; e < ept; e += blockDim.x) {
     float sum = 0.0f;
     for (int t = 0; t < n; ++t) {
-      const float k = prompt_value(request, i, t, e, 1);
-      const float v = prompt_value(request, i, t, e, 2);
+      uint32_t x = combine_hash(xr, t, 0x27d4eb2fu);
+      x = combine_hash(x, e, 0x165667b1u);
+      const float k = hash_to_unit(combine_hash(x, 1, 0xd3a2646cu));
+      const float v = hash_to_unit(combine_hash(x, 2, 0xd3a2646cu));
       key_pool[(size_t(page) * page_size + t) * ept + e] = k;
       value_pool[(size_t(page) * page_size + t) * ept + e] = v;
       sum = __fadd_rn(sum, k);

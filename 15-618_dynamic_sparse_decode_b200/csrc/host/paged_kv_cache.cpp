@@ -18,6 +18,7 @@ const std::vector<PageId>& NoPages() {
 PagedKvCache::PagedKvCache(ModelConfig config, int capacity_pages, bool allocate_kv_storage)
     : config_(config), pool_(config, capacity_pages, allocate_kv_storage) {
   summaries_.assign(static_cast<std::size_t>(capacity_pages) * ElementsPerToken(), 0.0f);
+  summary_dirty_.assign(static_cast<std::size_t>(capacity_pages), 0);
   pages_.reserve(static_cast<std::size_t>(capacity_pages));
   for (PageId p = 0; p < capacity_pages; ++p) pages_.push_back(FreeDescriptor(p));
 }
@@ -44,6 +45,16 @@ const float* PagedKvCache::Summary(PageId page_id) const {
   if (page_id < 0 || page_id >= static_cast<PageId>(pages_.size()))
     throw std::out_of_range("invalid page id");
   return summaries_.data() + static_cast<std::ptrdiff_t>(page_id) * ElementsPerToken();
+}
+
+// Clears a page's summary row unless it is known to be zero already: rows of
+// pages that were only reserved for GPU-resident prompts are never written
+// on the host, so admission does not memset 16 KiB per reserved page.
+void PagedKvCache::ClearSummary(PageId page_id) {
+  float* s = Summary(page_id);
+  auto& dirty = summary_dirty_[static_cast<std::size_t>(page_id)];
+  if (dirty) std::fill(s, s + ElementsPerToken(), 0.0f);
+  dirty = 0;
 }
 
 PageId PagedKvCache::AppendPage(int request_id, const std::vector<float>& keys,
@@ -75,9 +86,10 @@ PageId PagedKvCache::AppendPage(int request_id, const float* keys, const float* 
   const int start = NextStartToken(request_id);
   std::copy(keys, keys + n, pool_.get_k_page_ptr(id));
   std::copy(values, values + n, pool_.get_v_page_ptr(id));
+  ClearSummary(id);
   float* s = Summary(id);
-  std::fill(s, s + ept, 0.0f);
   if (compute_summary) {
+    summary_dirty_[static_cast<std::size_t>(id)] = 1;
     for (int t = 0; t < token_count; ++t) {
       const float* k = keys + static_cast<std::size_t>(t) * ept;
       for (int i = 0; i < ept; ++i) s[i] += k[i];
@@ -103,11 +115,9 @@ std::vector<PageId> PagedKvCache::ReservePagesForRequest(int request_id,
   std::sort(ids.begin(), ids.end());
   int start = NextStartToken(request_id);
   auto& list = request_pages_[request_id];
-  const int ept = ElementsPerToken();
   for (std::size_t i = 0; i < ids.size(); ++i) {
     const PageId id = ids[i];
-    float* s = Summary(id);
-    std::fill(s, s + ept, 0.0f);
+    ClearSummary(id);
     const std::size_t off = static_cast<std::size_t>(id) * ElementsPerPage();
     pages_[static_cast<std::size_t>(id)] = PageDescriptor{id, request_id, start, token_counts[i], off, off};
     list.push_back(id);
@@ -130,8 +140,7 @@ PageId PagedKvCache::TailForAppend(int request_id, bool force_new_page, bool* al
     const std::size_t off = static_cast<std::size_t>(id) * ElementsPerPage();
     pages_[static_cast<std::size_t>(id)] =
         PageDescriptor{id, request_id, NextStartToken(request_id), 0, off, off};
-    float* s = Summary(id);
-    std::fill(s, s + ElementsPerToken(), 0.0f);
+    ClearSummary(id);
     list.push_back(id);
     ++active_pages_;
     *allocated = true;
@@ -171,6 +180,7 @@ AppendTokenResult PagedKvCache::AppendToken(int request_id, const float* key, co
   std::copy(key, key + ept, pool_.get_k_page_ptr(id) + static_cast<std::ptrdiff_t>(off) * ept);
   std::copy(value, value + ept, pool_.get_v_page_ptr(id) + static_cast<std::ptrdiff_t>(off) * ept);
   float* s = Summary(id);
+  summary_dirty_[static_cast<std::size_t>(id)] = 1;
   const float old_c = static_cast<float>(page.token_count);
   const float new_c = old_c + 1.0f;
   for (int i = 0; i < ept; ++i) s[i] = (s[i] * old_c + key[i]) / new_c;
@@ -194,6 +204,7 @@ AppendTokenResult PagedKvCache::AppendTokenMetadataOnly(int request_id, const fl
   auto& page = pages_[static_cast<std::size_t>(id)];
   const int off = page.token_count;
   float* s = Summary(id);
+  summary_dirty_[static_cast<std::size_t>(id)] = 1;
   const float old_c = static_cast<float>(page.token_count);
   const float new_c = old_c + 1.0f;
   for (int i = 0; i < ElementsPerToken(); ++i) s[i] = (s[i] * old_c + key[i]) / new_c;
@@ -233,7 +244,7 @@ void PagedKvCache::Reset() {
   request_pages_.clear();
   active_pages_ = 0;
   pool_.reset_pool();
-  std::fill(summaries_.begin(), summaries_.end(), 0.0f);
+  for (PageId p = 0; p < static_cast<PageId>(pages_.size()); ++p) ClearSummary(p);
   for (PageId p = 0; p < static_cast<PageId>(pages_.size()); ++p)
     pages_[static_cast<std::size_t>(p)] = FreeDescriptor(p);
 }

@@ -7,6 +7,7 @@
 #pragma once
 
 #include <cstddef>
+#include <cstdint>
 #include <unordered_map>
 #include <vector>
 
@@ -83,11 +84,13 @@ class PagedKvCache {
   float* Summary(PageId page_id);
   const float* Summary(PageId page_id) const;
   PageId TailForAppend(int request_id, bool force_new_page, bool* allocated);
+  void ClearSummary(PageId page_id);
 
   ModelConfig config_;
   PagePool pool_;
   std::vector<PageDescriptor> pages_;
   std::vector<float> summaries_;
+  std::vector<std::uint8_t> summary_dirty_;   // row may hold non-zero values
   std::unordered_map<int, std::vector<PageId>> request_pages_;
   int active_pages_ = 0;
 };
