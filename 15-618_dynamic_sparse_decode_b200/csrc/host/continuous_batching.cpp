@@ -14,6 +14,11 @@
 #include <numeric>
 #include <random>
 #include <stdexcept>
+#include <atomic>
+#include <condition_variable>
+#include <functional>
+#include <mutex>
+#include <thread>
 #include <unordered_set>
 
 #include "capi_error.h"
@@ -92,6 +97,81 @@ std::vector<ContinuousRequestSpec> BuildSpecs(const ModelConfig& config, int num
   });
   return specs;
 }
+
+// A small persistent thread pool: ParallelFor(n, fn) runs fn(0..n-1) on the
+// workers and the calling thread, returning when every index is done.  Used
+// for the per-request payload generation of a step, which is independent
+// across requests (the page allocator stays serial).
+class WorkerPool {
+ public:
+  explicit WorkerPool(int threads) {
+    for (int t = 0; t < threads; ++t) workers_.emplace_back([this] { Loop(); });
+  }
+  ~WorkerPool() {
+    {
+      std::lock_guard<std::mutex> g(mu_);
+      stop_ = true;
+    }
+    cv_.notify_all();
+    for (auto& w : workers_) w.join();
+  }
+  void ParallelFor(int n, const std::function<void(int)>& fn) {
+    if (n <= 0) return;
+    if (workers_.empty() || n == 1) {
+      for (int i = 0; i < n; ++i) fn(i);
+      return;
+    }
+    {
+      std::lock_guard<std::mutex> g(mu_);
+      fn_.store(&fn);
+      n_.store(n);
+      next_.store(0);
+      done_ = 0;
+      ++generation_;
+    }
+    cv_.notify_all();
+    Work();
+    std::unique_lock<std::mutex> g(mu_);
+    done_cv_.wait(g, [&] { return done_ == n_.load(); });
+  }
+
+ private:
+  void Work() {
+    int finished = 0;
+    // n_ and fn_ are published before next_ is reset, so an index claimed
+    // from next_ always belongs to the job they describe
+    for (int i = next_.fetch_add(1); i < n_.load(); i = next_.fetch_add(1)) {
+      (*fn_.load())(i);
+      ++finished;
+    }
+    if (finished) {
+      std::lock_guard<std::mutex> g(mu_);
+      done_ += finished;
+      if (done_ == n_.load()) done_cv_.notify_all();
+    }
+  }
+  void Loop() {
+    long seen = 0;
+    for (;;) {
+      {
+        std::unique_lock<std::mutex> g(mu_);
+        cv_.wait(g, [&] { return stop_ || generation_ != seen; });
+        if (stop_) return;
+        seen = generation_;
+      }
+      Work();
+    }
+  }
+  std::vector<std::thread> workers_;
+  std::mutex mu_;
+  std::condition_variable cv_, done_cv_;
+  std::atomic<const std::function<void(int)>*> fn_{nullptr};
+  std::atomic<int> next_{1 << 30};
+  std::atomic<int> n_{0};
+  int done_ = 0;
+  long generation_ = 0;
+  bool stop_ = false;
+};
 
 double Percentile(std::vector<double> v, double p) {
   if (v.empty()) return 0.0;
@@ -303,6 +383,10 @@ ContinuousBatchStats RunContinuousSparseDecode(const ModelConfig& config,
   std::vector<int> up_pages, up_offs, up_reqs, up_steps;
   std::vector<float> up_k, up_v;
   std::vector<AppendTokenResult> results;
+  std::vector<std::vector<float>> gen_k, gen_v;
+  const int pool_threads = static_cast<int>(
+      std::min<unsigned>(8, std::max(1u, std::thread::hardware_concurrency())) - 1);
+  WorkerPool pool(pool_threads);
   std::vector<std::pair<int, PageId>> new_pages;
   while (next < specs.size() || !pending.empty() || !active.empty()) {
     if (active.empty() && pending.empty() && next < specs.size() &&
@@ -367,10 +451,32 @@ ContinuousBatchStats RunContinuousSparseDecode(const ModelConfig& config,
     up_pages.clear(); up_offs.clear(); up_reqs.clear(); up_steps.clear();
     up_k.clear(); up_v.clear();
     new_pages.clear();
-    for (auto& a : active) {
+    // payloads of this step (K/V of the token, the next query): independent
+    // per request, generated on the worker pool
+    const bool gen_kv = !options.gpu_synthetic_decode_append && !options.precompute_decode_payloads;
+    if (gen_kv) {
+      gen_k.resize(active.size());
+      gen_v.resize(active.size());
+    }
+    pool.ParallelFor(static_cast<int>(active.size()), [&](int i) {
+      auto& a = active[static_cast<std::size_t>(i)];
       const int rid = a.state.request_id;
       const int d = a.decode_step_index;
-      std::vector<float> gk, gv;
+      if (gen_kv) {
+        gen_k[static_cast<std::size_t>(i)] = DeterministicTokenVector(ept, rid, d, 1);
+        gen_v[static_cast<std::size_t>(i)] = DeterministicTokenVector(ept, rid, d, 2);
+      }
+      if (options.precompute_decode_payloads) {
+        const float* q = pre_q[a.spec_index].data() + static_cast<std::size_t>(d) * ept;
+        a.state.query.assign(q, q + ept);
+      } else {
+        a.state.query = DeterministicTokenVector(ept, rid, d + 1, 0);
+      }
+    });
+    for (std::size_t ai = 0; ai < active.size(); ++ai) {
+      auto& a = active[ai];
+      const int rid = a.state.request_id;
+      const int d = a.decode_step_index;
       const float* kp = nullptr;
       const float* vp = nullptr;
       if (!options.gpu_synthetic_decode_append) {
@@ -378,10 +484,8 @@ ContinuousBatchStats RunContinuousSparseDecode(const ModelConfig& config,
           kp = pre_k[a.spec_index].data() + static_cast<std::size_t>(d) * ept;
           vp = pre_v[a.spec_index].data() + static_cast<std::size_t>(d) * ept;
         } else {
-          gk = DeterministicTokenVector(ept, rid, d, 1);
-          gv = DeterministicTokenVector(ept, rid, d, 2);
-          kp = gk.data();
-          vp = gv.data();
+          kp = gen_k[ai].data();
+          vp = gen_v[ai].data();
         }
       }
       // GPU admission modes open a new page for the first decoded token (:614-616)
@@ -408,12 +512,6 @@ ContinuousBatchStats RunContinuousSparseDecode(const ModelConfig& config,
       if (!tables) {
         const auto& pages = cache.GetRequestPages(rid);
         a.state.candidate_page_ids.assign(pages.begin(), pages.end());
-      }
-      if (options.precompute_decode_payloads) {
-        const float* q = pre_q[a.spec_index].data() + static_cast<std::size_t>(d) * ept;
-        a.state.query.assign(q, q + ept);
-      } else {
-        a.state.query = DeterministicTokenVector(ept, rid, d + 1, 0);
       }
       ++a.decode_step_index;
       --a.remaining_decode_steps;
