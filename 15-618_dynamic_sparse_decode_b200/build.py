@@ -60,7 +60,8 @@ CXXFLAGS = ["-O3", "-std=c++17", "-fPIC", "-ffp-contract=off", "-Wall", "-Wextra
 
 def build_host(force: bool = False) -> None:
     headers = [os.path.join(INCLUDE, "dsd", h) for h in os.listdir(os.path.join(INCLUDE, "dsd"))]
-    headers += [os.path.join(HOST_DIR, "capi_error.h"), os.path.join(INCLUDE, "dsd_b200.h")]
+    headers += [os.path.join(HOST_DIR, h) for h in os.listdir(HOST_DIR) if h.endswith(".h")]
+    headers += [os.path.join(INCLUDE, "dsd_b200.h")]
     srcs = [os.path.join(HOST_DIR, s) for s in HOST_SOURCES]
     if force or not _newer(HOST_LIB, srcs + headers + [LIB]):
         subprocess.run([CXX, *CXXFLAGS, "-shared", "-o", HOST_LIB, *srcs, f"-L{PKG}",

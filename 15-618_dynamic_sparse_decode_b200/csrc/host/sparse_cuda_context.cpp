@@ -10,6 +10,7 @@
 #include <stdexcept>
 
 #include "capi_error.h"
+#include "worker_pool.h"
 #include "dsd_b200.h"
 #include "dsd/profiler.h"
 
@@ -49,9 +50,28 @@ SparseCudaContext::SparseCudaContext(const PagedKvCache& cache, const ModelConfi
   // queries are packed straight into the context's pinned staging and
   // outputs read from it: no extra host copy per step
   ThrowIf(dsd_step_host_buffers(ctx_, &host_queries_, &host_outputs_));
+  const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+  pack_pool_.reset(new detail::WorkerPool(static_cast<int>(std::min(4u, hw) - 1)));
+}
+
+// Copies every request's query into the pinned step staging; large batches
+// are split over the pack pool (the host copy is memory-bound).
+void SparseCudaContext::PackQueries(const std::vector<const RequestState*>& requests) {
+  const int B = static_cast<int>(requests.size());
+  const int ept = elements_per_token_;
+  auto copy_one = [&](int r) {
+    const auto& q = requests[static_cast<std::size_t>(r)]->query;
+    std::copy(q.begin(), q.end(), host_queries_ + static_cast<std::size_t>(r) * ept);
+  };
+  if (static_cast<std::size_t>(B) * ept < (std::size_t(1) << 17)) {
+    for (int r = 0; r < B; ++r) copy_one(r);
+  } else {
+    pack_pool_->ParallelFor(B, copy_one);
+  }
 }
 
 SparseCudaContext::~SparseCudaContext() {
+  pack_pool_.reset();
   pool_.reset();
   if (ctx_) dsd_ctx_destroy(ctx_);
 }
@@ -109,7 +129,6 @@ SparseBatchCudaResult SparseCudaContext::Run(const std::vector<const RequestStat
       if (!q) throw std::invalid_argument("request pointer must be non-null");
       if (static_cast<int>(q->query.size()) != ept)
         throw std::invalid_argument("query length does not match model config");
-      std::copy(q->query.begin(), q->query.end(), host_queries_ + static_cast<std::size_t>(r) * ept);
       int n;
       if (tables) {
         request_ids_.push_back(q->request_id);
@@ -123,6 +142,7 @@ SparseBatchCudaResult SparseCudaContext::Run(const std::vector<const RequestStat
           sel_off[static_cast<std::size_t>(r)] + std::max(0, std::min(config_.top_k_pages, n));
     }
     total_cand = offsets_.back();
+    PackQueries(requests);
   }
   const int total_sel = sel_off.back();
   if (B > max_batch_size_)
@@ -205,7 +225,6 @@ void SparseCudaContext::BeginStep(const std::vector<const RequestState*>& reques
     if (!q) throw std::invalid_argument("request pointer must be non-null");
     if (static_cast<int>(q->query.size()) != ept)
       throw std::invalid_argument("query length does not match model config");
-    std::copy(q->query.begin(), q->query.end(), host_queries_ + static_cast<std::size_t>(r) * ept);
     request_ids_.push_back(q->request_id);
     const int n = std::max(0, dsd_request_num_pages(ctx_, q->request_id));
     offsets_.push_back(offsets_.back() + n);
@@ -216,6 +235,7 @@ void SparseCudaContext::BeginStep(const std::vector<const RequestState*>& reques
     throw std::invalid_argument("candidate page count exceeds sparse CUDA context capacity");
   if (pending_sel_off_.back() > max_total_selected_pages_)
     throw std::invalid_argument("selected page count exceeds sparse CUDA context capacity");
+  PackQueries(requests);
   pending_prep_ms_ =
       std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   const int mode = options.output_mode == SparseBatchOutputMode::kNoOutputs ? DSD_OUTPUT_NONE

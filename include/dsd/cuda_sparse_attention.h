@@ -21,6 +21,10 @@ struct dsd_ctx;
 
 namespace dsd {
 
+namespace detail {
+class WorkerPool;
+}
+
 bool SparseAttentionCudaAvailable();
 
 enum class SparseBatchOutputMode { kNoOutputs, kOutputsOnly, kDebugTensors };
@@ -133,6 +137,8 @@ class SparseCudaContext {
   SparseRunBatchOptions pending_options_;
   double pending_prep_ms_ = 0.0;
   bool pending_ = false;
+  std::unique_ptr<detail::WorkerPool> pack_pool_;   // parallel query packing
+  void PackQueries(const std::vector<const RequestState*>& requests);
 };
 
 SparseDecodeResult SparseDecodeCuda(const PagedKvCache& cache, const RequestState& request,
