@@ -124,17 +124,19 @@ void SetAllAttnAttributes(size_t smem) {
 template <int NV, int S>
 void LaunchAttnT(const AttnShape& a, int grid, cudaStream_t st, const dsdk::StepPlan& plan,
                  const float* q, const float* k, const float* v, const int* tc, const int* sel,
-                 float* pacc, float* pml, int H, int D, int P, float scale) {
-  dsdk::attn_kernel<NV, S><<<grid, dsdk::kAttnThreads, a.smem, st>>>(plan, q, k, v, tc, sel, pacc,
-                                                                     pml, H, D, P, a.tps, scale);
+                 float* pacc, float* pml, int H, int D, int P, float scale, int part, int nparts) {
+  dsdk::attn_kernel<NV, S><<<grid, dsdk::kAttnThreads, a.smem, st>>>(
+      plan, q, k, v, tc, sel, pacc, pml, H, D, P, a.tps, scale, part, nparts);
 }
 
 void LaunchAttn(const AttnShape& a, int grid, cudaStream_t st, const dsdk::StepPlan& plan,
                 const float* q, const float* k, const float* v, const int* tc, const int* sel,
-                float* pacc, float* pml, int H, int D, int P, float scale) {
+                float* pacc, float* pml, int H, int D, int P, float scale, int part = 0,
+                int nparts = 1) {
 #define DSD_ATTN_CASE(NV, S)                                                        \
   if (a.nv == NV && a.slots == S) {                                                 \
-    LaunchAttnT<NV, S>(a, grid, st, plan, q, k, v, tc, sel, pacc, pml, H, D, P, scale); \
+    LaunchAttnT<NV, S>(a, grid, st, plan, q, k, v, tc, sel, pacc, pml, H, D, P, scale, part, \
+                       nparts);                                                     \
     return;                                                                         \
   }
   DSD_ATTN_CASE(1, 1) DSD_ATTN_CASE(1, 2) DSD_ATTN_CASE(1, 4) DSD_ATTN_CASE(1, 8)
@@ -155,7 +157,9 @@ struct dsd_ctx {
   AttnShape attn;     // attention launch shape
   float scale = 0.f;
   cudaStream_t stream = nullptr;
+  cudaStream_t stream2 = nullptr;      // second chain of a split step
   cudaEvent_t ev[6] = {};
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
 
   // pool
   float* k_pool = nullptr;
@@ -361,26 +365,45 @@ void RecordEvent(dsd_ctx* c, int i, bool capturing) {
                   : cudaEventRecord(c->ev[i], c->stream), "event record");
 }
 
+// One decode step.  Untimed steps split the requests into kStepParts ranges
+// whose kernel chains run on two streams (fork/join inside the captured
+// graph), so one part's small kernels and kernel tails overlap the other
+// part's bandwidth-bound kernels.  Timed steps run one chain with an event
+// between the stages.
+constexpr int kStepParts = 2;
+
 void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool capturing = false) {
   const dsdk::StepPlan& plan = c->plan;
   const int target_units = 8 * c->num_sms;
+  const int H = c->cfg.num_heads, D = c->cfg.head_dim, P = c->cfg.page_size;
+  const int sel_grid = std::max(1, std::min(c->opt.max_batch, 2 * c->num_sms));
+  const int pairs = c->opt.max_batch * H;
+  const int comb_grid = std::max(1, std::min((pairs + 7) / 8, 8 * c->num_sms));
+  const int nparts = timed ? 1 : kStepParts;
   if (timed) RecordEvent(c, 0, capturing);
   dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, c->stream>>>(plan, c->cfg.top_k_pages,
                                                              target_units, 2 * c->num_sms);
-  dsdk::score_kernel<<<2 * c->num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, c->stream>>>(
-      plan, d_q, c->summaries, c->ept, c->scale, c->d_scores);
-  if (timed) RecordEvent(c, 1, capturing);
-  const int sel_grid = std::max(1, std::min(c->opt.max_batch, 2 * c->num_sms));
-  dsdk::select_kernel<<<sel_grid, dsdk::kSelectThreads, dsdk::kSelectSmem, c->stream>>>(
-      plan, c->d_scores, c->d_selected);
-  if (timed) RecordEvent(c, 2, capturing);
-  const int H = c->cfg.num_heads, D = c->cfg.head_dim, P = c->cfg.page_size;
-  LaunchAttn(c->attn, c->num_sms, c->stream, plan, d_q, c->k_pool, c->v_pool, c->token_counts,
-             c->d_selected, c->d_part_acc, c->d_part_ml, H, D, P, c->scale);
-  const int pairs = c->opt.max_batch * H;
-  const int comb_grid = std::max(1, std::min((pairs + 7) / 8, 8 * c->num_sms));
-  dsdk::combine_kernel<<<comb_grid, 256, 0, c->stream>>>(plan, c->d_part_acc, c->d_part_ml, H, D,
-                                                         d_out);
+  if (nparts > 1) {
+    Check(cudaEventRecord(c->ev_fork, c->stream), "fork");
+    Check(cudaStreamWaitEvent(c->stream2, c->ev_fork, 0), "fork wait");
+  }
+  for (int part = 0; part < nparts; ++part) {
+    cudaStream_t st = part == 0 ? c->stream : c->stream2;
+    dsdk::score_kernel<<<2 * c->num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, st>>>(
+        plan, d_q, c->summaries, c->ept, c->scale, c->d_scores, part, nparts);
+    if (timed) RecordEvent(c, 1, capturing);
+    dsdk::select_kernel<<<sel_grid, dsdk::kSelectThreads, dsdk::kSelectSmem, st>>>(
+        plan, c->d_scores, c->d_selected, part, nparts);
+    if (timed) RecordEvent(c, 2, capturing);
+    LaunchAttn(c->attn, c->num_sms, st, plan, d_q, c->k_pool, c->v_pool, c->token_counts,
+               c->d_selected, c->d_part_acc, c->d_part_ml, H, D, P, c->scale, part, nparts);
+    dsdk::combine_kernel<<<comb_grid, 256, 0, st>>>(plan, c->d_part_acc, c->d_part_ml, H, D,
+                                                    d_out, part, nparts);
+  }
+  if (nparts > 1) {
+    Check(cudaEventRecord(c->ev_join, c->stream2), "join");
+    Check(cudaStreamWaitEvent(c->stream, c->ev_join, 0), "join wait");
+  }
   Check(cudaGetLastError(), "kernel launch");
   if (timed) RecordEvent(c, 3, capturing);
 }
@@ -647,6 +670,9 @@ int dsd_ctx_create(int device, const dsd_model_config* config, const dsd_ctx_opt
       c->scale = 1.0f / std::sqrt(static_cast<float>(D));
       Check(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream");
       for (auto& e : c->ev) Check(cudaEventCreate(&e), "event");
+      Check(cudaStreamCreateWithFlags(&c->stream2, cudaStreamNonBlocking), "stream");
+      Check(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming), "event");
+      Check(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming), "event");
 
       const size_t cap = size_t(opt.capacity_pages);
       c->k_pool = DeviceAlloc<float>(cap * cfg.page_size * ept, "key pool");
@@ -751,6 +777,9 @@ int dsd_ctx_destroy(dsd_ctx* c) {
     if (p) cudaFreeHost(p);
   for (auto& e : c->ev)
     if (e) cudaEventDestroy(e);
+  if (c->ev_fork) cudaEventDestroy(c->ev_fork);
+  if (c->ev_join) cudaEventDestroy(c->ev_join);
+  if (c->stream2) cudaStreamDestroy(c->stream2);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
   return DSD_OK;
@@ -1454,15 +1483,15 @@ extern "C" int dsd_decode_batch_noalloc(int device, const dsd_model_config* conf
     const float scale = 1.0f / std::sqrt(static_cast<float>(D));
     dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, s>>>(plan, cfg.top_k_pages, target, 2 * nd.num_sms);
     dsdk::score_kernel<<<2 * nd.num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, s>>>(
-        plan, d_queries, d_summaries, ept, scale, scores);
+        plan, d_queries, d_summaries, ept, scale, scores, 0, 1);
     dsdk::select_kernel<<<std::min(batch, 2 * nd.num_sms), dsdk::kSelectThreads,
-                          dsdk::kSelectSmem, s>>>(plan, scores, selected);
+                          dsdk::kSelectSmem, s>>>(plan, scores, selected, 0, 1);
     const AttnShape ash = MakeAttnShape(cfg.num_heads, D, cfg.page_size);
     LaunchAttn(ash, nd.num_sms, s, plan, d_queries, d_keys, d_values, d_token_counts, selected,
                part_acc, part_ml, cfg.num_heads, D, cfg.page_size, scale);
     const int pairs = batch * cfg.num_heads;
     dsdk::combine_kernel<<<std::max(1, std::min((pairs + 7) / 8, 8 * nd.num_sms)), 256, 0, s>>>(
-        plan, part_acc, part_ml, cfg.num_heads, D, d_outputs);
+        plan, part_acc, part_ml, cfg.num_heads, D, d_outputs, 0, 1);
     Check(cudaGetLastError(), "kernel launch");
     int status = 0;
     Check(cudaMemcpyAsync(&status, plan.status, sizeof(int), cudaMemcpyDeviceToHost, s),

@@ -183,6 +183,13 @@ __host__ __device__ __forceinline__ size_t summary_off(int page, int e, int ept)
   return summary_row_base(page, ept) + size_t(e / cw) * 128 * cw + (e % cw);
 }
 
+// Requests [r0, r1) of part `part` of `nparts` (a step may be split into
+// request ranges that run on different streams).
+__device__ __forceinline__ void part_range(int B, int part, int nparts, int* r0, int* r1) {
+  *r0 = static_cast<int>(static_cast<long long>(B) * part / nparts);
+  *r1 = static_cast<int>(static_cast<long long>(B) * (part + 1) / nparts);
+}
+
 // ------------------------------------------------------------------ plan
 
 // Block-wide exclusive scan of up to 4 ints per thread (one element per thread).
@@ -324,7 +331,7 @@ __device__ __forceinline__ void cp_async_wait() {
 // keeps the page offsets of the tile it is loading in registers.
 __global__ void __launch_bounds__(kScoreThreads, 2) score_kernel(
     StepPlan plan, const float* __restrict__ queries, const float* __restrict__ summaries,
-    int ept, float scale, float* __restrict__ scores) {
+    int ept, float scale, float* __restrict__ scores, int part, int nparts) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   float* stage_base = reinterpret_cast<float*>(smem_raw);
   constexpr int kCols = kScoreChunk / 4;                  // float4 columns per row chunk
@@ -336,7 +343,10 @@ __global__ void __launch_bounds__(kScoreThreads, 2) score_kernel(
   const int B = plan.hdr[0];
   const int mode = plan.hdr[1];
   const int* ids_src = mode == 0 ? plan.cand_ids : plan.table;
-  const int total_tiles = plan.tile_off[B];
+  int r_begin, r_end;
+  part_range(B, part, nparts, &r_begin, &r_end);
+  const int tile_begin = plan.tile_off[r_begin];
+  const int total_tiles = plan.tile_off[r_end];
   const int ts = plan.misc[1];
   const int cw = summary_chunk(ept);          // floats of a page's summary per stage
   const int nchunks = ept / cw;
@@ -345,7 +355,7 @@ __global__ void __launch_bounds__(kScoreThreads, 2) score_kernel(
   const int row0 = tid / kCols;
 
   // ---- loader state (runs kScoreStages-1 chunks ahead of the compute)
-  int ld_tile = blockIdx.x, ld_ch = 0, ld_slot = 0, ld_nvalid = 0;
+  int ld_tile = tile_begin + blockIdx.x, ld_ch = 0, ld_slot = 0, ld_nvalid = 0;
   const float* ld_q = queries;
   size_t ld_off[kRowsPerThread];
   auto load_tile = [&]() {
@@ -393,7 +403,7 @@ __global__ void __launch_bounds__(kScoreThreads, 2) score_kernel(
   for (int i = 0; i < kScoreStages - 1; ++i) issue();
 
   int slot = 0;
-  for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+  for (int tile = tile_begin + blockIdx.x; tile < total_tiles; tile += gridDim.x) {
     const int r = upper_segment(plan.tile_off, B, tile);
     const int c0 = (tile - plan.tile_off[r]) * ts;
     const int nvalid = min(ts, plan.n_cand[r] - c0);
@@ -456,7 +466,8 @@ __device__ __forceinline__ unsigned long long page_key(float score, int page) {
 // bitonic-sorted descending and written as page ids.
 __global__ void __launch_bounds__(kSelectThreads) select_kernel(StepPlan plan,
                                                                 const float* __restrict__ scores,
-                                                                int* __restrict__ selected) {
+                                                                int* __restrict__ selected,
+                                                                int part, int nparts) {
   extern __shared__ __align__(16) unsigned long long sel_smem[];
   unsigned long long* keys = sel_smem;                      // winners [kSelectMaxK]
   unsigned long long* all = sel_smem + kSelectMaxK;         // candidates [kSelectSmemKeys]
@@ -472,7 +483,9 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(StepPlan plan,
   const int* ids_src = mode == 0 ? plan.cand_ids : plan.table;
   const int tid = threadIdx.x;
 
-  for (int r = blockIdx.x; r < B; r += gridDim.x) {
+  int r_begin, r_end;
+  part_range(B, part, nparts, &r_begin, &r_end);
+  for (int r = r_begin + blockIdx.x; r < r_end; r += gridDim.x) {
     const int n = plan.n_cand[r];
     const int k = plan.sel_off[r + 1] - plan.sel_off[r];
     if (k <= 0) continue;
@@ -657,7 +670,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(
     StepPlan plan, const float* __restrict__ queries, const float* __restrict__ key_pool,
     const float* __restrict__ value_pool, const int* __restrict__ token_counts,
     const int* __restrict__ selected, float* __restrict__ part_acc, float* __restrict__ part_ml,
-    int num_heads, int head_dim, int page_size, int tps, float scale) {
+    int num_heads, int head_dim, int page_size, int tps, float scale, int part, int nparts) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   constexpr int kMaxTps = kAttnMaxTokensPerStage;
   const int ept = num_heads * head_dim;
@@ -676,12 +689,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(
   __syncthreads();
 
   const int B = plan.hdr[0];
-  const int total_units = plan.unit_off[B];
+  int r_begin, r_end;
+  part_range(B, part, nparts, &r_begin, &r_end);
+  const int unit_begin = plan.unit_off[r_begin];
+  const int total_units = plan.unit_off[r_end];
   const int ppu = plan.misc[0];
   const size_t page_floats = size_t(page_size) * ept;
   int* status = plan.status;
 
-  AttnWalk w{static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x), 0, 0, 0, 0, 0, false};
+  AttnWalk w{unit_begin + static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x), 0, 0, 0, 0,
+             0, false};
   auto issue = [&](int s) {
     const int nt = min(tps, w.n - w.t0);
     const uint32_t bytes = uint32_t(nt) * uint32_t(ept) * 4u;
@@ -713,7 +730,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(
 
   uint32_t g = 0;
   bool alive = true;
-  for (int u = blockIdx.x; u < total_units && alive; u += gridDim.x) {
+  for (int u = unit_begin + blockIdx.x; u < total_units && alive; u += gridDim.x) {
     int r, p_begin, p_end;
     attn_unit_range(plan, B, ppu, u, &r, &p_begin, &p_end);
     float4 q[SLOTS][NV], acc[SLOTS][NV];
@@ -810,13 +827,16 @@ __global__ void __launch_bounds__(256) combine_kernel(StepPlan plan,
                                                       const float* __restrict__ part_acc,
                                                       const float* __restrict__ part_ml,
                                                       int num_heads, int head_dim,
-                                                      float* __restrict__ outputs) {
+                                                      float* __restrict__ outputs, int part,
+                                                      int nparts) {
   const int B = plan.hdr[0];
   const int lane = threadIdx.x & 31;
   const int ept = num_heads * head_dim;
-  const int pairs = B * num_heads;
+  int r_begin, r_end;
+  part_range(B, part, nparts, &r_begin, &r_end);
+  const int pairs = r_end * num_heads;
   const int g4 = head_dim >> 2;
-  for (int wg = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wg < pairs;
+  for (int wg = r_begin * num_heads + ((blockIdx.x * blockDim.x + threadIdx.x) >> 5); wg < pairs;
        wg += (gridDim.x * blockDim.x) >> 5) {
     const int r = wg / num_heads, h = wg - (wg / num_heads) * num_heads;
     const int u0 = plan.unit_off[r], u1 = plan.unit_off[r + 1];
