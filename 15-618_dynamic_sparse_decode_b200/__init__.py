@@ -95,6 +95,7 @@ SIGNATURES = [
     ("dsd_decode_bound", ctypes.c_int, [_VP, _VP, _VP]),
     ("dsd_decode_bound_timed", ctypes.c_int, [_VP, _VP, _VP, ctypes.POINTER(StepTiming)]),
     ("dsd_read_step_timing", ctypes.c_int, [_VP, ctypes.POINTER(StepTiming)]),
+    ("dsd_set_attention_mode", ctypes.c_int, [_VP, ctypes.c_int]),
     ("dsd_kernels_per_step", ctypes.c_int, []),
     ("dsd_selftest_bounded_wait", ctypes.c_int, [_VP, ctypes.c_int64]),
     ("dsd_decode_batch_noalloc", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ModelConfig),
@@ -300,13 +301,19 @@ class SparseDecodeContext:
         sel = np.zeros(max(1, total_sel), np.int32) if output_mode == OUTPUT_DEBUG else None
         return out, scores, sel
 
+    def set_dense(self, dense: bool):
+        """Dense baseline: later steps attend over every candidate page."""
+        _check(self.lib.dsd_set_attention_mode(self.h, int(dense)))
+        self.dense = bool(dense)
+
     def decode_batch(self, queries, cand_offsets, cand_ids, output_mode=OUTPUT_DEBUG, timing=False):
         """RunBatch with explicit candidates.  Returns dict(outputs, scores, selected, timing)."""
         q = _f32(queries)
         offs, ids = _i32(cand_offsets), _i32(cand_ids)
         B = len(offs) - 1
         n = np.diff(offs)
-        total_sel = int(np.minimum(n, self.cfg.top_k_pages).clip(0).sum())
+        total_sel = int(n.sum() if getattr(self, "dense", False)
+                        else np.minimum(n, self.cfg.top_k_pages).clip(0).sum())
         out, scores, sel = self._results(B, int(offs[-1]) if B > 0 else 0, total_sel, output_mode)
         t = StepTiming()
         _check(self.lib.dsd_decode_batch(self.h, B, _fp(q), _ip(offs), _ip(ids), output_mode,

@@ -222,6 +222,7 @@ struct dsd_ctx {
   std::vector<StepGraph> graphs;
 
   dsd_transfer_stats stats{};
+  int dense = 0;   // attend over every candidate (dense baseline) instead of the top-k
 
   // a step queued by dsd_decode_step_begin, finished by dsd_decode_step_end
   struct PendingStep {
@@ -620,6 +621,14 @@ int dsd_available(void) {
 }
 
 int dsd_kernels_per_step(void) { return 5; }
+
+int dsd_set_attention_mode(dsd_ctx* c, int dense) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    if (c->pending.active) Fail(DSD_EINVAL, "a decode step is pending");
+    c->dense = dense ? 1 : 0;
+  });
+}
 
 int dsd_selftest_bounded_wait(dsd_ctx* c, int64_t budget_cycles) {
   return Guard([&]() {
@@ -1147,7 +1156,7 @@ int dsd_decode_batch(dsd_ctx* c, int batch, const float* queries, const int32_t*
     for (int r = 0; r < batch; ++r) {
       const int n = cand_offsets[r + 1] - cand_offsets[r];
       if (n < 0) Fail(DSD_EINVAL, "cand_offsets must be non-decreasing");
-      total_sel += std::min(c->cfg.top_k_pages, n);
+      total_sel += c->dense ? n : std::min(c->cfg.top_k_pages, n);
     }
     const int total_cand = cand_offsets[batch];
     if (total_cand > c->opt.max_candidates)
@@ -1159,6 +1168,7 @@ int dsd_decode_batch(dsd_ctx* c, int batch, const float* queries, const int32_t*
     int* hdr = HdrPtr(c);
     hdr[0] = batch;
     hdr[1] = 0;
+    hdr[2] = c->dense;
     std::memcpy(ReqPtr(c), cand_offsets, size_t(batch + 1) * 4);
     std::memcpy(IdsPtr(c), cand_ids, size_t(total_cand) * 4);
     UploadQueries(c, queries, batch);
@@ -1240,7 +1250,7 @@ void PackSlots(dsd_ctx* c, const int32_t* request_ids, int batch, int* total_can
     req[r] = slot;
     const int n = int(c->slot_pages[slot].size());
     tc += n;
-    ts += std::min(c->cfg.top_k_pages, n);
+    ts += c->dense ? n : std::min(c->cfg.top_k_pages, n);
   }
   req[batch] = 0;
   if (tc > c->opt.max_candidates)
@@ -1250,6 +1260,7 @@ void PackSlots(dsd_ctx* c, const int32_t* request_ids, int batch, int* total_can
   int* hdr = HdrPtr(c);
   hdr[0] = batch;
   hdr[1] = 1;
+  hdr[2] = c->dense;
   *total_cand = tc;
   *total_sel = ts;
 }

@@ -59,7 +59,7 @@ constexpr long long kWaitBudgetCycles = 2LL << 30;
 
 struct StepPlan {
   // written by the host each step (one packed H2D copy)
-  const int* hdr;          // [0] batch, [1] mode (0 = CSR, 1 = page tables)
+  const int* hdr;          // [0] batch, [1] mode (0 = CSR, 1 = page tables), [2] dense
   const int* req;          // CSR: cand_offsets[B+1]; tables: slot[B]
   const int* cand_ids;     // CSR ids
   // device page tables
@@ -73,7 +73,7 @@ struct StepPlan {
   int* sel_off;            // [B+1]
   int* tile_off;           // [B+1]
   int* unit_off;           // [B+1]
-  int* misc;               // [0] pages per attention unit, [1] score tile size
+  int* misc;               // [0] pages per attention unit, [1] score tile size, [2] dense
   int* status;             // error bits
 };
 
@@ -240,6 +240,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(StepPlan plan, int t
                                                             int target_units, int score_grid) {
   const int B = plan.hdr[0];
   const int mode = plan.hdr[1];
+  const int dense = plan.hdr[2];   // 1: attend over every candidate (no scoring, no top-k)
   const int r = threadIdx.x;
   int n = 0, base = 0;
   if (r < B) {
@@ -253,7 +254,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(StepPlan plan, int t
     }
     if (n < 0) { n = 0; atomicOr(plan.status, kStatusBadInput); }
   }
-  const int ksel = max(0, min(top_k, n));
+  const int ksel = dense ? n : max(0, min(top_k, n));
   int v[2] = {n, ksel};
   int tot[2];
   block_exclusive_scan<2>(v, tot);
@@ -277,7 +278,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(StepPlan plan, int t
     __syncthreads();
     if (count <= target_tiles) break;
   }
-  int t1[1] = {(n + ts - 1) / ts};
+  int t1[1] = {dense ? 0 : (n + ts - 1) / ts};
   int ttot[1];
   block_exclusive_scan<1>(t1, ttot);
   if (r < B) {
@@ -292,6 +293,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(StepPlan plan, int t
     plan.sel_off[B] = tot[1];
     plan.tile_off[B] = ttot[0];
     plan.misc[1] = ts;
+    plan.misc[2] = dense;
   }
   // pages per attention unit: enough units to fill the GPU, at most 16 pages
   int ppu = (tot[1] + target_units - 1) / max(1, target_units);
@@ -489,12 +491,18 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(StepPlan plan,
     const int n = plan.n_cand[r];
     const int k = plan.sel_off[r + 1] - plan.sel_off[r];
     if (k <= 0) continue;
-    if (k > kSelectMaxK) {
+    if (k > kSelectMaxK && !plan.misc[2]) {
       if (tid == 0) atomicOr(plan.status, kStatusBadInput);
       continue;
     }
-    const float* sc = scores + plan.score_off[r];
     const int* ids = ids_src + plan.id_base[r];
+    if (plan.misc[2]) {
+      // dense attention: every candidate, in candidate order
+      int* out = selected + plan.sel_off[r];
+      for (int i = tid; i < k; i += blockDim.x) out[i] = __ldg(ids + i);
+      continue;
+    }
+    const float* sc = scores + plan.score_off[r];
     const bool staged = n <= kSelectSmemKeys;
     if (staged) {
       for (int i = tid; i < n; i += blockDim.x) all[i] = page_key(sc[i], __ldg(ids + i));

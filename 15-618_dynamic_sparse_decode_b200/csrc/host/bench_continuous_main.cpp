@@ -7,7 +7,7 @@
 //   1 direct_gpu_upload, 2 synthetic_gpu_prefill) 14 preadmit 15 precompute
 //   16 gpu_synthetic_append 17 lazy_release 18 output_mode (0 none, 1 outputs,
 //   2 debug) 19 timing (0 none, 1 kernel_events) 20 benchmark_mode (0 sparse,
-//   1 dense_gpu: not part of this build)
+//   1 dense_gpu)
 // Added: 21 device_page_tables (default 1), 22 skip the serial run (default 0),
 // 23 shard_world (default 1), 24 shard_rank (default 0): serve only requests
 // with request_id % shard_world == shard_rank (one process per GPU),
@@ -132,17 +132,13 @@ int main(int argc, char** argv) try {
             << "\nbenchmark_mode=" << (bench_mode == 1 ? "dense_gpu" : "sparse")
             << "\ndevice_page_tables=" << o.device_page_tables << "\nshard_world=" << shard_world
             << "\nshard_rank=" << shard_rank << "\n";
-  if (bench_mode == 1) {
-    std::cout << "continuous_dense_gpu_available=0\n"
-              << "continuous dense GPU benchmark skipped: not part of this build\n";
-    return 0;
-  }
+
+  const char* avail = bench_mode == 1 ? "continuous_dense_gpu_available" : "continuous_sparse_available";
   if (!dsd::SparseAttentionCudaAvailable()) {
-    std::cout << "continuous_sparse_available=0\n"
-              << "continuous benchmark skipped: no visible sm_100 GPU\n";
+    std::cout << avail << "=0\ncontinuous benchmark skipped: no visible sm_100 GPU\n";
     return 0;
   }
-  std::cout << "continuous_sparse_available=1\n";
+  std::cout << avail << "=1\n";
   auto specs =
       admission == 2
           ? dsd::BuildSyntheticContinuousSpecs(config, num_requests, arrival_window, min_prompt,
@@ -156,6 +152,12 @@ int main(int argc, char** argv) try {
     specs.swap(mine);
   }
   std::cout << "shard_requests=" << specs.size() << "\n";
+  if (bench_mode == 1) {
+    const auto d = dsd::RunContinuousDenseGpuDecode(config, specs, o);
+    std::cout << "total_generated_tokens=" << d.total_generated_tokens << "\n";
+    Print("continuous_dense_gpu", d);
+    return 0;
+  }
   if (skip_serial) {
     std::vector<dsd::ContinuousBatchStats> runs;
     for (int i = 0; i < repeats; ++i) {

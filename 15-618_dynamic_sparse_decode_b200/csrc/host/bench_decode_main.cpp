@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "dsd/config.h"
+#include "dsd/cuda_dense_attention.h"
 #include "dsd/cuda_sparse_attention.h"
 #include "dsd/decode_pipeline.h"
 #include "dsd/reference_kernels.h"
@@ -75,13 +76,18 @@ int main(int argc, char** argv) {
   }
 
   std::unique_ptr<dsd::SparseCudaContext> gpu;
+  std::unique_ptr<dsd::DenseCudaContext> dense_gpu;
   const bool gpu_ok = dsd::SparseAttentionCudaAvailable();
-  if (gpu_ok)
+  if (gpu_ok) {
     gpu.reset(new dsd::SparseCudaContext(batch.cache, config, batch_size, static_cast<int>(cand),
                                          total_sel));
+    dense_gpu.reset(new dsd::DenseCudaContext(batch.cache, config));
+  }
 
   double dense_total = 0, sparse_total = 0, s_score = 0, s_topk = 0, s_gather = 0, s_attn = 0;
   double g_total = 0, g_score = 0, g_topk = 0, g_attn = 0, g_kernel = 0;
+  double dg_total = 0, dg_kernel = 0;
+  dsd::DenseBatchResult dense_gpu_out;
   dsd::RuntimeOverheadTimings g_oh;
   std::vector<dsd::AttentionResult> dense_out;
   dsd::BatchDecodeResult cpu_out;
@@ -102,6 +108,13 @@ int main(int argc, char** argv) {
       s_attn += cpu_out.aggregate_timings.attention_ms;
     }
     if (gpu_ok) {
+      const auto h0 = Clock::now();
+      dense_gpu_out = dense_gpu->RunBatch(batch.requests);
+      const auto h1 = Clock::now();
+      if (timed) {
+        dg_total += Ms(h0, h1);
+        dg_kernel += dense_gpu_out.kernel_ms;
+      }
       const auto g0 = Clock::now();
       gpu_out = gpu->RunBatch(batch.requests, dsd::SparseBatchOutputMode::kDebugTensors);
       const auto g1 = Clock::now();
@@ -119,6 +132,7 @@ int main(int argc, char** argv) {
   const double n = std::max(1, iterations);
   dense_total /= n; sparse_total /= n; s_score /= n; s_topk /= n; s_gather /= n; s_attn /= n;
   g_total /= n; g_score /= n; g_topk /= n; g_attn /= n; g_kernel /= n;
+  dg_total /= n; dg_kernel /= n;
   g_oh.time_sync_ms /= n; g_oh.time_prepare_sparse_layout_ms /= n;
 
   std::cout << "\n== Decode Benchmark ==\n";
@@ -159,7 +173,7 @@ int main(int argc, char** argv) {
             << std::setw(14) << "Speedup" << "  Note\n" << std::string(72, '-') << "\n";
   e2e("dense_cpu", dense_total, true, "reference wall time");
   e2e("sparse_cpu", sparse_total, true, "naive sparse pipeline");
-  e2e("dense_gpu", 0.0, false, "not part of this build");
+  e2e("dense_gpu", dg_total, gpu_ok, gpu_ok ? "dense split-K attention (all pages)" : "unavailable");
   e2e("sparse_gpu", g_total, gpu_ok, gpu_ok ? "B200 sparse path (RunBatch)" : "unavailable");
 
   auto brk = [&](const char* name, double a, double b, double c, double d, double k, bool ok,
@@ -174,7 +188,7 @@ int main(int argc, char** argv) {
             << std::setw(14) << "GPUKernel" << "  Note\n" << std::string(86, '-') << "\n";
   brk("dense_cpu", 0, 0, 0, dense_total, 0, true, "attention only");
   brk("sparse_cpu", s_score, s_topk, s_gather, s_attn, 0, true, "full CPU stage split");
-  brk("dense_gpu", 0, 0, 0, 0, 0, false, "not part of this build");
+  brk("dense_gpu", 0, 0, 0, dg_kernel, dg_kernel, gpu_ok, "attention kernel only");
   brk("sparse_gpu", g_score, g_topk, 0, g_attn, g_kernel, gpu_ok,
       gpu_ok ? "gather fused into attention" : "unavailable");
 
@@ -195,11 +209,11 @@ int main(int argc, char** argv) {
   const dsd::RuntimeOverheadTimings none;
   oh("dense_cpu", none, true, "host only");
   oh("sparse_cpu", none, true, "host only");
-  oh("dense_gpu", none, false, "not part of this build");
+  oh("dense_gpu", dense_gpu_out.runtime_overheads, gpu_ok, "copies+launch+wait in one call");
   oh("sparse_gpu", g_oh, gpu_ok, "copies+launch+wait are one C ABI call (Sync)");
 
   // accuracy against dense_cpu and sparse_cpu; selection exactness
-  double cpu_vs_dense = 0, gpu_vs_cpu = 0, gpu_vs_dense = 0;
+  double cpu_vs_dense = 0, gpu_vs_cpu = 0, gpu_vs_dense = 0, dgpu_vs_dense = 0;
   bool exact = true;
   for (std::size_t i = 0; i < batch.requests.size(); ++i) {
     cpu_vs_dense += dsd::MaxAbsDiff(cpu_out.per_request[i].output.output, dense_out[i].output);
@@ -207,6 +221,7 @@ int main(int argc, char** argv) {
       gpu_vs_cpu += dsd::MaxAbsDiff(gpu_out.per_request[i].output.output,
                                     cpu_out.per_request[i].output.output);
       gpu_vs_dense += dsd::MaxAbsDiff(gpu_out.per_request[i].output.output, dense_out[i].output);
+      dgpu_vs_dense += dsd::MaxAbsDiff(dense_gpu_out.outputs[i].output, dense_out[i].output);
       exact = exact && gpu_out.per_request[i].selected_page_ids ==
                            cpu_out.per_request[i].selected_page_ids;
     }
@@ -217,6 +232,7 @@ int main(int argc, char** argv) {
   if (gpu_ok) {
     std::cout << "avg_max_abs_diff_sparse_gpu_vs_sparse_cpu=" << gpu_vs_cpu / nb << "\n";
     std::cout << "avg_max_abs_diff_sparse_gpu_vs_dense_cpu=" << gpu_vs_dense / nb << "\n";
+    std::cout << "avg_max_abs_diff_dense_gpu_vs_dense_cpu=" << dgpu_vs_dense / nb << "\n";
     std::cout << "sparse_gpu_selection_exact=" << (exact ? 1 : 0) << "\n";
     // algorithmic bytes of one GPU step over its kernel time
     std::uint64_t sel_tokens = 0;

@@ -209,9 +209,25 @@ ContinuousBatchStats RunContinuousSparseDecode(const ModelConfig& config,
   return RunContinuousSparseDecode(config, requests, o);
 }
 
+namespace {
+ContinuousBatchStats RunContinuous(const ModelConfig& config,
+                                   const std::vector<ContinuousRequestSpec>& specs,
+                                   const ContinuousDecodeOptions& options, bool dense);
+}  // namespace
+
 ContinuousBatchStats RunContinuousSparseDecode(const ModelConfig& config,
                                                const std::vector<ContinuousRequestSpec>& specs,
                                                const ContinuousDecodeOptions& options) {
+  return RunContinuous(config, specs, options, false);
+}
+
+namespace {
+
+// The serving loop of both backends; `dense` attends over every page of each
+// active request (the dense GPU baseline) instead of the top-k pages.
+ContinuousBatchStats RunContinuous(const ModelConfig& config,
+                                   const std::vector<ContinuousRequestSpec>& specs,
+                                   const ContinuousDecodeOptions& options, bool dense) {
   using Mode = ContinuousPromptAdmissionMode;
   if (options.max_active_requests <= 0)
     throw std::invalid_argument("max_active_requests must be positive");
@@ -238,7 +254,8 @@ ContinuousBatchStats RunContinuousSparseDecode(const ModelConfig& config,
   const int window = std::max(1, options.max_active_requests * max_pages);
   const int capacity = options.preadmit_prompts ? total_pages : std::min(total_pages, window);
   const int max_cand = options.max_active_requests * max_pages;
-  const int max_sel = options.max_active_requests * std::min(config.top_k_pages, max_pages);
+  const int max_sel =
+      dense ? max_cand : options.max_active_requests * std::min(config.top_k_pages, max_pages);
   const bool metadata_only = options.prompt_admission_mode != Mode::kCpuCache;
   const bool tables = options.device_page_tables;
   const int table_slots = options.preadmit_prompts ? static_cast<int>(specs.size())
@@ -248,6 +265,7 @@ ContinuousBatchStats RunContinuousSparseDecode(const ModelConfig& config,
   SparseCudaContext ctx(cache, config, options.max_active_requests, max_cand, max_sel,
                         tables ? std::max(1, table_slots) : 0, tables ? max_pages : 0,
                         options.device);
+  if (dense) detail::ThrowIf(dsd_set_attention_mode(ctx.handle(), 1));
   ctx.ResetDeviceTransferStats();
   const int ept = Ept(config);
 
@@ -516,15 +534,20 @@ ContinuousBatchStats RunContinuousSparseDecode(const ModelConfig& config,
   return stats;
 }
 
-ContinuousBatchStats RunContinuousDenseGpuDecode(const ModelConfig&,
-                                                 const std::vector<ContinuousRequestSpec>&, int) {
-  throw std::runtime_error("the dense GPU baseline is not part of this build");
+}  // namespace
+
+ContinuousBatchStats RunContinuousDenseGpuDecode(const ModelConfig& config,
+                                                 const std::vector<ContinuousRequestSpec>& specs,
+                                                 int max_active_requests) {
+  ContinuousDecodeOptions o;
+  o.max_active_requests = max_active_requests;
+  return RunContinuousDenseGpuDecode(config, specs, o);
 }
 
-ContinuousBatchStats RunContinuousDenseGpuDecode(const ModelConfig&,
-                                                 const std::vector<ContinuousRequestSpec>&,
-                                                 const ContinuousDecodeOptions&) {
-  throw std::runtime_error("the dense GPU baseline is not part of this build");
+ContinuousBatchStats RunContinuousDenseGpuDecode(const ModelConfig& config,
+                                                 const std::vector<ContinuousRequestSpec>& specs,
+                                                 const ContinuousDecodeOptions& options) {
+  return RunContinuous(config, specs, options, true);
 }
 
 ContinuousBenchmarkResult RunContinuousSparseBenchmark(

@@ -216,6 +216,12 @@ int dsd_decode_bound_timed(dsd_ctx* ctx, const float* d_queries, float* d_output
                            dsd_step_timing* out_timing);
 int dsd_read_step_timing(dsd_ctx* ctx, dsd_step_timing* out_timing);
 
+/* Dense baseline (DenseCudaContext, src/cuda/kernels.cu:76-330 in the
+ * reference): with dense != 0 every later step of this context attends over
+ * ALL candidate pages in candidate order (no scoring, no top-k); selected
+ * counts then equal candidate counts, so max_selected must cover them. */
+int dsd_set_attention_mode(dsd_ctx* ctx, int dense);
+
 /* Number of kernels one decode step launches (for launch accounting). */
 int dsd_kernels_per_step(void);
 

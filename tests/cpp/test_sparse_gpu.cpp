@@ -7,6 +7,7 @@
 
 #include "check.h"
 #include "dsd/continuous_batching.h"
+#include "dsd/cuda_dense_attention.h"
 #include "dsd/cuda_sparse_attention.h"
 #include "dsd/decode_pipeline.h"
 #include "dsd/device_page_pool.h"
@@ -54,6 +55,23 @@ void SyntheticCase(dsd::ModelConfig c, int batch, int lo, int hi, int seed, floa
   o.timing_mode = dsd::SparseBatchTimingMode::kNone;
   const auto none = ctx.RunBatch(b.requests, o);
   CHECK(none.per_request.empty() && none.kernel_ms == 0.0, "no-output mode returns nothing");
+}
+
+// dense_gpu vs dense_cpu (tests/test_dense_cuda.cpp:21-156) incl. a request with no pages
+void DenseBaseline() {
+  const auto c = Cfg(4, 32, 8, 4);
+  auto b = dsd::BuildSyntheticBatch(c, 3, 40, 120, 5);
+  dsd::RequestState empty;
+  empty.request_id = 99;
+  empty.query = b.requests[0].query;
+  b.requests.push_back(empty);
+  dsd::DenseCudaContext ctx(b.cache, c);
+  const auto g = ctx.RunBatch(b.requests);
+  dsd::DecodePipeline p(c);
+  CHECK(g.outputs.size() == b.requests.size(), "one dense output per request");
+  for (std::size_t i = 0; i < b.requests.size(); ++i)
+    CHECK(dsd::MaxAbsDiff(p.RunDenseStep(b.cache, b.requests[i]).output, g.outputs[i].output) <= 5e-5f,
+          "dense output differs");
 }
 
 void TopKZero() {
@@ -200,6 +218,7 @@ int main() {
   SyntheticCase(Cfg(2, 16, 8, 8), 2, 160, 184, 123, 3e-5f);
   SyntheticCase(Cfg(32, 128, 16, 8), 16, 512, 2048, 7, 1e-4f);
   TopKZero();
+  DenseBaseline();
   TieBreak();
   DevicePoolRoundTrip();
   ContinuousSequence();

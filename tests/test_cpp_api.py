@@ -56,3 +56,15 @@ def test_cli_continuous_small():
     assert int(kv["total_generated_tokens"]) > 0
     assert float(kv["continuous_sparse_tokens_per_second"]) > 0
     assert float(kv["continuous_vs_serial_speedup"]) > 0
+
+
+@pytest.mark.gpu
+def test_cli_continuous_dense_mode():
+    exe = os.path.join(PKG, "bin", "dsd_continuous_bench")
+    r = subprocess.run([exe, "8", "4", "8", "40", "120", "3", "9", "7", "4", "16", "8", "3", "1",
+                        "0", "0", "0", "0", "1", "1", "1"], capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0, r.stderr
+    kv = dict(l.split("=", 1) for l in r.stdout.splitlines() if "=" in l)
+    assert kv["continuous_dense_gpu_available"] == "1"
+    assert float(kv["continuous_dense_gpu_tokens_per_second"]) > 0

@@ -238,3 +238,24 @@ def test_pinned_host_buffers_match_pageable(dsd, orc):
         assert np.array_equal(o_pin, ref["outputs"])
         res = ctx.decode_batch(q_pin, b.cand_offsets, b.cand_ids)
         check_against_oracle(orc, b, res, 1e-4)
+
+
+# tests/test_dense_cuda.cpp:21-156: dense_gpu vs dense_cpu on five shapes
+DENSE_CASES = [((2, 8, 4, 4, 3, 5, 19, 11), 1e-5), ((4, 16, 16, 4, 4, 33, 97, 7), 2e-5),
+               ((2, 64, 8, 4, 2, 17, 45, 17), 5e-5), ((8, 32, 16, 4, 3, 100, 300, 5), 5e-5),
+               ((32, 128, 16, 8, 4, 256, 1024, 7), 1e-4)]
+
+
+@pytest.mark.parametrize("cfg,tol", DENSE_CASES, ids=[f"dense{i}" for i in range(len(DENSE_CASES))])
+def test_dense_baseline_matches_dense_cpu(dsd, orc, cfg, tol):
+    b = orc.synthetic_batch(*cfg)
+    n = np.diff(b.cand_offsets)
+    with dsd.SparseDecodeContext(b.num_heads, b.head_dim, b.page_size, b.top_k, b.capacity,
+                                 b.batch, int(n.sum()), int(n.sum())) as ctx:
+        ctx.upload_pool(b.key_pool, b.value_pool, b.token_counts)
+        ctx.set_dense(True)
+        res = ctx.decode_batch(b.queries, b.cand_offsets, b.cand_ids)
+        assert np.array_equal(res["selected"], b.cand_ids)      # every page, candidate order
+        assert float(np.abs(res["outputs"] - orc.dense_decode(b)).max()) <= tol
+        ctx.set_dense(False)                                    # back to the sparse path
+        check_against_oracle(orc, b, ctx.decode_batch(b.queries, b.cand_offsets, b.cand_ids), 1e-4)
