@@ -61,6 +61,7 @@ SIGNATURES = [
                                                ctypes.POINTER(_VP), ctypes.POINTER(_VP)]),
     ("dsd_ctx_stream", _VP, [_VP]),
     ("dsd_step_host_buffers", ctypes.c_int, [_VP, ctypes.POINTER(_VP), ctypes.POINTER(_VP)]),
+    ("dsd_step_staging_wait", ctypes.c_int, [_VP]),
     ("dsd_pool_reset", ctypes.c_int, [_VP]),
     ("dsd_pool_upload_pages", ctypes.c_int, [_VP, _I32P, _I32P, ctypes.c_int, _F32P, _F32P,
                                              ctypes.c_int]),
@@ -363,12 +364,14 @@ class SparseDecodeContext:
 
     def decode_step_begin(self, request_ids, queries, output_mode=OUTPUT_OUTPUTS):
         req, q = _i32(request_ids), _f32(queries)
-        self._pending = (len(req), output_mode,
-                         np.array([self.request_num_pages(int(r)) for r in req]))
+        if not hasattr(self, "_pending"):
+            self._pending = []
+        n = np.array([self.request_num_pages(int(r)) for r in req])
         _check(self.lib.dsd_decode_step_begin(self.h, _ip(req), len(req), _fp(q), output_mode, 0))
+        self._pending.append((len(req), output_mode, n))
 
     def decode_step_end(self):
-        B, mode, n = self._pending
+        B, mode, n = self._pending.pop(0)
         total_sel = int(np.minimum(n, self.cfg.top_k_pages).sum())
         out, scores, sel = self._results(B, int(n.sum()), total_sel, mode)
         _check(self.lib.dsd_decode_step_end(self.h, _fp(out), _fp(scores), _ip(sel), None))

@@ -158,7 +158,10 @@ struct dsd_ctx {
   float scale = 0.f;
   cudaStream_t stream = nullptr;
   cudaStream_t stream2 = nullptr;      // second chain of a split step
-  cudaEvent_t ev[6] = {};
+  cudaEvent_t ev[6] = {};          // [0..3] stage events (set 0), [4], [5] step-done per slot
+  cudaEvent_t ev_set1[4] = {};      // stage events of the second in-flight step
+  cudaEvent_t ev_inputs = nullptr;  // the step input upload has been consumed
+  int ev_set = 0;                   // stage-event set the next launch records into
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
 
   // pool
@@ -189,7 +192,10 @@ struct dsd_ctx {
   int* d_planbuf = nullptr;
   int* d_status = nullptr;
   dsdk::StepPlan plan{};
-  float* h_outputs = nullptr;   // pinned D2H staging
+  float* h_outputs = nullptr;   // pinned D2H staging (slot 0; slot 1 below)
+  float* h_outputs1 = nullptr;
+  float* h_scores1 = nullptr;
+  int* h_selected1 = nullptr;
   float* h_scores = nullptr;
   int* h_selected = nullptr;
   int* h_status = nullptr;
@@ -216,6 +222,7 @@ struct dsd_ctx {
     const float* q;
     float* out;
     bool timed;
+    int ev_set;
     cudaGraph_t graph;
     cudaGraphExec_t exec;
   };
@@ -224,11 +231,13 @@ struct dsd_ctx {
   dsd_transfer_stats stats{};
   int dense = 0;   // attend over every candidate (dense baseline) instead of the top-k
 
-  // a step queued by dsd_decode_step_begin, finished by dsd_decode_step_end
+  // steps queued by dsd_decode_step_begin and finished, oldest first, by
+  // dsd_decode_step_end; up to two may be in flight (result staging slots 0/1)
   struct PendingStep {
     bool active = false;
     int batch = 0, total_cand = 0, total_sel = 0, output_mode = 0, timing = 0;
-  } pending;
+  } pend[2];
+  int pend_head = 0, pend_count = 0;
 };
 
 namespace {
@@ -362,8 +371,9 @@ void CheckStatus(dsd_ctx* c) {
 
 void RecordEvent(dsd_ctx* c, int i, bool capturing) {
   // inside a capture the record must become a graph node of its own
-  Check(capturing ? cudaEventRecordWithFlags(c->ev[i], c->stream, cudaEventRecordExternal)
-                  : cudaEventRecord(c->ev[i], c->stream), "event record");
+  cudaEvent_t e = c->ev_set ? c->ev_set1[i] : c->ev[i];
+  Check(capturing ? cudaEventRecordWithFlags(e, c->stream, cudaEventRecordExternal)
+                  : cudaEventRecord(e, c->stream), "event record");
 }
 
 // One decode step.  Untimed steps split the requests into kStepParts ranges
@@ -412,12 +422,12 @@ void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool cap
 // Replays the step as a CUDA graph (captured on first use for this pointer pair).
 void LaunchStepGraph(dsd_ctx* c, const float* d_q, float* d_out, bool timed) {
   for (auto& g : c->graphs) {
-    if (g.q == d_q && g.out == d_out && g.timed == timed) {
+    if (g.q == d_q && g.out == d_out && g.timed == timed && (!timed || g.ev_set == c->ev_set)) {
       Check(cudaGraphLaunch(g.exec, c->stream), "graph launch");
       return;
     }
   }
-  dsd_ctx::StepGraph g{d_q, d_out, timed, nullptr, nullptr};
+  dsd_ctx::StepGraph g{d_q, d_out, timed, c->ev_set, nullptr, nullptr};
   Check(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
   try {
     LaunchStep(c, d_q, d_out, timed, true);
@@ -433,13 +443,14 @@ void LaunchStepGraph(dsd_ctx* c, const float* d_q, float* d_out, bool timed) {
   Check(cudaGraphLaunch(g.exec, c->stream), "graph launch");
 }
 
-void ReadTiming(dsd_ctx* c, dsd_step_timing* t) {
+void ReadTiming(dsd_ctx* c, dsd_step_timing* t, int set = 0) {
   if (!t) return;
-  Check(cudaEventSynchronize(c->ev[3]), "event sync");
-  Check(cudaEventElapsedTime(&t->score_ms, c->ev[0], c->ev[1]), "event time");
-  Check(cudaEventElapsedTime(&t->topk_ms, c->ev[1], c->ev[2]), "event time");
-  Check(cudaEventElapsedTime(&t->attention_ms, c->ev[2], c->ev[3]), "event time");
-  Check(cudaEventElapsedTime(&t->total_ms, c->ev[0], c->ev[3]), "event time");
+  const cudaEvent_t* e = set ? c->ev_set1 : c->ev;
+  Check(cudaEventSynchronize(e[3]), "event sync");
+  Check(cudaEventElapsedTime(&t->score_ms, e[0], e[1]), "event time");
+  Check(cudaEventElapsedTime(&t->topk_ms, e[1], e[2]), "event time");
+  Check(cudaEventElapsedTime(&t->attention_ms, e[2], e[3]), "event time");
+  Check(cudaEventElapsedTime(&t->total_ms, e[0], e[3]), "event time");
 }
 
 // True for page-locked host memory (cudaMallocHost / cudaHostRegister):
@@ -453,6 +464,10 @@ bool IsPinnedHost(const void* p) {
   return a.type == cudaMemoryTypeHost;
 }
 
+// The pinned input staging may be rewritten once the previous step's upload
+// of it has completed (a second step can be queued while one is in flight).
+void WaitInputStaging(dsd_ctx* c) { Check(cudaEventSynchronize(c->ev_inputs), "input staging"); }
+
 int* HdrPtr(dsd_ctx* c) { return reinterpret_cast<int*>(c->h_in); }
 int* ReqPtr(dsd_ctx* c) { return reinterpret_cast<int*>(c->h_in + c->in_req_off); }
 float* QPtr(dsd_ctx* c) { return reinterpret_cast<float*>(c->h_in + c->in_q_off); }
@@ -465,10 +480,11 @@ void UploadQueries(dsd_ctx* c, const float* queries, int batch) {
   if (queries != QPtr(c) && IsPinnedHost(queries)) {
     H2D(c, c->d_in, c->h_in, c->in_q_off);
     H2D(c, c->d_in + c->in_q_off, queries, qbytes);
-    return;
+  } else {
+    if (queries != QPtr(c)) std::memcpy(QPtr(c), queries, qbytes);
+    H2D(c, c->d_in, c->h_in, c->in_q_off + qbytes);
   }
-  if (queries != QPtr(c)) std::memcpy(QPtr(c), queries, qbytes);
-  H2D(c, c->d_in, c->h_in, c->in_q_off + qbytes);
+  Check(cudaEventRecord(c->ev_inputs, c->stream), "event record");
 }
 
 // Common tail of a host-facing step: launch, copy results back, unpack.
@@ -499,30 +515,42 @@ void RunHostStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int outpu
   }
 }
 
-// Queues the step and its result copies into the pinned staging; records
-// ev[4] when everything (status word included) has landed on the host.
+// Queues the step and its result copies into the pinned staging of a free
+// slot; records the slot's done event when everything (status word
+// included) has landed on the host.
 void EnqueueStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int output_mode,
                  int timing) {
+  if (c->pend_count >= 2) Fail(DSD_EINVAL, "two decode steps are already pending");
+  const int slot = (c->pend_head + c->pend_count) & 1;
+  c->ev_set = slot;
   LaunchStepGraph(c, reinterpret_cast<const float*>(c->d_in + c->in_q_off), c->d_outputs,
                   timing != 0);
+  c->ev_set = 0;
+  float* h_out = slot ? c->h_outputs1 : c->h_outputs;
   if (output_mode != DSD_OUTPUT_NONE)
-    D2H(c, c->h_outputs, c->d_outputs, size_t(batch) * c->ept * sizeof(float));
+    D2H(c, h_out, c->d_outputs, size_t(batch) * c->ept * sizeof(float));
   if (output_mode == DSD_OUTPUT_DEBUG) {
-    if (total_cand > 0) D2H(c, c->h_scores, c->d_scores, size_t(total_cand) * sizeof(float));
-    if (total_sel > 0) D2H(c, c->h_selected, c->d_selected, size_t(total_sel) * sizeof(int));
+    if (total_cand > 0)
+      D2H(c, slot ? c->h_scores1 : c->h_scores, c->d_scores, size_t(total_cand) * sizeof(float));
+    if (total_sel > 0)
+      D2H(c, slot ? c->h_selected1 : c->h_selected, c->d_selected, size_t(total_sel) * sizeof(int));
   }
   Check(cudaMemcpyAsync(c->h_status, c->d_status, sizeof(int), cudaMemcpyDeviceToHost, c->stream),
         "status read");
-  Check(cudaEventRecord(c->ev[4], c->stream), "event record");
-  c->pending = dsd_ctx::PendingStep{true, batch, total_cand, total_sel, output_mode, timing};
+  Check(cudaEventRecord(c->ev[4 + slot], c->stream), "event record");
+  c->pend[slot] = dsd_ctx::PendingStep{true, batch, total_cand, total_sel, output_mode, timing};
+  ++c->pend_count;
 }
 
 void FinishStep(dsd_ctx* c, float* outputs, float* scores, int32_t* selected,
                 dsd_step_timing* out_timing) {
-  if (!c->pending.active) Fail(DSD_EINVAL, "no decode step is pending");
-  const auto p = c->pending;
-  c->pending.active = false;
-  Check(cudaEventSynchronize(c->ev[4]), "step wait");
+  if (c->pend_count == 0) Fail(DSD_EINVAL, "no decode step is pending");
+  const int slot = c->pend_head;
+  const auto p = c->pend[slot];
+  c->pend[slot].active = false;
+  c->pend_head ^= 1;
+  --c->pend_count;
+  Check(cudaEventSynchronize(c->ev[4 + slot]), "step wait");
   const int st = *c->h_status;
   if (st != 0) {
     Check(cudaMemsetAsync(c->d_status, 0, sizeof(int), c->stream), "status clear");
@@ -530,14 +558,16 @@ void FinishStep(dsd_ctx* c, float* outputs, float* scores, int32_t* selected,
     if (st & dsdk::kStatusTimeout) Fail(DSD_ETIMEOUT, "a device-side wait exceeded its budget");
     Fail(DSD_EINVAL, "device kernels rejected the step input (status " + std::to_string(st) + ")");
   }
-  if (p.timing) ReadTiming(c, out_timing);
-  if (p.output_mode != DSD_OUTPUT_NONE && outputs && outputs != c->h_outputs)
-    std::memcpy(outputs, c->h_outputs, size_t(p.batch) * c->ept * sizeof(float));
+  if (p.timing) ReadTiming(c, out_timing, slot);
+  const float* h_out = slot ? c->h_outputs1 : c->h_outputs;
+  if (p.output_mode != DSD_OUTPUT_NONE && outputs && outputs != h_out)
+    std::memcpy(outputs, h_out, size_t(p.batch) * c->ept * sizeof(float));
   if (p.output_mode == DSD_OUTPUT_DEBUG) {
     if (scores && p.total_cand > 0)
-      std::memcpy(scores, c->h_scores, size_t(p.total_cand) * sizeof(float));
+      std::memcpy(scores, slot ? c->h_scores1 : c->h_scores, size_t(p.total_cand) * sizeof(float));
     if (selected && p.total_sel > 0)
-      std::memcpy(selected, c->h_selected, size_t(p.total_sel) * sizeof(int));
+      std::memcpy(selected, slot ? c->h_selected1 : c->h_selected,
+                  size_t(p.total_sel) * sizeof(int));
   }
 }
 
@@ -625,7 +655,7 @@ int dsd_kernels_per_step(void) { return 5; }
 int dsd_set_attention_mode(dsd_ctx* c, int dense) {
   return Guard([&]() {
     if (!c) Fail(DSD_EINVAL, "null context");
-    if (c->pending.active) Fail(DSD_EINVAL, "a decode step is pending");
+    if (c->pend_count) Fail(DSD_EINVAL, "a decode step is pending");
     c->dense = dense ? 1 : 0;
   });
 }
@@ -679,6 +709,8 @@ int dsd_ctx_create(int device, const dsd_model_config* config, const dsd_ctx_opt
       c->scale = 1.0f / std::sqrt(static_cast<float>(D));
       Check(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream");
       for (auto& e : c->ev) Check(cudaEventCreate(&e), "event");
+      for (auto& e : c->ev_set1) Check(cudaEventCreate(&e), "event");
+      Check(cudaEventCreateWithFlags(&c->ev_inputs, cudaEventDisableTiming), "event");
       Check(cudaStreamCreateWithFlags(&c->stream2, cudaStreamNonBlocking), "stream");
       Check(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming), "event");
       Check(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming), "event");
@@ -725,6 +757,9 @@ int dsd_ctx_create(int device, const dsd_model_config* config, const dsd_ctx_opt
       c->d_status = DeviceAlloc<int>(1, "status word");
       Check(cudaMemsetAsync(c->d_status, 0, 4, c->stream), "memset");
       c->h_outputs = PinnedAlloc<float>(size_t(mb) * ept, "output staging");
+      c->h_outputs1 = PinnedAlloc<float>(size_t(mb) * ept, "output staging");
+      c->h_scores1 = PinnedAlloc<float>(mc, "score staging");
+      c->h_selected1 = PinnedAlloc<int>(ms, "selected staging");
       c->h_scores = PinnedAlloc<float>(mc, "score staging");
       c->h_selected = PinnedAlloc<int>(ms, "selected staging");
       c->h_status = PinnedAlloc<int>(1, "status staging");
@@ -781,11 +816,15 @@ int dsd_ctx_destroy(dsd_ctx* c) {
                  c->d_part_ml, c->d_planbuf, c->d_status, c->d_stage};
   for (void* p : dev)
     if (p) cudaFree(p);
-  void* host[] = {c->h_in, c->h_outputs, c->h_scores, c->h_selected, c->h_status};
+  void* host[] = {c->h_in, c->h_outputs, c->h_scores, c->h_selected, c->h_status,
+                  c->h_outputs1, c->h_scores1, c->h_selected1};
   for (void* p : host)
     if (p) cudaFreeHost(p);
   for (auto& e : c->ev)
     if (e) cudaEventDestroy(e);
+  for (auto& e : c->ev_set1)
+    if (e) cudaEventDestroy(e);
+  if (c->ev_inputs) cudaEventDestroy(c->ev_inputs);
   if (c->ev_fork) cudaEventDestroy(c->ev_fork);
   if (c->ev_join) cudaEventDestroy(c->ev_join);
   if (c->stream2) cudaStreamDestroy(c->stream2);
@@ -806,6 +845,14 @@ int dsd_ctx_device_pointers(dsd_ctx* c, float** keys, float** values, float** su
 }
 
 void* dsd_ctx_stream(dsd_ctx* c) { return c ? static_cast<void*>(c->stream) : nullptr; }
+
+int dsd_step_staging_wait(dsd_ctx* c) {
+  return Guard([&]() {
+    if (!c) Fail(DSD_EINVAL, "null context");
+    SetDevice(c);
+    WaitInputStaging(c);
+  });
+}
 
 int dsd_step_host_buffers(dsd_ctx* c, float** queries, float** outputs) {
   return Guard([&]() {
@@ -1165,6 +1212,7 @@ int dsd_decode_batch(dsd_ctx* c, int batch, const float* queries, const int32_t*
       Fail(DSD_EINVAL, "selected page count exceeds sparse CUDA context capacity");
     for (int i = 0; i < total_cand; ++i) ValidatePage(c, cand_ids[i]);
     SetDevice(c);
+    WaitInputStaging(c);
     int* hdr = HdrPtr(c);
     hdr[0] = batch;
     hdr[1] = 0;
@@ -1243,6 +1291,7 @@ namespace {
 void PackSlots(dsd_ctx* c, const int32_t* request_ids, int batch, int* total_cand,
                int* total_sel) {
   if (batch > c->opt.max_batch) Fail(DSD_EINVAL, "request batch exceeds sparse CUDA context capacity");
+  WaitInputStaging(c);
   int* req = ReqPtr(c);
   int tc = 0, ts = 0;
   for (int r = 0; r < batch; ++r) {
@@ -1288,7 +1337,7 @@ int dsd_decode_step_begin(dsd_ctx* c, const int32_t* request_ids, int batch,
   return Guard([&]() {
     if (!c) Fail(DSD_EINVAL, "null context");
     RequireTables(c);
-    if (c->pending.active) Fail(DSD_EINVAL, "a decode step is already pending");
+    if (c->pend_count >= 2) Fail(DSD_EINVAL, "two decode steps are already pending");
     if (batch <= 0) Fail(DSD_EINVAL, "empty batch");
     if (!queries || !request_ids) Fail(DSD_EINVAL, "null step input");
     SetDevice(c);

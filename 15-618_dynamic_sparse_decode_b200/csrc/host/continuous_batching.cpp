@@ -323,6 +323,18 @@ ContinuousBatchStats RunContinuous(const ModelConfig& config,
 
   std::size_t next = 0;
   int step = 0;
+  std::deque<Clock::time_point> step_starts;
+  // Waits for the oldest queued step; its wall time runs from its BeginStep
+  // to the moment its results are back on the host.
+  auto finish_oldest = [&]() {
+    const auto out = ctx.FinishStep();
+    const double ms = Ms(step_starts.front(), Clock::now());
+    step_starts.pop_front();
+    stats.run_batch_wall_ms += ms;
+    step_ms.push_back(ms);
+    Add(&timings_sum, out.aggregate_timings);
+    Add(&overhead_sum, out.runtime_overheads);
+  };
   const auto wall0 = Clock::now();
   std::vector<int> up_pages, up_offs, up_reqs, up_steps;
   std::vector<float> up_k, up_v;
@@ -366,27 +378,24 @@ ContinuousBatchStats RunContinuous(const ModelConfig& config,
       continue;
     }
 
-    const auto s0 = Clock::now();
     batch.clear();
     for (const auto& a : active) batch.push_back(&a.state);
-    // With device page tables the step is queued asynchronously: the host
-    // bookkeeping of this step's token appends (and their uploads, ordered
-    // after the step on the same stream) overlaps the GPU work.
-    SparseBatchCudaResult out;
+    // With device page tables steps are queued asynchronously and up to two
+    // are in flight: the host bookkeeping of this step's token appends, its
+    // releases and the next step's admission overlap the GPU work (every
+    // upload is ordered after the step on the context stream).
     if (tables) {
+      step_starts.push_back(Clock::now());
       ctx.BeginStep(batch, run_opts);
     } else {
-      out = ctx.RunBatch(batch, run_opts);
-    }
-    auto finish_step = [&]() {
-      if (tables) out = ctx.FinishStep();
+      const auto s0 = Clock::now();
+      const auto out = ctx.RunBatch(batch, run_opts);
       const double ms = Ms(s0, Clock::now());
       stats.run_batch_wall_ms += ms;
       step_ms.push_back(ms);
       Add(&timings_sum, out.aggregate_timings);
       Add(&overhead_sum, out.runtime_overheads);
-    };
-    if (!tables) finish_step();
+    }
     ++nonempty;
     active_sum += static_cast<int>(active.size());
 
@@ -482,7 +491,7 @@ ContinuousBatchStats RunContinuous(const ModelConfig& config,
         for (const auto& np : new_pages) ctx.AppendRequestPages(np.first, {np.second});
     }
     stats.append_sync_ms += Ms(a0, Clock::now());
-    if (tables) finish_step();
+    if (tables && ctx.PendingSteps() == 2) finish_oldest();
 
     std::vector<PageId> released;
     active.erase(std::remove_if(active.begin(), active.end(),
@@ -500,6 +509,7 @@ ContinuousBatchStats RunContinuous(const ModelConfig& config,
     ++step;
   }
 
+  while (tables && ctx.PendingSteps() > 0) finish_oldest();
   stats.total_wall_ms = Ms(wall0, Clock::now());
   stats.tokens_per_second = stats.total_wall_ms > 0.0
                                 ? stats.total_generated_tokens / (stats.total_wall_ms / 1000.0)

@@ -210,57 +210,60 @@ void SparseCudaContext::BeginStep(const std::vector<const RequestState*>& reques
                                   SparseRunBatchOptions options) {
   if (!HasRequestTables())
     throw std::invalid_argument("context was created without device request page tables");
-  if (pending_) throw std::invalid_argument("a step is already pending");
+  if (pending_.size() >= 2) throw std::invalid_argument("two steps are already pending");
   const int B = static_cast<int>(requests.size());
   if (B == 0) throw std::invalid_argument("empty batch");
   if (B > max_batch_size_)
     throw std::invalid_argument("request batch exceeds sparse CUDA context capacity");
   const int ept = elements_per_token_;
+  const bool debug = options.output_mode == SparseBatchOutputMode::kDebugTensors;
   const auto t0 = std::chrono::steady_clock::now();
-  pending_sel_off_.assign(static_cast<std::size_t>(B) + 1, 0);
-  offsets_.assign(1, 0);
-  request_ids_.clear();
+  PendingStep ps;
+  ps.options = options;
+  ps.sel_off.assign(static_cast<std::size_t>(B) + 1, 0);
+  ps.cand_off.assign(1, 0);
   for (int r = 0; r < B; ++r) {
     const RequestState* q = requests[static_cast<std::size_t>(r)];
     if (!q) throw std::invalid_argument("request pointer must be non-null");
     if (static_cast<int>(q->query.size()) != ept)
       throw std::invalid_argument("query length does not match model config");
-    request_ids_.push_back(q->request_id);
+    ps.request_ids.push_back(q->request_id);
+    if (debug) ps.candidates.push_back(q->candidate_page_ids);
     const int n = std::max(0, dsd_request_num_pages(ctx_, q->request_id));
-    offsets_.push_back(offsets_.back() + n);
-    pending_sel_off_[static_cast<std::size_t>(r) + 1] =
-        pending_sel_off_[static_cast<std::size_t>(r)] + std::min(config_.top_k_pages, n);
+    ps.cand_off.push_back(ps.cand_off.back() + n);
+    ps.sel_off[static_cast<std::size_t>(r) + 1] =
+        ps.sel_off[static_cast<std::size_t>(r)] + std::min(config_.top_k_pages, n);
   }
-  if (offsets_.back() > max_total_candidates_)
+  if (ps.cand_off.back() > max_total_candidates_)
     throw std::invalid_argument("candidate page count exceeds sparse CUDA context capacity");
-  if (pending_sel_off_.back() > max_total_selected_pages_)
+  if (ps.sel_off.back() > max_total_selected_pages_)
     throw std::invalid_argument("selected page count exceeds sparse CUDA context capacity");
+  ThrowIf(dsd_step_staging_wait(ctx_));   // the staging may still feed the previous step
   PackQueries(requests);
-  pending_prep_ms_ =
+  ps.prep_ms =
       std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   const int mode = options.output_mode == SparseBatchOutputMode::kNoOutputs ? DSD_OUTPUT_NONE
-                   : options.output_mode == SparseBatchOutputMode::kDebugTensors
-                       ? DSD_OUTPUT_DEBUG : DSD_OUTPUT_OUTPUTS;
+                   : debug ? DSD_OUTPUT_DEBUG : DSD_OUTPUT_OUTPUTS;
   const bool timed = options.timing_mode == SparseBatchTimingMode::kKernelEvents;
-  ThrowIf(dsd_decode_step_begin(ctx_, request_ids_.data(), B, host_queries_, mode, timed ? 1 : 0));
-  pending_requests_ = requests;
-  pending_options_ = options;
-  pending_ = true;
+  ThrowIf(dsd_decode_step_begin(ctx_, ps.request_ids.data(), B, host_queries_, mode,
+                                timed ? 1 : 0));
+  pending_.push_back(std::move(ps));
 }
 
 SparseBatchCudaResult SparseCudaContext::FinishStep() {
-  if (!pending_) throw std::invalid_argument("no step is pending");
-  pending_ = false;
-  const auto& requests = pending_requests_;
-  const int B = static_cast<int>(requests.size());
+  if (pending_.empty()) throw std::invalid_argument("no step is pending");
+  PendingStep ps = std::move(pending_.front());
+  pending_.erase(pending_.begin());
+  const int B = static_cast<int>(ps.request_ids.size());
   const int ept = elements_per_token_;
-  const bool debug = pending_options_.output_mode == SparseBatchOutputMode::kDebugTensors;
-  const bool timed = pending_options_.timing_mode == SparseBatchTimingMode::kKernelEvents;
-  scores_.resize(static_cast<std::size_t>(std::max(1, offsets_.back())));
-  selected_.resize(static_cast<std::size_t>(std::max(1, pending_sel_off_.back())));
+  const bool debug = ps.options.output_mode == SparseBatchOutputMode::kDebugTensors;
+  const bool timed = ps.options.timing_mode == SparseBatchTimingMode::kKernelEvents;
+  scores_.resize(static_cast<std::size_t>(std::max(1, ps.cand_off.back())));
+  selected_.resize(static_cast<std::size_t>(std::max(1, ps.sel_off.back())));
+  finish_outputs_.resize(static_cast<std::size_t>(B) * ept);
   dsd_step_timing st{};
   const auto t0 = std::chrono::steady_clock::now();
-  ThrowIf(dsd_decode_step_end(ctx_, host_outputs_, scores_.data(), selected_.data(), &st));
+  ThrowIf(dsd_decode_step_end(ctx_, finish_outputs_.data(), scores_.data(), selected_.data(), &st));
   SparseBatchCudaResult result;
   if (timed) {
     result.aggregate_timings.page_scoring_ms = st.score_ms;
@@ -268,26 +271,27 @@ SparseBatchCudaResult SparseCudaContext::FinishStep() {
     result.aggregate_timings.attention_ms = st.attention_ms;
     result.aggregate_timings.total_ms = st.score_ms + st.topk_ms + st.attention_ms;
     result.kernel_ms = result.aggregate_timings.total_ms;
-    result.runtime_overheads.time_prepare_sparse_layout_ms = pending_prep_ms_;
+    result.runtime_overheads.time_prepare_sparse_layout_ms = ps.prep_ms;
     result.runtime_overheads.time_sync_ms =
         std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   }
-  if (pending_options_.output_mode == SparseBatchOutputMode::kNoOutputs) return result;
+  if (ps.options.output_mode == SparseBatchOutputMode::kNoOutputs) return result;
   result.per_request.reserve(static_cast<std::size_t>(B));
   for (int r = 0; r < B; ++r) {
     SparseDecodeResult one;
-    one.request_id = requests[static_cast<std::size_t>(r)]->request_id;
+    one.request_id = ps.request_ids[static_cast<std::size_t>(r)];
     if (debug) {
-      const auto& cand = requests[static_cast<std::size_t>(r)]->candidate_page_ids;
-      for (int c = offsets_[static_cast<std::size_t>(r)]; c < offsets_[static_cast<std::size_t>(r) + 1]; ++c) {
-        const std::size_t i = static_cast<std::size_t>(c - offsets_[static_cast<std::size_t>(r)]);
+      const auto& cand = ps.candidates[static_cast<std::size_t>(r)];
+      const int c0 = ps.cand_off[static_cast<std::size_t>(r)];
+      for (int c = c0; c < ps.cand_off[static_cast<std::size_t>(r) + 1]; ++c) {
+        const std::size_t i = static_cast<std::size_t>(c - c0);
         one.scores.push_back(PageScore{i < cand.size() ? cand[i] : -1, scores_[static_cast<std::size_t>(c)]});
       }
-      one.selected_page_ids.assign(selected_.begin() + pending_sel_off_[static_cast<std::size_t>(r)],
-                                   selected_.begin() + pending_sel_off_[static_cast<std::size_t>(r) + 1]);
+      one.selected_page_ids.assign(selected_.begin() + ps.sel_off[static_cast<std::size_t>(r)],
+                                   selected_.begin() + ps.sel_off[static_cast<std::size_t>(r) + 1]);
     }
-    one.output.output.assign(host_outputs_ + static_cast<std::ptrdiff_t>(r) * ept,
-                             host_outputs_ + static_cast<std::ptrdiff_t>(r + 1) * ept);
+    one.output.output.assign(finish_outputs_.begin() + static_cast<std::ptrdiff_t>(r) * ept,
+                             finish_outputs_.begin() + static_cast<std::ptrdiff_t>(r + 1) * ept);
     result.per_request.push_back(std::move(one));
   }
   return result;

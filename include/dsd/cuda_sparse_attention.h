@@ -78,9 +78,10 @@ class SparseCudaContext {
                                 SparseRunBatchOptions options);
 
   // RunStep split in two: BeginStep uploads the queries and queues the step;
-  // host work and further uploads on this context (appends, frees) may
-  // follow before FinishStep waits for the results.  `requests` must stay
-  // alive until FinishStep.
+  // host work and further uploads on this context (appends, frees, the next
+  // BeginStep) may follow before FinishStep waits for the OLDEST pending
+  // step's results.  Up to two steps may be pending; the requests are copied
+  // as needed, so they may change after BeginStep returns.
   void BeginStep(const std::vector<const RequestState*>& requests, SparseRunBatchOptions options);
   SparseBatchCudaResult FinishStep();
 
@@ -110,6 +111,7 @@ class SparseCudaContext {
   void AppendRequestPages(int request_id, const std::vector<PageId>& page_ids);
   void ReleaseRequestPages(int request_id, bool free_pages);
   bool HasRequestTables() const { return max_requests_ > 0; }
+  int PendingSteps() const { return static_cast<int>(pending_.size()); }
 
   DevicePagePool& device_pool() { return *pool_; }
   dsd_ctx* handle() const { return ctx_; }
@@ -131,12 +133,16 @@ class SparseCudaContext {
   float* host_outputs_ = nullptr;
   std::vector<int> offsets_, ids_, request_ids_, selected_;
   std::vector<float> scores_;
-  // pending BeginStep
-  std::vector<const RequestState*> pending_requests_;
-  std::vector<int> pending_sel_off_;
-  SparseRunBatchOptions pending_options_;
-  double pending_prep_ms_ = 0.0;
-  bool pending_ = false;
+  std::vector<float> finish_outputs_;
+  // steps queued by BeginStep, oldest first
+  struct PendingStep {
+    std::vector<int> request_ids;
+    std::vector<std::vector<PageId>> candidates;   // debug mode only
+    std::vector<int> cand_off, sel_off;
+    SparseRunBatchOptions options;
+    double prep_ms = 0.0;
+  };
+  std::vector<PendingStep> pending_;
   std::unique_ptr<detail::WorkerPool> pack_pool_;   // parallel query packing
   void PackQueries(const std::vector<const RequestState*>& requests);
 };

@@ -103,6 +103,9 @@ void* dsd_ctx_stream(dsd_ctx* ctx);
  * dsd_decode_batch / dsd_decode_step skips one host copy each way.  Valid
  * until the context is destroyed; the next step overwrites them. */
 int dsd_step_host_buffers(dsd_ctx* ctx, float** queries, float** outputs);
+/* Waits until the previous step's upload of the pinned query staging has
+ * completed; call before writing the staging while a step is in flight. */
+int dsd_step_staging_wait(dsd_ctx* ctx);
 
 /* DevicePagePool::Reset (src/device_page_pool.cpp:286-302): zero counts, live
  * flags and summaries; drop every request page table. */
@@ -194,10 +197,11 @@ int dsd_decode_step(dsd_ctx* ctx, const int32_t* request_ids, int batch, const f
 
 /* The same step split in two, so the caller's host work overlaps the GPU:
  * begin uploads the queries and queues the step and its result copies;
- * end waits and returns the results (copied out of the context's pinned
- * staging, see dsd_step_host_buffers).  Work the caller queues on this
- * context between the two (token appends, frees) runs after the step on
- * the GPU.  One step may be pending at a time. */
+ * end waits for the OLDEST pending step and returns its results (copied out
+ * of the context's pinned staging).  Work the caller queues on this context
+ * in between (token appends, frees, the next begin) runs after the step on
+ * the GPU.  Up to two steps may be pending; pinned caller queries passed to
+ * begin must stay unchanged until the step ends. */
 int dsd_decode_step_begin(dsd_ctx* ctx, const int32_t* request_ids, int batch,
                           const float* queries, int output_mode, int timing);
 int dsd_decode_step_end(dsd_ctx* ctx, float* outputs, float* scores, int32_t* selected,

@@ -63,7 +63,7 @@ class HostMirror:
 
 
 def run_continuous(dsd, H, D, P, K, n_req, max_active, window, pmin, pmax, dmin, dmax, seed,
-                   split_step=False):
+                   split_step=False, depth=1):
     E = H * D
     w = o.continuous_workload(H, D, n_req, window, pmin, pmax, dmin, dmax, seed)
     ids, arr, pt, ds = w["request_ids"], w["arrival_steps"], w["prompt_tokens"], w["decode_steps"]
@@ -78,6 +78,14 @@ def run_continuous(dsd, H, D, P, K, n_req, max_active, window, pmin, pmax, dmin,
                                   max_pages_per_request=max_pages)
     active = []            # dicts: rid, remaining, step, query
     nxt, step, checked = 0, 0, 0
+    inflight = []          # oracle results of steps begun but not yet ended
+
+    def end_oldest():
+        res = ctx.decode_step_end()
+        sel, out, scores, at = inflight.pop(0)
+        assert np.array_equal(res["scores"].view(np.uint32), scores.view(np.uint32)), at
+        assert np.array_equal(res["selected"], sel), at
+        assert float(np.abs(res["outputs"] - out).max()) <= 1e-4, at
     order = list(range(n_req))
     pending = []
     while nxt < n_req or pending or active:
@@ -122,7 +130,7 @@ def run_continuous(dsd, H, D, P, K, n_req, max_active, window, pmin, pmax, dmin,
                     np.concatenate(cand))
         sel, so, out, scores = o.sparse_decode(b)
         if split_step:
-            pending_check = (sel, out, scores)
+            inflight.append((sel, out, scores, step))
         else:
             assert np.array_equal(res["scores"].view(np.uint32), scores.view(np.uint32)), step
             assert np.array_equal(res["selected"], sel), step
@@ -142,25 +150,25 @@ def run_continuous(dsd, H, D, P, K, n_req, max_active, window, pmin, pmax, dmin,
             a["remaining"] -= 1
         if up_p:
             ctx.append_tokens(up_p, up_o, np.stack(up_k), np.stack(up_v), request_ids=up_r)
-        if split_step:
-            # the appends were queued while the step was pending: it must not see them
-            res = ctx.decode_step_end()
-            sel, out, scores = pending_check
-            assert np.array_equal(res["scores"].view(np.uint32), scores.view(np.uint32)), step
-            assert np.array_equal(res["selected"], sel), step
-            assert float(np.abs(res["outputs"] - out).max()) <= 1e-4, step
+        if split_step and len(inflight) >= depth:
+            # the appends (and, at depth 2, the next step) were queued while the
+            # step was pending: it must not see them
+            end_oldest()
         for a in [a for a in active if a["remaining"] == 0]:
             ctx.release_request(a["rid"], free_pages=True)
             host.release(a["rid"])
         active = [a for a in active if a["remaining"] > 0]
         step += 1
+    while inflight:
+        end_oldest()
     ctx.close()
     return checked
 
 
-@pytest.mark.parametrize("split_step", [False, True], ids=["sync_step", "begin_end_step"])
-def test_continuous_small_shapes(dsd, split_step):
-    assert run_continuous(dsd, 4, 16, 8, 3, 10, 4, 6, 20, 60, 3, 10, 7, split_step) > 5
+@pytest.mark.parametrize("split_step,depth", [(False, 1), (True, 1), (True, 2)],
+                         ids=["sync_step", "begin_end_step", "two_steps_in_flight"])
+def test_continuous_small_shapes(dsd, split_step, depth):
+    assert run_continuous(dsd, 4, 16, 8, 3, 10, 4, 6, 20, 60, 3, 10, 7, split_step, depth) > 5
 
 
 def test_continuous_config4_shape(dsd):
