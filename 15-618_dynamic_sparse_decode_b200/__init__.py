@@ -21,6 +21,7 @@ LIB_PATH = os.path.join(PKG_DIR, "libdsd_b200.so")
 
 DSD_OK, DSD_EINVAL, DSD_ERANGE, DSD_ENOMEM, DSD_ECUDA, DSD_ETIMEOUT, DSD_EUNAVAILABLE = range(7)
 OUTPUT_NONE, OUTPUT_OUTPUTS, OUTPUT_DEBUG = 0, 1, 2
+KV_F32, KV_BF16 = 0, 1
 
 _I32P = ctypes.POINTER(ctypes.c_int32)
 _F32P = ctypes.POINTER(ctypes.c_float)
@@ -57,6 +58,10 @@ SIGNATURES = [
     ("dsd_ctx_create", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ModelConfig),
                                       ctypes.POINTER(CtxOptions), ctypes.POINTER(_VP)]),
     ("dsd_ctx_destroy", ctypes.c_int, [_VP]),
+    ("dsd_ctx_create_ex", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ModelConfig),
+                                         ctypes.POINTER(CtxOptions), ctypes.c_int,
+                                         ctypes.POINTER(_VP)]),
+    ("dsd_ctx_kv_format", ctypes.c_int, [_VP]),
     ("dsd_ctx_device_pointers", ctypes.c_int, [_VP, ctypes.POINTER(_VP), ctypes.POINTER(_VP),
                                                ctypes.POINTER(_VP), ctypes.POINTER(_VP)]),
     ("dsd_ctx_stream", _VP, [_VP]),
@@ -185,16 +190,20 @@ class SparseDecodeContext:
 
     def __init__(self, num_heads, head_dim, page_size, top_k_pages, capacity_pages, max_batch,
                  max_candidates, max_selected, max_requests=0, max_pages_per_request=0,
-                 device=0):
+                 device=0, kv_format=KV_F32):
+        """kv_format: KV_F32 (the reference's fp32 pages) or KV_BF16 (pages and
+        summaries stored as bf16, arithmetic in fp32; payloads in and
+        downloads out stay float32 arrays)."""
         self.lib = load_library()
         self.cfg = ModelConfig(num_heads, head_dim, page_size, top_k_pages)
         self.opt = CtxOptions(capacity_pages, max_batch, max_candidates, max_selected,
                               max_requests, max_pages_per_request)
         self.ept = num_heads * head_dim
         h = _VP()
-        _check(self.lib.dsd_ctx_create(device, ctypes.byref(self.cfg), ctypes.byref(self.opt),
-                                       ctypes.byref(h)))
+        _check(self.lib.dsd_ctx_create_ex(device, ctypes.byref(self.cfg), ctypes.byref(self.opt),
+                                          int(kv_format), ctypes.byref(h)))
         self.h = h
+        self.kv_format = int(kv_format)
 
     def close(self):
         if getattr(self, "h", None):

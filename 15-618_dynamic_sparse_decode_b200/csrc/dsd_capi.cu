@@ -13,6 +13,7 @@
 #include <cstring>
 #include <mutex>
 #include <thread>
+#include <type_traits>
 #include <stdexcept>
 #include <string>
 #include <unordered_map>
@@ -91,9 +92,22 @@ struct AttnShape {
   size_t smem = 0;
 };
 
-AttnShape MakeAttnShape(int num_heads, int head_dim, int page_size) {
+AttnShape MakeAttnShape(int num_heads, int head_dim, int page_size, bool bf16 = false) {
   AttnShape a;
   const int ept = num_heads * head_dim;
+  if (bf16) {
+    // 16-byte vectors of 8 bf16: NV = 2 for head_dim >= 16, 1 for head_dim 8
+    const int G = head_dim / 8;
+    a.nv = G >= 2 ? 2 : 1;
+    const int items = num_heads * (G / a.nv);
+    const int slots = (items + dsdk::kAttnThreads - 1) / dsdk::kAttnThreads;
+    if (slots > 4) Fail(DSD_EINVAL, "num_heads*head_dim is too large for the attention kernel");
+    a.slots = slots <= 1 ? 1 : slots <= 2 ? 2 : 4;
+    a.tps = std::max(1, std::min({page_size, dsdk::kAttnStageFloats * 4 / (2 * ept * 2),
+                                  dsdk::kAttnMaxTokensPerStage}));
+    a.smem = size_t(dsdk::kAttnStages) * 2 * a.tps * ept * 2 + dsdk::kAttnStages * 8;
+    return a;
+  }
   const int G = head_dim / 4;
   a.nv = G >= 4 ? 4 : G;
   const int items = num_heads * (G / a.nv);
@@ -119,6 +133,35 @@ void SetAllAttnAttributes(size_t smem) {
   SetAttnAttr<1, 1>(smem); SetAttnAttr<1, 2>(smem); SetAttnAttr<1, 4>(smem); SetAttnAttr<1, 8>(smem);
   SetAttnAttr<2, 1>(smem); SetAttnAttr<2, 2>(smem); SetAttnAttr<2, 4>(smem);
   SetAttnAttr<4, 1>(smem); SetAttnAttr<4, 2>(smem);
+}
+
+template <int NV, int S>
+void SetAttnAttrBf16(size_t smem) {
+  Check(cudaFuncSetAttribute(dsdk::attn_kernel_bf16<NV, S>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+        "smem attribute");
+}
+
+// bf16 pages: NV = 1 serves head_dim 8 (<= 1024 items), NV = 2 the rest (<= 512).
+void SetAllAttnAttributesBf16(size_t smem) {
+  SetAttnAttrBf16<1, 1>(smem); SetAttnAttrBf16<1, 2>(smem); SetAttnAttrBf16<1, 4>(smem);
+  SetAttnAttrBf16<2, 1>(smem); SetAttnAttrBf16<2, 2>(smem);
+}
+
+void LaunchAttnBf16(const AttnShape& a, int grid, cudaStream_t st, const dsdk::StepPlan& plan,
+                    const float* q, const __nv_bfloat16* k, const __nv_bfloat16* v, const int* tc,
+                    const int* sel, float* pacc, float* pml, int H, int D, int P, float scale,
+                    int part, int nparts) {
+#define DSD_ATTN_CASE(NV, S)                                                                  \
+  if (a.nv == NV && a.slots == S) {                                                           \
+    dsdk::attn_kernel_bf16<NV, S><<<grid, dsdk::kAttnThreads, a.smem, st>>>(                  \
+        plan, q, k, v, tc, sel, pacc, pml, H, D, P, a.tps, scale, part, nparts);              \
+    return;                                                                                   \
+  }
+  DSD_ATTN_CASE(1, 1) DSD_ATTN_CASE(1, 2) DSD_ATTN_CASE(1, 4)
+  DSD_ATTN_CASE(2, 1) DSD_ATTN_CASE(2, 2)
+#undef DSD_ATTN_CASE
+  Fail(DSD_EINVAL, "unsupported attention shape");
 }
 
 template <int NV, int S>
@@ -148,6 +191,9 @@ void LaunchAttn(const AttnShape& a, int grid, cudaStream_t st, const dsdk::StepP
 
 }  // namespace
 
+template <typename T>
+struct KvTag { using type = T; };
+
 struct dsd_ctx {
   int device = 0;
   dsd_model_config cfg{};
@@ -164,10 +210,12 @@ struct dsd_ctx {
   int ev_set = 0;                   // stage-event set the next launch records into
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
 
-  // pool
-  float* k_pool = nullptr;
-  float* v_pool = nullptr;
-  float* summaries = nullptr;     // chunk-major in 128-page groups (see summary_off)
+  // pool: fp32 or bf16 elements (kv_format); summary_floats counts elements
+  int kv_format = DSD_KV_F32;
+  size_t kv_elem = 4;
+  void* k_pool = nullptr;
+  void* v_pool = nullptr;
+  void* summaries = nullptr;      // chunk-major in 128-page groups (see summary_off)
   size_t summary_floats = 0;
   int* token_counts = nullptr;
   uint8_t* live = nullptr;
@@ -239,6 +287,13 @@ struct dsd_ctx {
   } pend[2];
   int pend_head = 0, pend_count = 0;
 };
+
+// Calls f(KvTag<T>{}) with T the context's page element type.
+template <typename F>
+void WithKv(const dsd_ctx* c, F&& f) {
+  if (c->kv_format == DSD_KV_BF16) f(KvTag<__nv_bfloat16>{});
+  else f(KvTag<float>{});
+}
 
 namespace {
 
@@ -400,14 +455,27 @@ void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool cap
   }
   for (int part = 0; part < nparts; ++part) {
     cudaStream_t st = part == 0 ? c->stream : c->stream2;
-    dsdk::score_kernel<<<2 * c->num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, st>>>(
-        plan, d_q, c->summaries, c->ept, c->scale, c->d_scores, part, nparts);
+    if (c->kv_format == DSD_KV_BF16)
+      dsdk::score_kernel_bf16<<<2 * c->num_sms, dsdk::kScoreThreads, dsdk::kScoreBfSmem, st>>>(
+          plan, d_q, static_cast<const __nv_bfloat16*>(c->summaries), c->ept, c->scale,
+          c->d_scores, part, nparts);
+    else
+      dsdk::score_kernel<<<2 * c->num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, st>>>(
+          plan, d_q, static_cast<const float*>(c->summaries), c->ept, c->scale, c->d_scores,
+          part, nparts);
     if (timed) RecordEvent(c, 1, capturing);
     dsdk::select_kernel<<<sel_grid, dsdk::kSelectThreads, dsdk::kSelectSmem, st>>>(
         plan, c->d_scores, c->d_selected, part, nparts);
     if (timed) RecordEvent(c, 2, capturing);
-    LaunchAttn(c->attn, c->num_sms, st, plan, d_q, c->k_pool, c->v_pool, c->token_counts,
-               c->d_selected, c->d_part_acc, c->d_part_ml, H, D, P, c->scale, part, nparts);
+    if (c->kv_format == DSD_KV_BF16)
+      LaunchAttnBf16(c->attn, c->num_sms, st, plan, d_q,
+                     static_cast<const __nv_bfloat16*>(c->k_pool),
+                     static_cast<const __nv_bfloat16*>(c->v_pool), c->token_counts, c->d_selected,
+                     c->d_part_acc, c->d_part_ml, H, D, P, c->scale, part, nparts);
+    else
+      LaunchAttn(c->attn, c->num_sms, st, plan, d_q, static_cast<const float*>(c->k_pool),
+                 static_cast<const float*>(c->v_pool), c->token_counts, c->d_selected,
+                 c->d_part_acc, c->d_part_ml, H, D, P, c->scale, part, nparts);
     dsdk::combine_kernel<<<comb_grid, 256, 0, st>>>(plan, c->d_part_acc, c->d_part_ml, H, D,
                                                     d_out, part, nparts);
   }
@@ -674,8 +742,18 @@ int dsd_selftest_bounded_wait(dsd_ctx* c, int64_t budget_cycles) {
 
 int dsd_ctx_create(int device, const dsd_model_config* config, const dsd_ctx_options* options,
                    dsd_ctx** out) {
+  return dsd_ctx_create_ex(device, config, options, DSD_KV_F32, out);
+}
+
+int dsd_ctx_kv_format(dsd_ctx* c) { return c ? c->kv_format : -1; }
+
+int dsd_ctx_create_ex(int device, const dsd_model_config* config, const dsd_ctx_options* options,
+                      int kv_format, dsd_ctx** out) {
   return Guard([&]() {
     if (!config || !options || !out) Fail(DSD_EINVAL, "null argument");
+    if (kv_format != DSD_KV_F32 && kv_format != DSD_KV_BF16) Fail(DSD_EINVAL, "unknown kv_format");
+    if (kv_format == DSD_KV_BF16 && config->head_dim < 8)
+      Fail(DSD_EINVAL, "bf16 pages need head_dim >= 8");
     *out = nullptr;
     const dsd_model_config cfg = *config;
     const dsd_ctx_options opt = *options;
@@ -705,7 +783,9 @@ int dsd_ctx_create(int device, const dsd_model_config* config, const dsd_ctx_opt
       c->opt = opt;
       c->ept = ept;
       c->num_sms = prop.multiProcessorCount;
-      c->attn = MakeAttnShape(cfg.num_heads, D, cfg.page_size);
+      c->kv_format = kv_format;
+      c->kv_elem = kv_format == DSD_KV_BF16 ? 2 : 4;
+      c->attn = MakeAttnShape(cfg.num_heads, D, cfg.page_size, kv_format == DSD_KV_BF16);
       c->scale = 1.0f / std::sqrt(static_cast<float>(D));
       Check(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream");
       for (auto& e : c->ev) Check(cudaEventCreate(&e), "event");
@@ -716,14 +796,15 @@ int dsd_ctx_create(int device, const dsd_model_config* config, const dsd_ctx_opt
       Check(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming), "event");
 
       const size_t cap = size_t(opt.capacity_pages);
-      c->k_pool = DeviceAlloc<float>(cap * cfg.page_size * ept, "key pool");
-      c->v_pool = DeviceAlloc<float>(cap * cfg.page_size * ept, "value pool");
+      const size_t el = c->kv_elem;
+      c->k_pool = DeviceAlloc<unsigned char>(cap * cfg.page_size * ept * el, "key pool");
+      c->v_pool = DeviceAlloc<unsigned char>(cap * cfg.page_size * ept * el, "value pool");
       c->summary_floats = (cap + 127) / 128 * dsdk::summary_group_floats(ept);
-      c->summaries = DeviceAlloc<float>(c->summary_floats, "page summaries");
+      c->summaries = DeviceAlloc<unsigned char>(c->summary_floats * el, "page summaries");
       c->token_counts = DeviceAlloc<int>(cap, "token counts");
       c->live = DeviceAlloc<uint8_t>(cap, "live mask");
-      Check(cudaMemsetAsync(c->summaries, 0, std::max<size_t>(1, c->summary_floats) * 4, c->stream),
-            "memset");
+      Check(cudaMemsetAsync(c->summaries, 0, std::max<size_t>(1, c->summary_floats) * el,
+                            c->stream), "memset");
       Check(cudaMemsetAsync(c->token_counts, 0, std::max<size_t>(1, cap) * 4, c->stream), "memset");
       Check(cudaMemsetAsync(c->live, 0, std::max<size_t>(1, cap), c->stream), "memset");
       c->host_counts.assign(cap, 0);
@@ -783,7 +864,14 @@ int dsd_ctx_create(int device, const dsd_model_config* config, const dsd_ctx_opt
 
       Check(cudaFuncSetAttribute(dsdk::score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)dsdk::kScoreSmem), "smem attribute");
-      SetAllAttnAttributes(c->attn.smem);
+      if (kv_format == DSD_KV_BF16) {
+        Check(cudaFuncSetAttribute(dsdk::score_kernel_bf16,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   int(dsdk::kScoreBfSmem)), "smem attribute");
+        SetAllAttnAttributesBf16(c->attn.smem);
+      } else {
+        SetAllAttnAttributes(c->attn.smem);
+      }
       Check(cudaFuncSetAttribute(dsdk::select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  int(dsdk::kSelectSmem)), "smem attribute");
       Sync(c);
@@ -837,9 +925,9 @@ int dsd_ctx_device_pointers(dsd_ctx* c, float** keys, float** values, float** su
                             int32_t** token_counts) {
   return Guard([&]() {
     if (!c) Fail(DSD_EINVAL, "null context");
-    if (keys) *keys = c->k_pool;
-    if (values) *values = c->v_pool;
-    if (summaries) *summaries = c->summaries;
+    if (keys) *keys = static_cast<float*>(c->k_pool);
+    if (values) *values = static_cast<float*>(c->v_pool);
+    if (summaries) *summaries = static_cast<float*>(c->summaries);
     if (token_counts) *token_counts = c->token_counts;
   });
 }
@@ -867,8 +955,8 @@ int dsd_pool_reset(dsd_ctx* c) {
     if (!c) Fail(DSD_EINVAL, "null context");
     SetDevice(c);
     const size_t cap = size_t(c->opt.capacity_pages);
-    Check(cudaMemsetAsync(c->summaries, 0, std::max<size_t>(1, c->summary_floats) * 4, c->stream),
-          "memset");
+    Check(cudaMemsetAsync(c->summaries, 0, std::max<size_t>(1, c->summary_floats) * c->kv_elem,
+                          c->stream), "memset");
     Check(cudaMemsetAsync(c->token_counts, 0, std::max<size_t>(1, cap) * 4, c->stream), "memset");
     Check(cudaMemsetAsync(c->live, 0, std::max<size_t>(1, cap), c->stream), "memset");
     std::fill(c->host_counts.begin(), c->host_counts.end(), 0);
@@ -935,10 +1023,14 @@ int dsd_pool_upload_pages(dsd_ctx* c, const int32_t* page_ids, const int32_t* to
       const int* d_ids = reinterpret_cast<const int*>(d_off + np);
       const int vec = c->ept / 4;
       dim3 grid(np, (vec + 255) / 256);
-      dsdk::upload_pages_kernel<<<grid, 256, 0, c->stream>>>(
-          d_ids, d_ids + np, d_off, reinterpret_cast<const float*>(c->d_stage),
-          reinterpret_cast<const float*>(c->d_stage + payload), c->ept, c->cfg.page_size,
-          compute_summary, c->k_pool, c->v_pool, c->summaries, c->token_counts, c->live);
+      WithKv(c, [&](auto tag) {
+        using T = typename decltype(tag)::type;
+        dsdk::upload_pages_kernel<T><<<grid, 256, 0, c->stream>>>(
+            d_ids, d_ids + np, d_off, reinterpret_cast<const float*>(c->d_stage),
+            reinterpret_cast<const float*>(c->d_stage + payload), c->ept, c->cfg.page_size,
+            compute_summary, static_cast<T*>(c->k_pool), static_cast<T*>(c->v_pool),
+            static_cast<T*>(c->summaries), c->token_counts, c->live);
+      });
       Check(cudaGetLastError(), "upload kernel");
       Sync(c);  // the staging buffer is reused by the next group
       for (int i = i0; i < i1; ++i) c->host_counts[page_ids[i]] = token_counts[i];
@@ -959,9 +1051,12 @@ int dsd_pool_upload_summaries(dsd_ctx* c, const int32_t* page_ids, int n, const 
     EnsureStage(c, ids_off + size_t(n) * 4);
     H2D(c, c->d_stage, summaries, sb);
     H2D(c, c->d_stage + ids_off, page_ids, size_t(n) * 4);
-    dsdk::set_summaries_kernel<<<n, 256, 0, c->stream>>>(
-        reinterpret_cast<const int*>(c->d_stage + ids_off),
-        reinterpret_cast<const float*>(c->d_stage), c->ept, c->summaries);
+    WithKv(c, [&](auto tag) {
+      using T = typename decltype(tag)::type;
+      dsdk::set_summaries_kernel<T><<<n, 256, 0, c->stream>>>(
+          reinterpret_cast<const int*>(c->d_stage + ids_off),
+          reinterpret_cast<const float*>(c->d_stage), c->ept, static_cast<T*>(c->summaries));
+    });
     Check(cudaGetLastError(), "summary kernel");
     Sync(c);
   });
@@ -982,9 +1077,12 @@ int dsd_pool_prefill_synthetic(dsd_ctx* c, const int32_t* page_ids, const int32_
     H2D(c, c->d_stage, page_ids, size_t(n) * 4);
     H2D(c, c->d_stage + size_t(n) * 4, token_counts, size_t(n) * 4);
     const int* d = reinterpret_cast<const int*>(c->d_stage);
-    dsdk::prefill_synthetic_kernel<<<n, 256, 0, c->stream>>>(d, d + n, request_id, c->ept,
-                                                            c->cfg.page_size, c->k_pool, c->v_pool,
-                                                            c->summaries, c->token_counts, c->live);
+    WithKv(c, [&](auto tag) {
+      using T = typename decltype(tag)::type;
+      dsdk::prefill_synthetic_kernel<T><<<n, 256, 0, c->stream>>>(
+          d, d + n, request_id, c->ept, c->cfg.page_size, static_cast<T*>(c->k_pool),
+          static_cast<T*>(c->v_pool), static_cast<T*>(c->summaries), c->token_counts, c->live);
+    });
     Check(cudaGetLastError(), "prefill kernel");
     Sync(c);
     for (int i = 0; i < n; ++i) c->host_counts[page_ids[i]] = token_counts[i];
@@ -1013,10 +1111,14 @@ int dsd_pool_generate_normal(dsd_ctx* c, const int32_t* page_ids, const int32_t*
       H2D(c, d + 2 * m, request_ids + i0, size_t(m) * 4);
       H2D(c, d + 3 * m, first_token + i0, size_t(m) * 4);
       dim3 grid(m, (c->ept + 255) / 256);
-      dsdk::generate_normal_kernel<<<grid, 256, 0, c->stream>>>(
-          d, d + m, d + 2 * m, d + 3 * m, c->ept, c->cfg.page_size, dsdk::normal_seed_mix(seed, 1),
-          dsdk::normal_seed_mix(seed, 2), c->k_pool, c->v_pool, c->summaries, c->token_counts,
-          c->live);
+      WithKv(c, [&](auto tag) {
+        using T = typename decltype(tag)::type;
+        dsdk::generate_normal_kernel<T><<<grid, 256, 0, c->stream>>>(
+            d, d + m, d + 2 * m, d + 3 * m, c->ept, c->cfg.page_size,
+            dsdk::normal_seed_mix(seed, 1), dsdk::normal_seed_mix(seed, 2),
+            static_cast<T*>(c->k_pool), static_cast<T*>(c->v_pool),
+            static_cast<T*>(c->summaries), c->token_counts, c->live);
+      });
       Check(cudaGetLastError(), "generate kernel");
       Sync(c);
     }
@@ -1076,10 +1178,14 @@ int dsd_append_tokens(dsd_ctx* c, const int32_t* page_ids, const int32_t* token_
     H2D(c, c->d_stage + meta_off, meta.data(), meta.size() * 4);
     const int ng = int(gpage.size());
     const int* d = reinterpret_cast<const int*>(c->d_stage + meta_off);
-    dsdk::append_tokens_kernel<<<ng, 256, 0, c->stream>>>(
-        d, d + ng, d + 2 * ng + 1, reinterpret_cast<const float*>(c->d_stage),
-        reinterpret_cast<const float*>(c->d_stage + payload), c->ept, c->cfg.page_size,
-        c->k_pool, c->v_pool, c->summaries, c->token_counts, c->live);
+    WithKv(c, [&](auto tag) {
+      using T = typename decltype(tag)::type;
+      dsdk::append_tokens_kernel<T><<<ng, 256, 0, c->stream>>>(
+          d, d + ng, d + 2 * ng + 1, reinterpret_cast<const float*>(c->d_stage),
+          reinterpret_cast<const float*>(c->d_stage + payload), c->ept, c->cfg.page_size,
+          static_cast<T*>(c->k_pool), static_cast<T*>(c->v_pool), static_cast<T*>(c->summaries),
+          c->token_counts, c->live);
+    });
     Check(cudaGetLastError(), "append kernel");
     // no wait: later users of the staging buffer are ordered on the same stream
     for (int i = 0; i < n; ++i)
@@ -1112,9 +1218,13 @@ int dsd_append_tokens_synthetic(dsd_ctx* c, const int32_t* page_ids, const int32
     const int ng = int(gpage.size());
     const int* d = reinterpret_cast<const int*>(c->d_stage);
     const int* toff = d + 2 * ng + 1;
-    dsdk::append_synthetic_kernel<<<ng, 256, 0, c->stream>>>(
-        d, d + ng, toff, toff + n, toff + 2 * n, c->ept, c->cfg.page_size, c->k_pool, c->v_pool,
-        c->summaries, c->token_counts, c->live);
+    WithKv(c, [&](auto tag) {
+      using T = typename decltype(tag)::type;
+      dsdk::append_synthetic_kernel<T><<<ng, 256, 0, c->stream>>>(
+          d, d + ng, toff, toff + n, toff + 2 * n, c->ept, c->cfg.page_size,
+          static_cast<T*>(c->k_pool), static_cast<T*>(c->v_pool), static_cast<T*>(c->summaries),
+          c->token_counts, c->live);
+    });
     Check(cudaGetLastError(), "synthetic append kernel");
     // no wait: later users of the staging buffer are ordered on the same stream
     for (int i = 0; i < n; ++i)
@@ -1130,9 +1240,12 @@ int dsd_pool_free_pages(dsd_ctx* c, const int32_t* page_ids, int n) {
     for (int i = 0; i < n; ++i) ValidatePage(c, page_ids[i]);
     EnsureStage(c, size_t(n) * 4);
     H2D(c, c->d_stage, page_ids, size_t(n) * 4);
-    dsdk::free_pages_kernel<<<n, 256, 0, c->stream>>>(reinterpret_cast<const int*>(c->d_stage),
-                                                      c->ept, c->summaries, c->token_counts,
-                                                      c->live);
+    WithKv(c, [&](auto tag) {
+      using T = typename decltype(tag)::type;
+      dsdk::free_pages_kernel<T><<<n, 256, 0, c->stream>>>(
+          reinterpret_cast<const int*>(c->d_stage), c->ept, static_cast<T*>(c->summaries),
+          c->token_counts, c->live);
+    });
     Check(cudaGetLastError(), "free kernel");
     // no wait: later users of the staging buffer are ordered on the same stream
     for (int i = 0; i < n; ++i) c->host_counts[page_ids[i]] = 0;
@@ -1146,19 +1259,40 @@ int dsd_download_page(dsd_ctx* c, int page_id, float* keys, float* values, float
     ValidatePage(c, page_id);
     SetDevice(c);
     const size_t pf = size_t(c->cfg.page_size) * c->ept;
-    if (keys) D2H(c, keys, c->k_pool + size_t(page_id) * pf, pf * 4);
-    if (values) D2H(c, values, c->v_pool + size_t(page_id) * pf, pf * 4);
+    const size_t el = c->kv_elem;
+    const bool bf16 = c->kv_format == DSD_KV_BF16;
+    // bf16 pools land in 16-bit host words and widen to fp32 after the sync
+    std::vector<uint16_t> hk(bf16 && keys ? pf : 0), hv(bf16 && values ? pf : 0),
+        hs(bf16 && summary ? size_t(c->ept) : 0);
+    const auto* kp = static_cast<const unsigned char*>(c->k_pool);
+    const auto* vp = static_cast<const unsigned char*>(c->v_pool);
+    if (keys) D2H(c, bf16 ? static_cast<void*>(hk.data()) : keys, kp + size_t(page_id) * pf * el,
+                  pf * el);
+    if (values) D2H(c, bf16 ? static_cast<void*>(hv.data()) : values,
+                    vp + size_t(page_id) * pf * el, pf * el);
     if (summary) {
-      // gather the page's NC chunks of CW floats (stride 128*CW) into one row
+      // gather the page's NC chunks of CW elements (stride 128*CW) into one row
       const int cw = dsdk::summary_chunk(c->ept);
-      Check(cudaMemcpy2DAsync(summary, size_t(cw) * 4,
-                              c->summaries + dsdk::summary_row_base(page_id, c->ept),
-                              size_t(128) * cw * 4, size_t(cw) * 4, size_t(c->ept / cw),
+      Check(cudaMemcpy2DAsync(bf16 ? static_cast<void*>(hs.data()) : summary, size_t(cw) * el,
+                              static_cast<const unsigned char*>(c->summaries) +
+                                  dsdk::summary_row_base(page_id, c->ept) * el,
+                              size_t(128) * cw * el, size_t(cw) * el, size_t(c->ept / cw),
                               cudaMemcpyDeviceToHost, c->stream), "summary download");
-      CountD2H(c, size_t(c->ept) * 4);
+      CountD2H(c, size_t(c->ept) * el);
     }
     if (token_count) D2H(c, token_count, c->token_counts + page_id, 4);
     Sync(c);
+    auto widen = [](const std::vector<uint16_t>& src, float* dst) {
+      for (size_t i = 0; i < src.size(); ++i) {
+        const uint32_t b = uint32_t(src[i]) << 16;
+        std::memcpy(dst + i, &b, 4);
+      }
+    };
+    if (bf16) {
+      if (keys) widen(hk, keys);
+      if (values) widen(hv, values);
+      if (summary) widen(hs, summary);
+    }
   });
 }
 

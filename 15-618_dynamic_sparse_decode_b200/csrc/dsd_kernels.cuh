@@ -22,10 +22,56 @@
 // mean, free, synthetic generators) follow at the end.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace dsdk {
+
+// Storage element of the K/V pages and the summaries: fp32 (the parity
+// path) or bf16 (opt-in; arithmetic stays fp32, values round to nearest even
+// when stored).  get/put convert one element; load4/store4 four.
+template <typename T>
+struct Kv;
+template <>
+struct Kv<float> {
+  __device__ __forceinline__ static float get(const float* p, size_t i) { return p[i]; }
+  __device__ __forceinline__ static float round(float v) { return v; }
+  __device__ __forceinline__ static void put(float* p, size_t i, float v) { p[i] = v; }
+  __device__ __forceinline__ static float4 load4(const float* p) {
+    return *reinterpret_cast<const float4*>(p);
+  }
+  __device__ __forceinline__ static void store4(float* p, float4 v) {
+    *reinterpret_cast<float4*>(p) = v;
+  }
+  __device__ __forceinline__ static float4 round4(float4 v) { return v; }
+};
+template <>
+struct Kv<__nv_bfloat16> {
+  using T = __nv_bfloat16;
+  __device__ __forceinline__ static float get(const T* p, size_t i) { return __bfloat162float(p[i]); }
+  __device__ __forceinline__ static float round(float v) {
+    return __bfloat162float(__float2bfloat16_rn(v));
+  }
+  __device__ __forceinline__ static void put(T* p, size_t i, float v) { p[i] = __float2bfloat16_rn(v); }
+  __device__ __forceinline__ static float4 load4(const T* p) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(p);
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+    return make_float4(__low2float(a), __high2float(a), __low2float(b), __high2float(b));
+  }
+  __device__ __forceinline__ static void store4(T* p, float4 v) {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y);
+    const __nv_bfloat162 b = __floats2bfloat162_rn(v.z, v.w);
+    uint2 raw;
+    raw.x = *reinterpret_cast<const uint32_t*>(&a);
+    raw.y = *reinterpret_cast<const uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(p) = raw;
+  }
+  __device__ __forceinline__ static float4 round4(float4 v) {
+    return make_float4(round(v.x), round(v.y), round(v.z), round(v.w));
+  }
+};
 
 constexpr int kMaxBatch = 1024;
 constexpr int kPlanThreads = 1024;
@@ -447,6 +493,128 @@ __global__ void __launch_bounds__(kScoreThreads, 2) score_kernel(
   cp_async_wait<0>();
 }
 
+// bf16 summaries: the score_kernel scheme with 16-byte pieces of 8 bf16 per
+// row column (kCols = 8 per 64-element row chunk), 144-byte padded rows (the
+// 8 threads of a quarter warp read 8 different 16 B bank groups), the fp32
+// query chunk in its own region and more stages in flight (a stage holds half
+// the bytes).  Each bf16 element widens to fp32 exactly; the dot product is
+// the same sequential round-to-nearest chain as score_kernel.
+constexpr int kScoreBfRowStride = kScoreChunk + 8;  // bf16 elements per smem row
+constexpr int kScoreBfStages = 5;
+constexpr size_t kScoreBfStageBytes =
+    size_t(kScoreTile) * kScoreBfRowStride * 2 + size_t(kScoreChunk) * 4;
+constexpr size_t kScoreBfSmem = kScoreBfStages * kScoreBfStageBytes;
+
+__global__ void __launch_bounds__(kScoreThreads, 2) score_kernel_bf16(
+    StepPlan plan, const float* __restrict__ queries, const __nv_bfloat16* __restrict__ summaries,
+    int ept, float scale, float* __restrict__ scores, int part, int nparts) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  constexpr int kCols = kScoreChunk / 8;                  // 16 B columns per row chunk
+  constexpr int kRowStep = kScoreThreads / kCols;
+  constexpr int kRowsPerThread = kScoreTile / kRowStep;
+
+  const int tid = threadIdx.x;
+  const int B = plan.hdr[0];
+  const int mode = plan.hdr[1];
+  const int* ids_src = mode == 0 ? plan.cand_ids : plan.table;
+  int r_begin, r_end;
+  part_range(B, part, nparts, &r_begin, &r_end);
+  const int tile_begin = plan.tile_off[r_begin];
+  const int total_tiles = plan.tile_off[r_end];
+  const int ts = plan.misc[1];
+  const int cw = summary_chunk(ept);          // elements of a page's summary per stage (>= 8)
+  const int nchunks = ept / cw;
+  const size_t chunk_stride = size_t(128) * cw;
+  const int col = tid % kCols;
+  const int row0 = tid / kCols;
+
+  int ld_tile = tile_begin + blockIdx.x, ld_ch = 0, ld_slot = 0, ld_nvalid = 0;
+  const float* ld_q = queries;
+  size_t ld_off[kRowsPerThread];
+  auto load_tile = [&]() {
+    if (ld_tile >= total_tiles) return;
+    const int r = upper_segment(plan.tile_off, B, ld_tile);
+    const int c0 = (ld_tile - plan.tile_off[r]) * ts;
+    ld_nvalid = min(ts, plan.n_cand[r] - c0);
+    ld_q = queries + size_t(r) * ept;
+    const int* ids = ids_src + plan.id_base[r] + c0;
+#pragma unroll
+    for (int j = 0; j < kRowsPerThread; ++j) {
+      const int row = row0 + kRowStep * j;
+      ld_off[j] = row < ld_nvalid ? summary_row_base(__ldg(ids + row), ept) : 0;
+    }
+  };
+  auto issue = [&]() {
+    if (ld_tile < total_tiles) {
+      unsigned char* st = smem_raw + size_t(ld_slot) * kScoreBfStageBytes;
+      __nv_bfloat16* rows = reinterpret_cast<__nv_bfloat16*>(st);
+      float* qst = reinterpret_cast<float*>(st + size_t(kScoreTile) * kScoreBfRowStride * 2);
+      if (col * 8 < cw) {
+        const size_t coff = size_t(ld_ch) * chunk_stride + col * 8;
+#pragma unroll
+        for (int j = 0; j < kRowsPerThread; ++j) {
+          const int row = row0 + kRowStep * j;
+          if (row < ld_nvalid)
+            cp_async16(rows + row * kScoreBfRowStride + col * 8, summaries + ld_off[j] + coff);
+        }
+      }
+      if (tid * 4 < cw) cp_async16(qst + tid * 4, ld_q + size_t(ld_ch) * cw + tid * 4);
+      if (++ld_ch == nchunks) {
+        ld_ch = 0;
+        ld_tile += gridDim.x;
+        load_tile();
+      }
+    }
+    cp_async_commit();
+    ld_slot = ld_slot + 1 == kScoreBfStages ? 0 : ld_slot + 1;
+  };
+
+  load_tile();
+#pragma unroll 1
+  for (int i = 0; i < kScoreBfStages - 1; ++i) issue();
+
+  int slot = 0;
+  for (int tile = tile_begin + blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+    const int r = upper_segment(plan.tile_off, B, tile);
+    const int c0 = (tile - plan.tile_off[r]) * ts;
+    const int nvalid = min(ts, plan.n_cand[r] - c0);
+    float acc = 0.0f;
+    for (int ch = 0; ch < nchunks; ++ch) {
+      cp_async_wait<kScoreBfStages - 2>();
+      __syncthreads();
+      issue();
+      const unsigned char* st = smem_raw + size_t(slot) * kScoreBfStageBytes;
+      if (tid < nvalid) {
+        const uint4* srow = reinterpret_cast<const uint4*>(
+            reinterpret_cast<const __nv_bfloat16*>(st) + tid * kScoreBfRowStride);
+        const float4* qv =
+            reinterpret_cast<const float4*>(st + size_t(kScoreTile) * kScoreBfRowStride * 2);
+        auto step8 = [&](int i) {
+          const uint4 raw = srow[i];
+          const float4 a0 = qv[2 * i], a1 = qv[2 * i + 1];
+          const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+          const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            // bf16 -> fp32 is a 16-bit shift (exact)
+            acc = __fadd_rn(acc, __fmul_rn(a[2 * h], __uint_as_float(w[h] << 16)));
+            acc = __fadd_rn(acc, __fmul_rn(a[2 * h + 1], __uint_as_float(w[h] & 0xffff0000u)));
+          }
+        };
+        if (cw == kScoreChunk) {
+#pragma unroll
+          for (int i = 0; i < kScoreChunk / 8; ++i) step8(i);
+        } else {
+          for (int i = 0; i < cw / 8; ++i) step8(i);
+        }
+      }
+      slot = slot + 1 == kScoreBfStages ? 0 : slot + 1;
+    }
+    if (tid < nvalid) scores[plan.score_off[r] + c0 + tid] = __fmul_rn(acc, scale);
+  }
+  cp_async_wait<0>();
+}
+
 // ------------------------------------------------------------------ select
 
 // Order-preserving 64-bit key: larger key = better page.  High word is the
@@ -827,6 +995,183 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(
   }
 }
 
+// bf16 pages: attn_kernel with 16-byte vectors of 8 bf16 instead of float4
+// (a head's D/8 vectors over LP = D/(8*NV) lanes, so the 8 lanes of a quarter
+// warp again read 128 contiguous bytes of one row), stages of `tps` K rows
+// then `tps` V rows in bf16, and fp32 queries, logits, softmax and partials.
+__device__ __forceinline__ void unpack_bf16x8(const uint4 raw, float (&f)[8]) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    f[2 * h] = __uint_as_float(w[h] << 16);
+    f[2 * h + 1] = __uint_as_float(w[h] & 0xffff0000u);
+  }
+}
+
+template <int NV, int SLOTS>
+__global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel_bf16(
+    StepPlan plan, const float* __restrict__ queries, const __nv_bfloat16* __restrict__ key_pool,
+    const __nv_bfloat16* __restrict__ value_pool, const int* __restrict__ token_counts,
+    const int* __restrict__ selected, float* __restrict__ part_acc, float* __restrict__ part_ml,
+    int num_heads, int head_dim, int page_size, int tps, float scale, int part, int nparts) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  constexpr int kMaxTps = kAttnMaxTokensPerStage;
+  const int ept = num_heads * head_dim;
+  const int vec = ept >> 3;                       // 16-byte vectors per token row
+  const int G = head_dim >> 3;                    // vectors per head
+  const int LP = G / NV;                          // lanes per head
+  const size_t stage_elems = size_t(2) * tps * ept;
+  __nv_bfloat16* stages = reinterpret_cast<__nv_bfloat16*>(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + kAttnStages * stage_elems * 2);
+
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    for (int s = 0; s < kAttnStages; ++s) mbar_init(&full[s], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  const int B = plan.hdr[0];
+  int r_begin, r_end;
+  part_range(B, part, nparts, &r_begin, &r_end);
+  const int unit_begin = plan.unit_off[r_begin];
+  const int total_units = plan.unit_off[r_end];
+  const int ppu = plan.misc[0];
+  const size_t page_elems = size_t(page_size) * ept;
+  int* status = plan.status;
+
+  AttnWalk w{unit_begin + static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x), 0, 0, 0, 0,
+             0, false};
+  auto issue = [&](int s) {
+    const int nt = min(tps, w.n - w.t0);
+    const uint32_t bytes = uint32_t(nt) * uint32_t(ept) * 2u;
+    __nv_bfloat16* st = stages + size_t(s) * stage_elems;
+    const size_t src = size_t(w.page) * page_elems + size_t(w.t0) * ept;
+    mbar_arrive_expect_tx(&full[s], 2u * bytes);
+    bulk_g2s(st, key_pool + src, bytes, &full[s]);
+    bulk_g2s(st + size_t(tps) * ept, value_pool + src, bytes, &full[s]);
+  };
+  if (tid == 0) {
+    for (int s = 0; s < kAttnStages; ++s) {
+      if (!attn_walk_next(w, plan, B, total_units, ppu, tps, page_size, selected, token_counts))
+        break;
+      issue(s);
+    }
+  }
+
+  int colv[SLOTS][NV];
+  bool ok[SLOTS];
+#pragma unroll
+  for (int m = 0; m < SLOTS; ++m) {
+    const int item = tid + kAttnThreads * m;
+    const int head = item / LP, li = item - (item / LP) * LP;
+    ok[m] = head < num_heads;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) colv[m][j] = ok[m] ? head * G + li + LP * j : 0;
+  }
+
+  uint32_t g = 0;
+  bool alive = true;
+  for (int u = unit_begin + blockIdx.x; u < total_units && alive; u += gridDim.x) {
+    int r, p_begin, p_end;
+    attn_unit_range(plan, B, ppu, u, &r, &p_begin, &p_end);
+    float q[SLOTS][NV][8], acc[SLOTS][NV][8];
+    float mrun[SLOTS], lrun[SLOTS];
+    const float4* qrow = reinterpret_cast<const float4*>(queries + size_t(r) * ept);
+#pragma unroll
+    for (int m = 0; m < SLOTS; ++m) {
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        const float4 a = ok[m] ? __ldg(qrow + 2 * colv[m][j]) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 b =
+            ok[m] ? __ldg(qrow + 2 * colv[m][j] + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+        q[m][j][0] = a.x; q[m][j][1] = a.y; q[m][j][2] = a.z; q[m][j][3] = a.w;
+        q[m][j][4] = b.x; q[m][j][5] = b.y; q[m][j][6] = b.z; q[m][j][7] = b.w;
+#pragma unroll
+        for (int x = 0; x < 8; ++x) acc[m][j][x] = 0.f;
+      }
+      mrun[m] = -INFINITY;
+      lrun[m] = 0.f;
+    }
+    for (int p = p_begin; p < p_end && alive; ++p) {
+      const int page = __ldg(selected + p);
+      const int n = min(__ldg(token_counts + page), page_size);
+      for (int t0 = 0; t0 < n; t0 += tps, ++g) {
+        const int s = g % kAttnStages;
+        if (!mbar_wait(&full[s], (g / kAttnStages) & 1, status)) { alive = false; break; }
+        const int nt = min(tps, n - t0);
+        const uint4* kst = reinterpret_cast<const uint4*>(stages + size_t(s) * stage_elems);
+        const uint4* vst = kst + size_t(tps) * vec;
+#pragma unroll
+        for (int m = 0; m < SLOTS; ++m) {
+          float logit[kMaxTps];
+          float cmax = mrun[m];
+#pragma unroll
+          for (int t = 0; t < kMaxTps; ++t) {
+            if (t < nt) {
+              float d = 0.f;
+#pragma unroll
+              for (int j = 0; j < NV; ++j) {
+                float kk[8];
+                unpack_bf16x8(kst[size_t(t) * vec + colv[m][j]], kk);
+#pragma unroll
+                for (int x = 0; x < 8; ++x) d += q[m][j][x] * kk[x];
+              }
+              for (int o = LP >> 1; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+              logit[t] = d * scale;
+              cmax = fmaxf(cmax, logit[t]);
+            }
+          }
+          const float alpha = expf(mrun[m] - cmax);
+          float l = lrun[m] * alpha;
+#pragma unroll
+          for (int j = 0; j < NV; ++j)
+#pragma unroll
+            for (int x = 0; x < 8; ++x) acc[m][j][x] *= alpha;
+#pragma unroll
+          for (int t = 0; t < kMaxTps; ++t) {
+            if (t < nt) {
+              const float beta = expf(logit[t] - cmax);
+              l += beta;
+#pragma unroll
+              for (int j = 0; j < NV; ++j) {
+                float vv[8];
+                unpack_bf16x8(vst[size_t(t) * vec + colv[m][j]], vv);
+#pragma unroll
+                for (int x = 0; x < 8; ++x) acc[m][j][x] += beta * vv[x];
+              }
+            }
+          }
+          lrun[m] = l;
+          mrun[m] = cmax;
+        }
+        __syncthreads();  // every thread is done with stage s
+        if (tid == 0) {
+          if (attn_walk_next(w, plan, B, total_units, ppu, tps, page_size, selected, token_counts))
+            issue(s);
+        }
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < SLOTS; ++m) {
+      if (!ok[m]) continue;
+      float4* pa = reinterpret_cast<float4*>(part_acc + size_t(u) * ept);
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        pa[2 * colv[m][j]] = make_float4(acc[m][j][0], acc[m][j][1], acc[m][j][2], acc[m][j][3]);
+        pa[2 * colv[m][j] + 1] =
+            make_float4(acc[m][j][4], acc[m][j][5], acc[m][j][6], acc[m][j][7]);
+      }
+      const int item = tid + kAttnThreads * m;
+      if (item % LP == 0) {
+        const int head = item / LP;
+        part_ml[(size_t(u) * num_heads + head) * 2 + 0] = mrun[m];
+        part_ml[(size_t(u) * num_heads + head) * 2 + 1] = lrun[m];
+      }
+    }
+  }
+}
+
 // One warp per (request, head): out = sum_u e^{m_u-M} acc_u / sum_u e^{m_u-M} l_u,
 // zero when the request attended to no token (SparseAttentionCpu returns zeros).
 // Lanes split the units for M and L (warp reductions), then each lane owns
@@ -885,13 +1230,14 @@ __global__ void __launch_bounds__(256) combine_kernel(StepPlan plan,
 // summary with PagedKvCache::AppendPage's formula (src/paged_kv_cache.cpp:88-99):
 // token-order sum, then * (1.0f / n), both rounded to nearest, no FMA.
 // grid (pages, ceil(E/4/256)); thread = one float4 column.
+template <typename T>
 __global__ void upload_pages_kernel(const int* __restrict__ page_ids,
                                     const int* __restrict__ counts,
                                     const long long* __restrict__ src_token_off,
                                     const float* __restrict__ staged_k,
                                     const float* __restrict__ staged_v, int ept, int page_size,
-                                    int compute_summary, float* __restrict__ key_pool,
-                                    float* __restrict__ value_pool, float* __restrict__ summaries,
+                                    int compute_summary, T* __restrict__ key_pool,
+                                    T* __restrict__ value_pool, T* __restrict__ summaries,
                                     int* __restrict__ token_counts, uint8_t* __restrict__ live) {
   const int i = blockIdx.x;
   const int j = blockIdx.y * blockDim.x + threadIdx.x;
@@ -901,13 +1247,14 @@ __global__ void upload_pages_kernel(const int* __restrict__ page_ids,
   if (j < vec) {
     const float4* sk = reinterpret_cast<const float4*>(staged_k + src_token_off[i] * ept);
     const float4* sv = reinterpret_cast<const float4*>(staged_v + src_token_off[i] * ept);
-    float4* dk = reinterpret_cast<float4*>(key_pool + size_t(page) * page_size * ept);
-    float4* dv = reinterpret_cast<float4*>(value_pool + size_t(page) * page_size * ept);
+    T* dk = key_pool + size_t(page) * page_size * ept;
+    T* dv = value_pool + size_t(page) * page_size * ept;
     float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int t = 0; t < n; ++t) {
-      const float4 k = sk[size_t(t) * vec + j];
-      dk[size_t(t) * vec + j] = k;
-      dv[size_t(t) * vec + j] = sv[size_t(t) * vec + j];
+      // the stored (rounded) key is what the summary averages
+      const float4 k = Kv<T>::round4(sk[size_t(t) * vec + j]);
+      Kv<T>::store4(dk + (size_t(t) * vec + j) * 4, k);
+      Kv<T>::store4(dv + (size_t(t) * vec + j) * 4, sv[size_t(t) * vec + j]);
       sum.x = __fadd_rn(sum.x, k.x);
       sum.y = __fadd_rn(sum.y, k.y);
       sum.z = __fadd_rn(sum.z, k.z);
@@ -919,7 +1266,7 @@ __global__ void upload_pages_kernel(const int* __restrict__ page_ids,
       out = make_float4(__fmul_rn(sum.x, inv), __fmul_rn(sum.y, inv), __fmul_rn(sum.z, inv),
                         __fmul_rn(sum.w, inv));
     }
-    *reinterpret_cast<float4*>(summaries + summary_off(page, 4 * j, ept)) = out;
+    Kv<T>::store4(summaries + summary_off(page, 4 * j, ept), out);
   }
   if (blockIdx.y == 0 && threadIdx.x == 0) {
     token_counts[page] = n;
@@ -927,26 +1274,28 @@ __global__ void upload_pages_kernel(const int* __restrict__ page_ids,
   }
 }
 
+template <typename T>
 __global__ void set_summaries_kernel(const int* __restrict__ page_ids,
                                      const float* __restrict__ staged, int ept,
-                                     float* __restrict__ summaries) {
+                                     T* __restrict__ summaries) {
   const int i = blockIdx.x;
   const int page = page_ids[i];
   for (int e = threadIdx.x; e < ept; e += blockDim.x)
-    summaries[summary_off(page, e, ept)] = staged[size_t(i) * ept + e];
+    Kv<T>::put(summaries, summary_off(page, e, ept), staged[size_t(i) * ept + e]);
 }
 
 // Token append.  One block per distinct page; its tokens (token_first[i] ..
 // token_first[i+1]) are applied in offset order with PagedKvCache::AppendToken's
 // running mean (src/paged_kv_cache.cpp:231-238): s = (s*old + k) / (old + 1).
 // Optional page-table entries (slot, position, page) are written first.
+template <typename T>
 __global__ void append_tokens_kernel(const int* __restrict__ group_page,
                                      const int* __restrict__ token_first,
                                      const int* __restrict__ token_offset,
                                      const float* __restrict__ staged_k,
                                      const float* __restrict__ staged_v, int ept, int page_size,
-                                     float* __restrict__ key_pool, float* __restrict__ value_pool,
-                                     float* __restrict__ summaries, int* __restrict__ token_counts,
+                                     T* __restrict__ key_pool, T* __restrict__ value_pool,
+                                     T* __restrict__ summaries, int* __restrict__ token_counts,
                                      uint8_t* __restrict__ live) {
   const int gidx = blockIdx.x;
   const int page = group_page[gidx];
@@ -957,15 +1306,15 @@ __global__ void append_tokens_kernel(const int* __restrict__ group_page,
     const int off = token_offset[i];
     const float old_c = static_cast<float>(off);
     const float new_c = __fadd_rn(old_c, 1.0f);
-    float* dk = key_pool + (size_t(page) * page_size + off) * ept;
-    float* dv = value_pool + (size_t(page) * page_size + off) * ept;
+    T* dk = key_pool + (size_t(page) * page_size + off) * ept;
+    T* dv = value_pool + (size_t(page) * page_size + off) * ept;
     for (int e = threadIdx.x; e < ept; e += blockDim.x) {
-      const float k = staged_k[size_t(i) * ept + e];
-      dk[e] = k;
-      dv[e] = staged_v[size_t(i) * ept + e];
-      float& slot = summaries[sbase + size_t(e / scw) * 128 * scw + (e % scw)];
-      const float s = off == 0 ? 0.0f : slot;
-      slot = __fdiv_rn(__fadd_rn(__fmul_rn(s, old_c), k), new_c);
+      const float k = Kv<T>::round(staged_k[size_t(i) * ept + e]);
+      Kv<T>::put(dk, e, k);
+      Kv<T>::put(dv, e, staged_v[size_t(i) * ept + e]);
+      const size_t so = sbase + size_t(e / scw) * 128 * scw + (e % scw);
+      const float s = off == 0 ? 0.0f : Kv<T>::get(summaries, so);
+      Kv<T>::put(summaries, so, __fdiv_rn(__fadd_rn(__fmul_rn(s, old_c), k), new_c));
     }
     last = max(last, off);
   }
@@ -992,11 +1341,13 @@ __global__ void table_set_count_kernel(const int* __restrict__ pairs, int n,
 }
 
 // DevicePagePool::MarkPagesFree: count 0, not live, summary zeroed.
+template <typename T>
 __global__ void free_pages_kernel(const int* __restrict__ page_ids, int ept,
-                                  float* __restrict__ summaries, int* __restrict__ token_counts,
+                                  T* __restrict__ summaries, int* __restrict__ token_counts,
                                   uint8_t* __restrict__ live) {
   const int page = page_ids[blockIdx.x];
-  for (int e = threadIdx.x; e < ept; e += blockDim.x) summaries[summary_off(page, e, ept)] = 0.0f;
+  for (int e = threadIdx.x; e < ept; e += blockDim.x)
+    Kv<T>::put(summaries, summary_off(page, e, ept), 0.0f);
   if (threadIdx.x == 0) {
     token_counts[page] = 0;
     live[page] = 0;
@@ -1039,11 +1390,12 @@ __device__ __forceinline__ float decode_value(int request, int step, int element
 // Synthetic prefill: page i is page_idx i of `request`; summary by AppendPage's formula.
 // The key (stream 1) and value (stream 2) hashes share every combine step but
 // the last, so the shared prefix is computed once per element and token.
+template <typename T>
 __global__ void prefill_synthetic_kernel(const int* __restrict__ page_ids,
                                          const int* __restrict__ counts, int request, int ept,
-                                         int page_size, float* __restrict__ key_pool,
-                                         float* __restrict__ value_pool,
-                                         float* __restrict__ summaries,
+                                         int page_size, T* __restrict__ key_pool,
+                                         T* __restrict__ value_pool,
+                                         T* __restrict__ summaries,
                                          int* __restrict__ token_counts,
                                          uint8_t* __restrict__ live) {
   const int i = blockIdx.x;
@@ -1057,14 +1409,14 @@ __global__ void prefill_synthetic_kernel(const int* __restrict__ page_ids,
     for (int t = 0; t < n; ++t) {
       uint32_t x = combine_hash(xr, t, 0x27d4eb2fu);
       x = combine_hash(x, e, 0x165667b1u);
-      const float k = hash_to_unit(combine_hash(x, 1, 0xd3a2646cu));
+      const float k = Kv<T>::round(hash_to_unit(combine_hash(x, 1, 0xd3a2646cu)));
       const float v = hash_to_unit(combine_hash(x, 2, 0xd3a2646cu));
-      key_pool[(size_t(page) * page_size + t) * ept + e] = k;
-      value_pool[(size_t(page) * page_size + t) * ept + e] = v;
+      Kv<T>::put(key_pool, (size_t(page) * page_size + t) * ept + e, k);
+      Kv<T>::put(value_pool, (size_t(page) * page_size + t) * ept + e, v);
       sum = __fadd_rn(sum, k);
     }
-    summaries[summary_off(page, e, ept)] =
-        n > 0 ? __fmul_rn(sum, __fdiv_rn(1.0f, static_cast<float>(n))) : 0.0f;
+    Kv<T>::put(summaries, summary_off(page, e, ept),
+               n > 0 ? __fmul_rn(sum, __fdiv_rn(1.0f, static_cast<float>(n))) : 0.0f);
   }
   if (threadIdx.x == 0) {
     token_counts[page] = n;
@@ -1073,13 +1425,14 @@ __global__ void prefill_synthetic_kernel(const int* __restrict__ page_ids,
 }
 
 // Synthetic append: token i = decode step steps[i] of request reqs[i].
+template <typename T>
 __global__ void append_synthetic_kernel(const int* __restrict__ group_page,
                                         const int* __restrict__ token_first,
                                         const int* __restrict__ token_offset,
                                         const int* __restrict__ reqs, const int* __restrict__ steps,
-                                        int ept, int page_size, float* __restrict__ key_pool,
-                                        float* __restrict__ value_pool,
-                                        float* __restrict__ summaries,
+                                        int ept, int page_size, T* __restrict__ key_pool,
+                                        T* __restrict__ value_pool,
+                                        T* __restrict__ summaries,
                                         int* __restrict__ token_counts,
                                         uint8_t* __restrict__ live) {
   const int gidx = blockIdx.x;
@@ -1092,12 +1445,13 @@ __global__ void append_synthetic_kernel(const int* __restrict__ group_page,
     const float old_c = static_cast<float>(off);
     const float new_c = __fadd_rn(old_c, 1.0f);
     for (int e = threadIdx.x; e < ept; e += blockDim.x) {
-      const float k = decode_value(reqs[i], steps[i], e, 1);
-      key_pool[(size_t(page) * page_size + off) * ept + e] = k;
-      value_pool[(size_t(page) * page_size + off) * ept + e] = decode_value(reqs[i], steps[i], e, 2);
-      float& slot = summaries[sbase + size_t(e / scw) * 128 * scw + (e % scw)];
-      const float s = off == 0 ? 0.0f : slot;
-      slot = __fdiv_rn(__fadd_rn(__fmul_rn(s, old_c), k), new_c);
+      const float k = Kv<T>::round(decode_value(reqs[i], steps[i], e, 1));
+      Kv<T>::put(key_pool, (size_t(page) * page_size + off) * ept + e, k);
+      Kv<T>::put(value_pool, (size_t(page) * page_size + off) * ept + e,
+                 decode_value(reqs[i], steps[i], e, 2));
+      const size_t so = sbase + size_t(e / scw) * 128 * scw + (e % scw);
+      const float s = off == 0 ? 0.0f : Kv<T>::get(summaries, so);
+      Kv<T>::put(summaries, so, __fdiv_rn(__fadd_rn(__fmul_rn(s, old_c), k), new_c));
     }
     last = max(last, off);
   }
@@ -1135,14 +1489,15 @@ __host__ __device__ __forceinline__ uint64_t normal_index(int request, long long
 }
 
 // grid (pages, ceil(E/256)); thread = one element column of one page.
+template <typename T>
 __global__ void generate_normal_kernel(const int* __restrict__ page_ids,
                                        const int* __restrict__ counts,
                                        const int* __restrict__ reqs,
                                        const int* __restrict__ first_token, int ept,
                                        int page_size, uint64_t kmix, uint64_t vmix,
-                                       float* __restrict__ key_pool,
-                                       float* __restrict__ value_pool,
-                                       float* __restrict__ summaries,
+                                       T* __restrict__ key_pool,
+                                       T* __restrict__ value_pool,
+                                       T* __restrict__ summaries,
                                        int* __restrict__ token_counts,
                                        uint8_t* __restrict__ live) {
   const int i = blockIdx.x;
@@ -1153,13 +1508,13 @@ __global__ void generate_normal_kernel(const int* __restrict__ page_ids,
     float sum = 0.0f;
     for (int t = 0; t < n; ++t) {
       const uint64_t idx = normal_index(reqs[i], first_token[i] + t, ept, e);
-      const float k = normal_value(kmix, idx);
-      key_pool[(size_t(page) * page_size + t) * ept + e] = k;
-      value_pool[(size_t(page) * page_size + t) * ept + e] = normal_value(vmix, idx);
+      const float k = Kv<T>::round(normal_value(kmix, idx));
+      Kv<T>::put(key_pool, (size_t(page) * page_size + t) * ept + e, k);
+      Kv<T>::put(value_pool, (size_t(page) * page_size + t) * ept + e, normal_value(vmix, idx));
       sum = __fadd_rn(sum, k);
     }
-    summaries[summary_off(page, e, ept)] =
-        n > 0 ? __fmul_rn(sum, __fdiv_rn(1.0f, static_cast<float>(n))) : 0.0f;
+    Kv<T>::put(summaries, summary_off(page, e, ept),
+               n > 0 ? __fmul_rn(sum, __fdiv_rn(1.0f, static_cast<float>(n))) : 0.0f);
   }
   if (blockIdx.y == 0 && threadIdx.x == 0) {
     token_counts[page] = n;

@@ -181,13 +181,13 @@ def run_reference(args):
 
 # ---------------------------------------------------------------- our arm
 
-def build_workload(dsd, ctx_lens, device):
+def build_workload(dsd, ctx_lens, device, kv_format=0):
     """Allocates the pool, generates K/V on device, sets the request page tables."""
     pages_per = (ctx_lens + P - 1) // P
     cap = int(pages_per.sum())
     ctx = dsd.SparseDecodeContext(H, D, P, K_TOP, cap, BATCH, cap, BATCH * K_TOP,
                                   max_requests=BATCH, max_pages_per_request=int(pages_per.max()),
-                                  device=device)
+                                  device=device, kv_format=kv_format)
     page_ids, counts, reqs, first = [], [], [], []
     nxt = cap - 1
     table = []
@@ -225,7 +225,9 @@ def run_ours(args):
         raise RuntimeError("no sm_100 GPU visible")
     torch.cuda.set_device(local)
     ctx_lens = workload_contexts()
-    ctx, cap, all_ids, all_counts = build_workload(dsd, ctx_lens, local)
+    bf16 = args.kv == "bf16"
+    ctx, cap, all_ids, all_counts = build_workload(dsd, ctx_lens, local,
+                                                   dsd.KV_BF16 if bf16 else dsd.KV_F32)
     qh = queries_host(dsd)
     reqs = np.arange(BATCH, dtype=np.int32)
 
@@ -236,9 +238,11 @@ def run_ours(args):
     C = cap
     S = int(dbg["selected"].size)
     T_sel = int(page_tokens[dbg["selected"]].sum())
-    score_bytes = 4 * E * C + 4 * E * BATCH + 4 * C            # summaries + queries + ids/scores
-    attn_bytes = 8 * E * T_sel + 4 * E * BATCH + 4 * S          # selected K/V + queries + ids
-    step_bytes = 4 * E * C + 8 * E * T_sel + 8 * E * BATCH + 4 * (C + 2 * S + 3 * BATCH + 3)
+    el = 2 if bf16 else 4                                       # bytes per stored element
+    score_bytes = el * E * C + 4 * E * BATCH + 4 * C           # summaries + queries + ids/scores
+    attn_bytes = 2 * el * E * T_sel + 4 * E * BATCH + 4 * S     # selected K/V + queries + ids
+    step_bytes = (el * E * C + 2 * el * E * T_sel + 8 * E * BATCH
+                  + 4 * (C + 2 * S + 3 * BATCH + 3))
 
     dq = torch.from_numpy(qh).cuda(local)
     do = torch.zeros_like(dq)
@@ -304,9 +308,10 @@ def run_ours(args):
         "metric": "sparse decode tokens/s", "value": world * BATCH / (ms_step * 1e-3),
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic (device-generated N(0,1) Irwin-Hall, seed 7)",
+        "dtype": "bf16 pages, f32 arithmetic" if bf16 else "f32",
+        "data": "synthetic (device-generated N(0,1) Irwin-Hall, seed 7)",
         "config": {"workload": "config3: batch 64/GPU, ctx U{16384..32768}, H32 D128 P16 k64",
-                   "requests_per_gpu": BATCH, "candidate_pages_per_gpu": C,
+                   "kv_format": args.kv, "requests_per_gpu": BATCH, "candidate_pages_per_gpu": C,
                    "selected_pages_per_gpu": S, "selected_tokens_per_gpu": T_sel,
                    "step_bytes_per_gpu": step_bytes,
                    "step_hbm_gbps": step_bytes / (ms_step * 1e-3) / 1e9,
@@ -318,14 +323,14 @@ def run_ours(args):
                    "kernel_ms": {"score(+plan)": score_ms,
                                  "select": float(np.mean(per_kernel["topk_ms"])),
                                  "attention(+combine)": attn_ms},
-                   "l2": "inputs larger than L2 (3.7 GB read per step)",
+                   "l2": "inputs larger than L2 (%.1f GB read per step)" % (step_bytes / 1e9),
                    "parallelism": f"request-sharded x{world}",
                    "per_rank_ms_per_step": [round(r["ms_per_step"], 4) for r in per_rank]},
         "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                      "algorithmic_bytes": dom[2],
                      "traffic": (profiled_traffic("attn" if dom[0] == "attention" else "score")
-                                 if BATCH == 64 else None)},
+                                 if BATCH == 64 and not bf16 else None)},
         "e2e": {"value": world * BATCH / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": st["h2d_bytes"] / args.steps,
                 "d2h_bytes_per_step": st["d2h_bytes"] / args.steps},
@@ -432,6 +437,9 @@ def main():
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="requests per GPU (default: the config-3 batch of 64; smaller only "
                          "for profiling captures)")
+    ap.add_argument("--kv", default="f32", choices=["f32", "bf16"],
+                    help="page format of the config-3 step: f32 (the reference's, default) or "
+                         "the opt-in bf16 pages (reported separately, never the headline)")
     args = ap.parse_args()
     BATCH = args.batch
     if args.impl == "reference":

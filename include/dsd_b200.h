@@ -93,6 +93,25 @@ int dsd_ctx_create(int device, const dsd_model_config* config, const dsd_ctx_opt
                    dsd_ctx** out);
 int dsd_ctx_destroy(dsd_ctx* ctx);
 
+/* Page element formats.  DSD_KV_F32 is the reference's format (fp32 pages and
+ * summaries, the parity path).  DSD_KV_BF16 stores K, V and summaries as bf16
+ * (round to nearest even on every store) while queries, dot products, the
+ * softmax and outputs stay fp32; it halves the bytes a step reads.  A key is
+ * rounded before it enters a summary, a summary is computed in fp32 and
+ * rounded once, and a running-mean update reads the stored bf16 mean.  No
+ * reference counterpart: the reference pool is fp32 only
+ * (src/device_page_pool.cpp:241-284); the host API (float payloads in, float
+ * downloads out) is the same for both formats. */
+#define DSD_KV_F32 0
+#define DSD_KV_BF16 1
+/* dsd_ctx_create with an explicit page format (bf16 needs head_dim >= 8).
+ * dsd_ctx_device_pointers then returns the pools as raw storage of that
+ * format (cast the float pointers to __nv_bfloat16* for DSD_KV_BF16). */
+int dsd_ctx_create_ex(int device, const dsd_model_config* config, const dsd_ctx_options* options,
+                      int kv_format, dsd_ctx** out);
+/* The context's DSD_KV_* format, -1 for a null context. */
+int dsd_ctx_kv_format(dsd_ctx* ctx);
+
 /* Device pointers for callers that keep their own data in HBM (bench, tests). */
 int dsd_ctx_device_pointers(dsd_ctx* ctx, float** keys, float** values, float** summaries,
                             int32_t** token_counts);

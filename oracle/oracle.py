@@ -187,6 +187,44 @@ def running_mean_append(summary: np.ndarray, key: np.ndarray, old_count: int) ->
     return s
 
 
+# ---------------------------------------------------------------- bf16 page format
+# The opt-in bf16 page format has no reference counterpart (the reference pool
+# is fp32 only).  Its contract is stated here so the fp32 oracle can check it:
+# every stored K, V and summary element is the fp32 value rounded to nearest
+# even bf16; a page summary is AppendPage's fp32 mean of the ROUNDED keys,
+# rounded once; a running-mean update applies AppendToken's fp32 formula to
+# the stored (bf16) mean and the rounded key, then rounds.  Scoring and
+# attention are the fp32 oracle run over those stored values.
+
+def bf16_round(a: np.ndarray) -> np.ndarray:
+    """Round float32 values to the nearest bf16 (ties to even), as float32."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+    return r.astype(np.uint32).view(np.float32).reshape(np.shape(a))
+
+
+def page_summary_bf16(keys: np.ndarray) -> np.ndarray:
+    return bf16_round(page_summary(bf16_round(keys)))
+
+
+def running_mean_append_bf16(summary: np.ndarray, key: np.ndarray, old_count: int) -> np.ndarray:
+    return bf16_round(running_mean_append(summary, bf16_round(key), old_count))
+
+
+def bf16_batch(b: Batch) -> Batch:
+    """The batch as a bf16-page context stores it (pools rounded, summaries
+    recomputed from the rounded keys); queries and candidates unchanged."""
+    kp = bf16_round(b.key_pool)
+    vp = bf16_round(b.value_pool)
+    summ = np.zeros_like(b.summaries)
+    for p in range(b.capacity):
+        n = int(b.token_counts[p])
+        if n > 0:
+            summ[p] = bf16_round(page_summary(kp[p, :n]))
+    return Batch(b.num_heads, b.head_dim, b.page_size, b.top_k, kp, vp, summ,
+                 b.token_counts.copy(), b.queries, b.cand_offsets, b.cand_ids)
+
+
 def deterministic_token_vector(count, request_id, decode_step, stream) -> np.ndarray:
     out = np.zeros(count, np.float32)
     lib().orc_deterministic_token_vector(count, request_id, decode_step, stream, fp(out))

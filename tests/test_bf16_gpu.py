@@ -1,0 +1,126 @@
+"""The opt-in bf16 page format vs the oracle (GPU).
+
+A bf16-page context stores K, V and summaries rounded to nearest-even bf16
+and computes in fp32.  The checker is the fp32 oracle run over what such a
+context must store (oracle.bf16_batch / bf16_round / page_summary_bf16 /
+running_mean_append_bf16): stored values bit for bit, selected ids equal in
+order, scores bit for bit, outputs <= 1e-4 max-abs.  The fp32 format stays
+the default and the reference-parity path; nothing here changes it.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as o
+from test_continuous_gpu import run_continuous
+from test_shapes_gpu import random_batch
+
+pytestmark = pytest.mark.gpu
+
+
+def bf16_ctx(dsd, b, top_k=None, **kw):
+    k = b.top_k if top_k is None else top_k
+    n = np.diff(b.cand_offsets)
+    opts = dict(capacity_pages=b.capacity, max_batch=max(1, b.batch),
+                max_candidates=max(1, int(n.sum())),
+                max_selected=max(1, int(np.minimum(n, k).sum())), kv_format=dsd.KV_BF16)
+    opts.update(kw)
+    return dsd.SparseDecodeContext(b.num_heads, b.head_dim, b.page_size, k, **opts)
+
+
+def check(res, ref, tol=1e-4):
+    sel, so, out, scores = o.sparse_decode(ref)
+    assert np.array_equal(res["scores"].view(np.uint32), scores.view(np.uint32))
+    assert np.array_equal(res["selected"], sel)
+    assert float(np.abs(res["outputs"] - out).max()) <= tol
+
+
+CASES = [
+    ("ragged", (4, 16, 16, 3, 4, 33, 97, 7)),
+    ("wide", (2, 64, 8, 4, 2, 17, 45, 17)),
+    ("larger_candidates", (2, 16, 8, 8, 2, 160, 184, 123)),
+    ("cfg2", (32, 128, 16, 8, 16, 512, 2048, 7)),
+]
+
+
+@pytest.mark.parametrize("name,cfg", CASES, ids=[c[0] for c in CASES])
+def test_bf16_decode_matches_oracle_on_stored_values(dsd, name, cfg):
+    b = o.synthetic_batch(*cfg)
+    ref = o.bf16_batch(b)
+    with bf16_ctx(dsd, b) as ctx:
+        assert ctx.lib.dsd_ctx_kv_format(ctx.h) == dsd.KV_BF16
+        ctx.upload_pool(b.key_pool, b.value_pool, b.token_counts)
+        for p in range(0, b.capacity, max(1, b.capacity // 16)):
+            k, v, s, n = ctx.download_page(p)
+            assert n == ref.token_counts[p]
+            assert np.array_equal(k[:n].view(np.uint32), ref.key_pool[p, :n].view(np.uint32))
+            assert np.array_equal(v[:n].view(np.uint32), ref.value_pool[p, :n].view(np.uint32))
+            assert np.array_equal(s.view(np.uint32), ref.summaries[p].view(np.uint32)), p
+        check(ctx.decode_batch(b.queries, b.cand_offsets, b.cand_ids), ref)
+
+
+def test_bf16_dense_mode(dsd):
+    b = o.synthetic_batch(8, 32, 16, 4, 6, 40, 300, 3)
+    ref = o.bf16_batch(b)
+    with bf16_ctx(dsd, b, max_selected=len(b.cand_ids)) as ctx:
+        ctx.upload_pool(b.key_pool, b.value_pool, b.token_counts)
+        ctx.set_dense(True)
+        res = ctx.decode_batch(b.queries, b.cand_offsets, b.cand_ids)
+        assert float(np.abs(res["outputs"] - o.dense_decode(ref)).max()) <= 1e-4
+
+
+@pytest.mark.parametrize("H,D,P", [(4, 8, 16), (16, 16, 4), (64, 128, 2), (8, 64, 32), (3, 32, 1)],
+                         ids=["d8", "d16", "e8192", "p32", "p1_h3"])
+def test_bf16_head_and_page_shapes(dsd, H, D, P):
+    rng = np.random.default_rng(H * 1000 + D * 10 + P)
+    b = random_batch(rng, H, D, P, 5, [3, 17, 40, 9])
+    with bf16_ctx(dsd, b) as ctx:
+        ctx.upload_pool(b.key_pool, b.value_pool, b.token_counts)
+        check(ctx.decode_batch(b.queries, b.cand_offsets, b.cand_ids), o.bf16_batch(b))
+
+
+def test_bf16_rejects_head_dim_4(dsd):
+    with pytest.raises(dsd.InvalidArgument):
+        dsd.SparseDecodeContext(4, 4, 8, 2, 8, 1, 8, 2, kv_format=dsd.KV_BF16)
+
+
+def test_bf16_generators_round_on_store(dsd):
+    E, P = 64, 8
+    with dsd.SparseDecodeContext(4, 16, P, 3, 16, 4, 64, 12, kv_format=dsd.KV_BF16) as ctx:
+        ctx.prefill_synthetic([5, 6, 7], [8, 8, 3], request_id=11)
+        ctx.generate_normal([3, 4], [8, 5], [2, 2], [0, 8], seed=9)
+        for i, (pid, n) in enumerate([(5, 8), (6, 8), (7, 3)]):
+            k, v, s, cnt = ctx.download_page(pid)
+            ek = o.synthetic_prompt(11, i, n, E, 1)
+            assert cnt == n
+            assert np.array_equal(k[:n], o.bf16_round(ek))
+            assert np.array_equal(v[:n], o.bf16_round(o.synthetic_prompt(11, i, n, E, 2)))
+            assert np.array_equal(s.view(np.uint32), o.page_summary_bf16(ek).view(np.uint32))
+        for pid, first, n in ((3, 0, 8), (4, 8, 5)):
+            k, v, s, cnt = ctx.download_page(pid)
+            ek = o.normal_fill(9, 1, (2 << 40) + first * E, n * E).reshape(n, E)
+            assert np.array_equal(k[:n], o.bf16_round(ek))
+            assert np.array_equal(s.view(np.uint32), o.page_summary_bf16(ek).view(np.uint32))
+        # synthetic decode tokens: running mean over the stored bf16 mean
+        ctx.append_tokens_synthetic([7, 7], [3, 4], [11, 11], [0, 1])
+        k, v, s, cnt = ctx.download_page(7)
+        summ = o.page_summary_bf16(o.synthetic_prompt(11, 2, 3, E, 1))
+        for off, step in ((3, 0), (4, 1)):
+            key = o.synthetic_decode(11, step, E, 1)
+            assert np.array_equal(k[off], o.bf16_round(key))
+            summ = o.running_mean_append_bf16(summ, key, off)
+        assert cnt == 5 and np.array_equal(s.view(np.uint32), summ.view(np.uint32))
+        ctx.free_pages([7])
+        _, _, s, _ = ctx.download_page(7)
+        assert not s.any()
+
+
+@pytest.mark.parametrize("split_step,depth", [(False, 1), (True, 2)],
+                         ids=["sync_step", "two_steps_in_flight"])
+def test_bf16_continuous_serving(dsd, split_step, depth):
+    assert run_continuous(dsd, 4, 16, 8, 3, 10, 4, 6, 20, 60, 3, 10, 7, split_step, depth,
+                          kv_format=dsd.KV_BF16) > 5
+
+
+def test_bf16_continuous_config4_shape(dsd):
+    assert run_continuous(dsd, 32, 128, 16, 8, 12, 6, 8, 1024, 4096, 4, 10, 7,
+                          kv_format=dsd.KV_BF16) > 5

@@ -21,7 +21,9 @@ pytestmark = pytest.mark.gpu
 class HostMirror:
     """PagePool + PagedKvCache bookkeeping with flat pools (oracle formulas)."""
 
-    def __init__(self, cap, P, E):
+    def __init__(self, cap, P, E, bf16=False):
+        # bf16: the stored-format rounding of a bf16-page context
+        self.rnd = o.bf16_round if bf16 else (lambda a: np.asarray(a, np.float32))
         self.free = list(range(cap))           # pops from the back: LIFO
         self.kp = np.zeros((cap, P, E), np.float32)
         self.vp = np.zeros((cap, P, E), np.float32)
@@ -47,9 +49,10 @@ class HostMirror:
             pid = pages[-1]
             new = False
         off = int(self.tc[pid])
+        key = self.rnd(key)
         self.kp[pid, off] = key
-        self.vp[pid, off] = value
-        self.summ[pid] = o.running_mean_append(self.summ[pid], key, off)
+        self.vp[pid, off] = self.rnd(value)
+        self.summ[pid] = self.rnd(o.running_mean_append(self.summ[pid], key, off))
         self.tc[pid] = off + 1
         return pid, off, new
 
@@ -63,7 +66,7 @@ class HostMirror:
 
 
 def run_continuous(dsd, H, D, P, K, n_req, max_active, window, pmin, pmax, dmin, dmax, seed,
-                   split_step=False, depth=1):
+                   split_step=False, depth=1, kv_format=0):
     E = H * D
     w = o.continuous_workload(H, D, n_req, window, pmin, pmax, dmin, dmax, seed)
     ids, arr, pt, ds = w["request_ids"], w["arrival_steps"], w["prompt_tokens"], w["decode_steps"]
@@ -72,10 +75,10 @@ def run_continuous(dsd, H, D, P, K, n_req, max_active, window, pmin, pmax, dmin,
     max_pages = int(max(pages_for(int(a)) + pages_for(int(b)) for a, b in zip(pt, ds)))
     cap = min(int(sum(pages_for(int(a)) + pages_for(int(b)) for a, b in zip(pt, ds))),
               max_active * max_pages)
-    host = HostMirror(cap, P, E)
+    host = HostMirror(cap, P, E, bf16=kv_format == dsd.KV_BF16)
     ctx = dsd.SparseDecodeContext(H, D, P, K, cap, max_active, max_active * max_pages,
                                   max_active * min(K, max_pages), max_requests=max_active,
-                                  max_pages_per_request=max_pages)
+                                  max_pages_per_request=max_pages, kv_format=kv_format)
     active = []            # dicts: rid, remaining, step, query
     nxt, step, checked = 0, 0, 0
     inflight = []          # oracle results of steps begun but not yet ended
@@ -102,9 +105,9 @@ def run_continuous(dsd, H, D, P, K, n_req, max_active, window, pmin, pmax, dmin,
             vals = w["prompt_values"][offs[i]:offs[i + 1]]
             t0 = 0
             for pid, c in zip(pids, counts):
-                host.kp[pid, :c] = keys[t0:t0 + c]
-                host.vp[pid, :c] = vals[t0:t0 + c]
-                host.summ[pid] = o.page_summary(keys[t0:t0 + c])
+                host.kp[pid, :c] = host.rnd(keys[t0:t0 + c])
+                host.vp[pid, :c] = host.rnd(vals[t0:t0 + c])
+                host.summ[pid] = host.rnd(o.page_summary(host.kp[pid, :c]))
                 host.tc[pid] = c
                 t0 += c
             ctx.upload_pages(pids, counts, keys, vals)
