@@ -88,7 +88,7 @@ size_t AlignUp(size_t x, size_t a) { return (x + a - 1) / a * a; }
 // Attention launch shape: NV float4 per lane, LP = D/(4*NV) lanes per head,
 // SLOTS items per thread, tokens per stage and dynamic shared memory.
 struct AttnShape {
-  int nv = 1, slots = 1, tps = 1;
+  int nv = 1, slots = 1, tps = 1, nstages = 0;
   size_t smem = 0;
 };
 
@@ -103,9 +103,12 @@ AttnShape MakeAttnShape(int num_heads, int head_dim, int page_size, bool bf16 = 
     const int slots = (items + dsdk::kAttnThreads - 1) / dsdk::kAttnThreads;
     if (slots > 4) Fail(DSD_EINVAL, "num_heads*head_dim is too large for the attention kernel");
     a.slots = slots <= 1 ? 1 : slots <= 2 ? 2 : 4;
-    a.tps = std::max(1, std::min({page_size, dsdk::kAttnStageFloats * 4 / (2 * ept * 2),
-                                  dsdk::kAttnMaxTokensPerStage}));
-    a.smem = size_t(dsdk::kAttnStages) * 2 * a.tps * ept * 2 + dsdk::kAttnStages * 8;
+    // 32 KiB stages, as many as fit in ~200 KiB (at most 8)
+    a.tps = std::max(1, std::min({page_size, 65536 / (2 * ept * 2),
+                                  dsdk::kAttnBfRegTokens}));
+    const size_t stage = size_t(2) * a.tps * ept * 2;
+    a.nstages = int(std::max<size_t>(2, std::min<size_t>(8, (200u << 10) / stage)));
+    a.smem = size_t(a.nstages) * (stage + 16);
     return a;
   }
   const int G = head_dim / 4;
@@ -135,6 +138,30 @@ void SetAllAttnAttributes(size_t smem) {
   SetAttnAttr<4, 1>(smem); SetAttnAttr<4, 2>(smem);
 }
 
+constexpr size_t ScoreBf16Smem(int stages) { return stages * dsdk::kScoreBfStageBytes; }
+
+// bf16 scoring runs 4 CTAs per SM with a 3-stage ring each: the per-thread
+// dependent add chain is twice as long per byte as in fp32, so it needs more
+// warps in flight (measured at config 3: 2 CTAs x 5 stages 0.178 ms, 3 x 3
+// 0.149 ms, 4 x 3 0.145 ms).
+constexpr int kScoreBf16Ctas = 4;
+constexpr int kScoreBf16Stages = 3;
+
+void SetScoreBf16Attributes() {
+  Check(cudaFuncSetAttribute(dsdk::score_kernel_bf16<kScoreBf16Stages, kScoreBf16Ctas>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(ScoreBf16Smem(kScoreBf16Stages))),
+        "smem attribute");
+}
+
+void LaunchScoreBf16(int num_sms, cudaStream_t st, const dsdk::StepPlan& plan, const float* q,
+                     const __nv_bfloat16* summ, int ept, float scale, float* scores, int part,
+                     int nparts) {
+  dsdk::score_kernel_bf16<kScoreBf16Stages, kScoreBf16Ctas>
+      <<<kScoreBf16Ctas * num_sms, dsdk::kScoreThreads, ScoreBf16Smem(kScoreBf16Stages), st>>>(
+          plan, q, summ, ept, scale, scores, part, nparts);
+}
+
 template <int NV, int S>
 void SetAttnAttrBf16(size_t smem) {
   Check(cudaFuncSetAttribute(dsdk::attn_kernel_bf16<NV, S>,
@@ -154,8 +181,8 @@ void LaunchAttnBf16(const AttnShape& a, int grid, cudaStream_t st, const dsdk::S
                     int part, int nparts) {
 #define DSD_ATTN_CASE(NV, S)                                                                  \
   if (a.nv == NV && a.slots == S) {                                                           \
-    dsdk::attn_kernel_bf16<NV, S><<<grid, dsdk::kAttnThreads, a.smem, st>>>(                  \
-        plan, q, k, v, tc, sel, pacc, pml, H, D, P, a.tps, scale, part, nparts);              \
+    dsdk::attn_kernel_bf16<NV, S><<<grid, dsdk::kAttnBfThreads, a.smem, st>>>(                \
+        plan, q, k, v, tc, sel, pacc, pml, H, D, P, a.tps, a.nstages, scale, part, nparts);   \
     return;                                                                                   \
   }
   DSD_ATTN_CASE(1, 1) DSD_ATTN_CASE(1, 2) DSD_ATTN_CASE(1, 4)
@@ -447,8 +474,9 @@ void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool cap
   const int comb_grid = std::max(1, std::min((pairs + 7) / 8, 8 * c->num_sms));
   const int nparts = timed ? 1 : kStepParts;
   if (timed) RecordEvent(c, 0, capturing);
+  const int score_ctas = (c->kv_format == DSD_KV_BF16 ? kScoreBf16Ctas : 2) * c->num_sms;
   dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, c->stream>>>(plan, c->cfg.top_k_pages,
-                                                             target_units, 2 * c->num_sms);
+                                                             target_units, score_ctas);
   if (nparts > 1) {
     Check(cudaEventRecord(c->ev_fork, c->stream), "fork");
     Check(cudaStreamWaitEvent(c->stream2, c->ev_fork, 0), "fork wait");
@@ -456,9 +484,9 @@ void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool cap
   for (int part = 0; part < nparts; ++part) {
     cudaStream_t st = part == 0 ? c->stream : c->stream2;
     if (c->kv_format == DSD_KV_BF16)
-      dsdk::score_kernel_bf16<<<2 * c->num_sms, dsdk::kScoreThreads, dsdk::kScoreBfSmem, st>>>(
-          plan, d_q, static_cast<const __nv_bfloat16*>(c->summaries), c->ept, c->scale,
-          c->d_scores, part, nparts);
+      LaunchScoreBf16(c->num_sms, st, plan, d_q,
+                      static_cast<const __nv_bfloat16*>(c->summaries), c->ept, c->scale,
+                      c->d_scores, part, nparts);
     else
       dsdk::score_kernel<<<2 * c->num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, st>>>(
           plan, d_q, static_cast<const float*>(c->summaries), c->ept, c->scale, c->d_scores,
@@ -865,9 +893,7 @@ int dsd_ctx_create_ex(int device, const dsd_model_config* config, const dsd_ctx_
       Check(cudaFuncSetAttribute(dsdk::score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)dsdk::kScoreSmem), "smem attribute");
       if (kv_format == DSD_KV_BF16) {
-        Check(cudaFuncSetAttribute(dsdk::score_kernel_bf16,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   int(dsdk::kScoreBfSmem)), "smem attribute");
+        SetScoreBf16Attributes();
         SetAllAttnAttributesBf16(c->attn.smem);
       } else {
         SetAllAttnAttributes(c->attn.smem);

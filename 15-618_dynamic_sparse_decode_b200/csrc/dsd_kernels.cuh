@@ -307,23 +307,33 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(StepPlan plan, int t
   // Score tile size: the smallest ts <= kScoreTile whose tile count fits a
   // whole number of waves over the score grid, so every CTA runs the same
   // number of (slightly shorter) tiles instead of a ragged last wave.
-  __shared__ int s_count;
+  // The 32 warps test 32 candidate sizes at a time.
+  __shared__ int s_n[kMaxBatch];
+  __shared__ int s_best;
   const int waves = max(1, (tot[0] + kScoreTile * score_grid - 1) / (kScoreTile * score_grid));
   const int target_tiles = waves * score_grid;
-  int ts = max(1, min(kScoreTile, (tot[0] + target_tiles - 1) / max(1, target_tiles)));
-  for (; ts < kScoreTile; ++ts) {
-    if (threadIdx.x == 0) s_count = 0;
-    __syncthreads();
-    const int c = (n + ts - 1) / ts;
-    int wsum = c;
+  const int ts0 = max(1, min(kScoreTile, (tot[0] + target_tiles - 1) / max(1, target_tiles)));
+  if (r < kMaxBatch) s_n[r] = n;
+  if (threadIdx.x == 0) s_best = kScoreTile;
+  __syncthreads();
+  {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int base_ts = ts0; base_ts < kScoreTile; base_ts += kPlanThreads / 32) {
+      const int cand = base_ts + warp;
+      if (cand < kScoreTile) {
+        int c = 0;
+        for (int i = lane; i < B; i += 32) c += (s_n[i] + cand - 1) / cand;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
-    if ((threadIdx.x & 31) == 0 && wsum) atomicAdd(&s_count, wsum);
-    __syncthreads();
-    const int count = s_count;
-    __syncthreads();
-    if (count <= target_tiles) break;
+        for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+        if (lane == 0 && c <= target_tiles) atomicMin(&s_best, cand);
+      }
+      __syncthreads();
+      const int best = s_best;
+      __syncthreads();
+      if (best < kScoreTile) break;
+    }
   }
+  const int ts = s_best;
   int t1[1] = {dense ? 0 : (n + ts - 1) / ts};
   int ttot[1];
   block_exclusive_scan<1>(t1, ttot);
@@ -500,12 +510,11 @@ __global__ void __launch_bounds__(kScoreThreads, 2) score_kernel(
 // the bytes).  Each bf16 element widens to fp32 exactly; the dot product is
 // the same sequential round-to-nearest chain as score_kernel.
 constexpr int kScoreBfRowStride = kScoreChunk + 8;  // bf16 elements per smem row
-constexpr int kScoreBfStages = 5;
 constexpr size_t kScoreBfStageBytes =
     size_t(kScoreTile) * kScoreBfRowStride * 2 + size_t(kScoreChunk) * 4;
-constexpr size_t kScoreBfSmem = kScoreBfStages * kScoreBfStageBytes;
 
-__global__ void __launch_bounds__(kScoreThreads, 2) score_kernel_bf16(
+template <int STAGES, int MINB>
+__global__ void __launch_bounds__(kScoreThreads, MINB) score_kernel_bf16(
     StepPlan plan, const float* __restrict__ queries, const __nv_bfloat16* __restrict__ summaries,
     int ept, float scale, float* __restrict__ scores, int part, int nparts) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -566,12 +575,12 @@ __global__ void __launch_bounds__(kScoreThreads, 2) score_kernel_bf16(
       }
     }
     cp_async_commit();
-    ld_slot = ld_slot + 1 == kScoreBfStages ? 0 : ld_slot + 1;
+    ld_slot = ld_slot + 1 == STAGES ? 0 : ld_slot + 1;
   };
 
   load_tile();
 #pragma unroll 1
-  for (int i = 0; i < kScoreBfStages - 1; ++i) issue();
+  for (int i = 0; i < STAGES - 1; ++i) issue();
 
   int slot = 0;
   for (int tile = tile_begin + blockIdx.x; tile < total_tiles; tile += gridDim.x) {
@@ -580,7 +589,7 @@ __global__ void __launch_bounds__(kScoreThreads, 2) score_kernel_bf16(
     const int nvalid = min(ts, plan.n_cand[r] - c0);
     float acc = 0.0f;
     for (int ch = 0; ch < nchunks; ++ch) {
-      cp_async_wait<kScoreBfStages - 2>();
+      cp_async_wait<STAGES - 2>();
       __syncthreads();
       issue();
       const unsigned char* st = smem_raw + size_t(slot) * kScoreBfStageBytes;
@@ -608,7 +617,7 @@ __global__ void __launch_bounds__(kScoreThreads, 2) score_kernel_bf16(
           for (int i = 0; i < cw / 8; ++i) step8(i);
         }
       }
-      slot = slot + 1 == kScoreBfStages ? 0 : slot + 1;
+      slot = slot + 1 == STAGES ? 0 : slot + 1;
     }
     if (tid < nvalid) scores[plan.score_off[r] + c0 + tid] = __fmul_rn(acc, scale);
   }
@@ -995,38 +1004,64 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(
   }
 }
 
-// bf16 pages: attn_kernel with 16-byte vectors of 8 bf16 instead of float4
-// (a head's D/8 vectors over LP = D/(8*NV) lanes, so the 8 lanes of a quarter
-// warp again read 128 contiguous bytes of one row), stages of `tps` K rows
-// then `tps` V rows in bf16, and fp32 queries, logits, softmax and partials.
-__device__ __forceinline__ void unpack_bf16x8(const uint4 raw, float (&f)[8]) {
+// bf16 pages: split-K flash decode with 16-byte vectors of 8 bf16 (a head's
+// D/8 vectors over LP = D/(8*NV) lanes, so the 8 lanes of a quarter warp
+// read 128 contiguous bytes of one row) and fp32 queries, logits, softmax
+// and partials.  Warp-specialised: kAttnThreads consumer threads plus one
+// producer warp whose lane 0 walks the CTA's units and keeps `nstages`
+// stages (tps K rows then tps V rows of one page, two cp.async.bulk copies)
+// in flight.  Consumers release a stage through its `empty` mbarrier (one
+// arrival per consumer warp), so refills never wait for a CTA-wide barrier
+// and the producer's page-table loads stay off the consumers' path.
+constexpr int kAttnBfThreads = kAttnThreads + 32;
+constexpr int kAttnBfRegTokens = 4;                 // tokens per bf16 stage (V held in registers)
+
+// 8 bf16 -> 4 float2 (elements 2h, 2h+1); widening is exact (16-bit shift / mask)
+__device__ __forceinline__ void unpack_bf16x8(const uint4 raw, float2 (&f)[4]) {
   const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-  for (int h = 0; h < 4; ++h) {
-    f[2 * h] = __uint_as_float(w[h] << 16);
-    f[2 * h + 1] = __uint_as_float(w[h] & 0xffff0000u);
-  }
+  for (int h = 0; h < 4; ++h)
+    f[h] = make_float2(__uint_as_float(w[h] << 16), __uint_as_float(w[h] & 0xffff0000u));
+}
+
+// The bf16 attention keeps its softmax in base 2: logits are scaled by
+// log2(e) and weights come from the hardware 2^x approximation
+// (ex2.approx.ftz, relative error ~2^-22); m is stored back in natural-log
+// units.  2^(x*log2 e) = e^x, so the outputs are the same softmax.
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 template <int NV, int SLOTS>
-__global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel_bf16(
+__global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_bf16(
     StepPlan plan, const float* __restrict__ queries, const __nv_bfloat16* __restrict__ key_pool,
     const __nv_bfloat16* __restrict__ value_pool, const int* __restrict__ token_counts,
     const int* __restrict__ selected, float* __restrict__ part_acc, float* __restrict__ part_ml,
-    int num_heads, int head_dim, int page_size, int tps, float scale, int part, int nparts) {
+    int num_heads, int head_dim, int page_size, int tps, int nstages, float scale, int part,
+    int nparts) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  constexpr int kMaxTps = kAttnMaxTokensPerStage;
+  constexpr int kConsumerWarps = kAttnThreads / 32;
   const int ept = num_heads * head_dim;
   const int vec = ept >> 3;                       // 16-byte vectors per token row
   const int G = head_dim >> 3;                    // vectors per head
   const int LP = G / NV;                          // lanes per head
   const size_t stage_elems = size_t(2) * tps * ept;
   __nv_bfloat16* stages = reinterpret_cast<__nv_bfloat16*>(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + kAttnStages * stage_elems * 2);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + nstages * stage_elems * 2);
+  uint64_t* empty = full + nstages;
 
   const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const float scale_log2 = scale * kLog2e;
   if (tid == 0) {
-    for (int s = 0; s < kAttnStages; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < nstages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
     fence_barrier_init();
   }
   __syncthreads();
@@ -1037,28 +1072,33 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel_bf16(
   const int unit_begin = plan.unit_off[r_begin];
   const int total_units = plan.unit_off[r_end];
   const int ppu = plan.misc[0];
-  const size_t page_elems = size_t(page_size) * ept;
   int* status = plan.status;
 
-  AttnWalk w{unit_begin + static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x), 0, 0, 0, 0,
-             0, false};
-  auto issue = [&](int s) {
-    const int nt = min(tps, w.n - w.t0);
-    const uint32_t bytes = uint32_t(nt) * uint32_t(ept) * 2u;
-    __nv_bfloat16* st = stages + size_t(s) * stage_elems;
-    const size_t src = size_t(w.page) * page_elems + size_t(w.t0) * ept;
-    mbar_arrive_expect_tx(&full[s], 2u * bytes);
-    bulk_g2s(st, key_pool + src, bytes, &full[s]);
-    bulk_g2s(st + size_t(tps) * ept, value_pool + src, bytes, &full[s]);
-  };
-  if (tid == 0) {
-    for (int s = 0; s < kAttnStages; ++s) {
-      if (!attn_walk_next(w, plan, B, total_units, ppu, tps, page_size, selected, token_counts))
-        break;
-      issue(s);
+  if (tid >= kAttnThreads) {
+    // ---- producer warp
+    if (lane == 0) {
+      const size_t page_elems = size_t(page_size) * ept;
+      AttnWalk w{unit_begin + static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x), 0, 0,
+                 0, 0, 0, false};
+      for (uint32_t g = 0;; ++g) {
+        if (!attn_walk_next(w, plan, B, total_units, ppu, tps, page_size, selected, token_counts))
+          break;
+        const int s = g % nstages;
+        const uint32_t use = g / nstages;
+        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, status)) break;
+        const int nt = min(tps, w.n - w.t0);
+        const uint32_t bytes = uint32_t(nt) * uint32_t(ept) * 2u;
+        __nv_bfloat16* st = stages + size_t(s) * stage_elems;
+        const size_t src = size_t(w.page) * page_elems + size_t(w.t0) * ept;
+        mbar_arrive_expect_tx(&full[s], 2u * bytes);
+        bulk_g2s(st, key_pool + src, bytes, &full[s]);
+        bulk_g2s(st + size_t(tps) * ept, value_pool + src, bytes, &full[s]);
+      }
     }
+    return;
   }
 
+  // ---- consumers
   int colv[SLOTS][NV];
   bool ok[SLOTS];
 #pragma unroll
@@ -1070,14 +1110,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel_bf16(
     for (int j = 0; j < NV; ++j) colv[m][j] = ok[m] ? head * G + li + LP * j : 0;
   }
 
-  uint32_t g = 0;
-  bool alive = true;
-  for (int u = unit_begin + blockIdx.x; u < total_units && alive; u += gridDim.x) {
-    int r, p_begin, p_end;
-    attn_unit_range(plan, B, ppu, u, &r, &p_begin, &p_end);
-    float q[SLOTS][NV][8], acc[SLOTS][NV][8];
-    float mrun[SLOTS], lrun[SLOTS];
-    const float4* qrow = reinterpret_cast<const float4*>(queries + size_t(r) * ept);
+  // The unit's request, page range, per-page token counts (lane j of every
+  // warp holds page j's count) and this thread's query pieces are loaded one
+  // unit ahead, so no global-load latency sits between two units.
+  // Query element pairs (2x, 2x+1) are float2 for the packed f32x2 math.
+  float2 nq[SLOTS][NV][4];
+  auto unit_info = [&](int uu, int& rr, int& pb, int& pe) {
+    attn_unit_range(plan, B, ppu, uu, &rr, &pb, &pe);
+    const float4* qrow = reinterpret_cast<const float4*>(queries + size_t(rr) * ept);
 #pragma unroll
     for (int m = 0; m < SLOTS; ++m) {
 #pragma unroll
@@ -1085,70 +1125,113 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel_bf16(
         const float4 a = ok[m] ? __ldg(qrow + 2 * colv[m][j]) : make_float4(0.f, 0.f, 0.f, 0.f);
         const float4 b =
             ok[m] ? __ldg(qrow + 2 * colv[m][j] + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
-        q[m][j][0] = a.x; q[m][j][1] = a.y; q[m][j][2] = a.z; q[m][j][3] = a.w;
-        q[m][j][4] = b.x; q[m][j][5] = b.y; q[m][j][6] = b.z; q[m][j][7] = b.w;
+        nq[m][j][0] = make_float2(a.x, a.y); nq[m][j][1] = make_float2(a.z, a.w);
+        nq[m][j][2] = make_float2(b.x, b.y); nq[m][j][3] = make_float2(b.z, b.w);
+      }
+    }
+    return pb + lane < pe ? min(__ldg(token_counts + __ldg(selected + pb + lane)), page_size) : 0;
+  };
+  int nx_r = 0, nx_pb = 0, nx_pe = 0, nx_cnt = 0;
+  if (unit_begin + static_cast<int>(blockIdx.x) < total_units)
+    nx_cnt = unit_info(unit_begin + blockIdx.x, nx_r, nx_pb, nx_pe);
+
+  uint32_t g = 0;
+  bool alive = true;
+  for (int u = unit_begin + blockIdx.x; u < total_units && alive; u += gridDim.x) {
+    const int p_begin = nx_pb, p_end = nx_pe, cnt = nx_cnt;
+    float2 q[SLOTS][NV][4], acc[SLOTS][NV][4];
+    float mrun[SLOTS], lrun[SLOTS];
 #pragma unroll
-        for (int x = 0; x < 8; ++x) acc[m][j][x] = 0.f;
+    for (int m = 0; m < SLOTS; ++m) {
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          q[m][j][x] = nq[m][j][x];
+          acc[m][j][x] = make_float2(0.f, 0.f);
+        }
       }
       mrun[m] = -INFINITY;
       lrun[m] = 0.f;
     }
+    if (u + static_cast<int>(gridDim.x) < total_units)
+      nx_cnt = unit_info(u + gridDim.x, nx_r, nx_pb, nx_pe);
     for (int p = p_begin; p < p_end && alive; ++p) {
-      const int page = __ldg(selected + p);
-      const int n = min(__ldg(token_counts + page), page_size);
+      const int n = __shfl_sync(0xffffffffu, cnt, p - p_begin);
       for (int t0 = 0; t0 < n; t0 += tps, ++g) {
-        const int s = g % kAttnStages;
-        if (!mbar_wait(&full[s], (g / kAttnStages) & 1, status)) { alive = false; break; }
+        const int s = g % nstages;
+        if (!mbar_wait(&full[s], (g / nstages) & 1, status)) { alive = false; break; }
         const int nt = min(tps, n - t0);
         const uint4* kst = reinterpret_cast<const uint4*>(stages + size_t(s) * stage_elems);
         const uint4* vst = kst + size_t(tps) * vec;
+        // V pieces go to registers and this lane's q.k partials are formed
+        // from K in place; then the stage is released, before the cross-lane
+        // reduction, the softmax and the V accumulation.  A stage is held only
+        // for its shared-memory reads and the partial dot products, so more of
+        // the ring stays in flight.
+        uint4 vreg[SLOTS][kAttnBfRegTokens][NV];
+        float logit[SLOTS][kAttnBfRegTokens];
 #pragma unroll
         for (int m = 0; m < SLOTS; ++m) {
-          float logit[kMaxTps];
-          float cmax = mrun[m];
 #pragma unroll
-          for (int t = 0; t < kMaxTps; ++t) {
+          for (int t = 0; t < kAttnBfRegTokens; ++t) {
             if (t < nt) {
-              float d = 0.f;
+              float2 d2 = make_float2(0.f, 0.f);
 #pragma unroll
               for (int j = 0; j < NV; ++j) {
-                float kk[8];
+                vreg[m][t][j] = vst[size_t(t) * vec + colv[m][j]];
+                float2 kk[4];
                 unpack_bf16x8(kst[size_t(t) * vec + colv[m][j]], kk);
 #pragma unroll
-                for (int x = 0; x < 8; ++x) d += q[m][j][x] * kk[x];
+                for (int x = 0; x < 4; ++x) d2 = __ffma2_rn(q[m][j][x], kk[x], d2);
               }
-              for (int o = LP >> 1; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-              logit[t] = d * scale;
-              cmax = fmaxf(cmax, logit[t]);
+              logit[m][t] = d2.x + d2.y;
             }
           }
-          const float alpha = expf(mrun[m] - cmax);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);   // release: this warp's reads are done
+#pragma unroll
+        for (int m = 0; m < SLOTS; ++m) {
+#pragma unroll
+          for (int t = 0; t < kAttnBfRegTokens; ++t) {
+            if (t < nt) {
+              float d = logit[m][t];
+              for (int o = LP >> 1; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+              logit[m][t] = d * scale_log2;     // base-2 logits
+            }
+          }
+        }
+#pragma unroll
+        for (int m = 0; m < SLOTS; ++m) {
+          float cmax = mrun[m];
+#pragma unroll
+          for (int t = 0; t < kAttnBfRegTokens; ++t)
+            if (t < nt) cmax = fmaxf(cmax, logit[m][t]);
+          const float alpha = fast_exp2(mrun[m] - cmax);
           float l = lrun[m] * alpha;
+          const float2 alpha2 = make_float2(alpha, alpha);
 #pragma unroll
           for (int j = 0; j < NV; ++j)
 #pragma unroll
-            for (int x = 0; x < 8; ++x) acc[m][j][x] *= alpha;
+            for (int x = 0; x < 4; ++x) acc[m][j][x] = __fmul2_rn(acc[m][j][x], alpha2);
 #pragma unroll
-          for (int t = 0; t < kMaxTps; ++t) {
+          for (int t = 0; t < kAttnBfRegTokens; ++t) {
             if (t < nt) {
-              const float beta = expf(logit[t] - cmax);
+              const float beta = fast_exp2(logit[m][t] - cmax);
               l += beta;
+              const float2 beta2 = make_float2(beta, beta);
 #pragma unroll
               for (int j = 0; j < NV; ++j) {
-                float vv[8];
-                unpack_bf16x8(vst[size_t(t) * vec + colv[m][j]], vv);
+                float2 vv[4];
+                unpack_bf16x8(vreg[m][t][j], vv);
 #pragma unroll
-                for (int x = 0; x < 8; ++x) acc[m][j][x] += beta * vv[x];
+                for (int x = 0; x < 4; ++x) acc[m][j][x] = __ffma2_rn(beta2, vv[x], acc[m][j][x]);
               }
             }
           }
           lrun[m] = l;
           mrun[m] = cmax;
-        }
-        __syncthreads();  // every thread is done with stage s
-        if (tid == 0) {
-          if (attn_walk_next(w, plan, B, total_units, ppu, tps, page_size, selected, token_counts))
-            issue(s);
         }
       }
     }
@@ -1158,14 +1241,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel_bf16(
       float4* pa = reinterpret_cast<float4*>(part_acc + size_t(u) * ept);
 #pragma unroll
       for (int j = 0; j < NV; ++j) {
-        pa[2 * colv[m][j]] = make_float4(acc[m][j][0], acc[m][j][1], acc[m][j][2], acc[m][j][3]);
+        pa[2 * colv[m][j]] =
+            make_float4(acc[m][j][0].x, acc[m][j][0].y, acc[m][j][1].x, acc[m][j][1].y);
         pa[2 * colv[m][j] + 1] =
-            make_float4(acc[m][j][4], acc[m][j][5], acc[m][j][6], acc[m][j][7]);
+            make_float4(acc[m][j][2].x, acc[m][j][2].y, acc[m][j][3].x, acc[m][j][3].y);
       }
       const int item = tid + kAttnThreads * m;
       if (item % LP == 0) {
         const int head = item / LP;
-        part_ml[(size_t(u) * num_heads + head) * 2 + 0] = mrun[m];
+        // back to natural-log units for the combine kernel
+        part_ml[(size_t(u) * num_heads + head) * 2 + 0] = mrun[m] * kLn2;
         part_ml[(size_t(u) * num_heads + head) * 2 + 1] = lrun[m];
       }
     }
@@ -1174,8 +1259,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel_bf16(
 
 // One warp per (request, head): out = sum_u e^{m_u-M} acc_u / sum_u e^{m_u-M} l_u,
 // zero when the request attended to no token (SparseAttentionCpu returns zeros).
-// Lanes split the units for M and L (warp reductions), then each lane owns
-// float4 columns of the head and sums the units' partials with their weights.
+// Units are taken 32 at a time: lane i loads unit i's (m, l) once, the warp
+// reduces M and L, lane i keeps its unit's weight e^{m_i-M}, and each lane
+// then sums its float4 columns over the units with the weights broadcast by
+// shuffles (the partial loads of a chunk are independent, so they overlap).
 __global__ void __launch_bounds__(256) combine_kernel(StepPlan plan,
                                                       const float* __restrict__ part_acc,
                                                       const float* __restrict__ part_ml,
@@ -1193,34 +1280,67 @@ __global__ void __launch_bounds__(256) combine_kernel(StepPlan plan,
        wg += (gridDim.x * blockDim.x) >> 5) {
     const int r = wg / num_heads, h = wg - (wg / num_heads) * num_heads;
     const int u0 = plan.unit_off[r], u1 = plan.unit_off[r + 1];
-    float M = -INFINITY;
-    for (int u = u0 + lane; u < u1; u += 32) M = fmaxf(M, part_ml[(size_t(u) * num_heads + h) * 2]);
+    float4* out = reinterpret_cast<float4*>(outputs + size_t(r) * ept + size_t(h) * head_dim);
+    // M over all units (one pass over the (m, l) pairs; this lane's first
+    // chunk stays in registers)
+    float m0 = -INFINITY, l0 = 0.f;
+    if (u0 + lane < u1) {
+      const float2 ml =
+          *reinterpret_cast<const float2*>(part_ml + (size_t(u0 + lane) * num_heads + h) * 2);
+      m0 = ml.x;
+      l0 = ml.y;
+    }
+    float M = m0;
+    for (int u = u0 + 32 + lane; u < u1; u += 32)
+      M = fmaxf(M, part_ml[(size_t(u) * num_heads + h) * 2]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    float4* out = reinterpret_cast<float4*>(outputs + size_t(r) * ept + size_t(h) * head_dim);
     if (M == -INFINITY) {
       for (int d = lane; d < g4; d += 32) out[d] = make_float4(0.f, 0.f, 0.f, 0.f);
       continue;
     }
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     float L = 0.f;
-    for (int u = u0 + lane; u < u1; u += 32) {
-      const float* ml = part_ml + (size_t(u) * num_heads + h) * 2;
-      L += ml[1] * expf(ml[0] - M);
+    const bool col = lane < g4;   // head_dim <= 128: one float4 column per lane
+    for (int c0 = u0; c0 < u1; c0 += 32) {
+      float w = 0.f;
+      if (c0 == u0) {
+        w = u0 + lane < u1 ? expf(m0 - M) : 0.f;
+        L += l0 * w;
+      } else if (c0 + lane < u1) {
+        const float2 ml =
+            *reinterpret_cast<const float2*>(part_ml + (size_t(c0 + lane) * num_heads + h) * 2);
+        w = expf(ml.x - M);
+        L += ml.y * w;
+      }
+      const int nu = min(32, u1 - c0);
+      const float* base = part_acc + size_t(c0) * ept + size_t(h) * head_dim + 4 * lane;
+      int i = 0;
+      for (; i + 4 <= nu; i += 4) {
+        float4 a[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          a[k] = col ? *reinterpret_cast<const float4*>(base + size_t(i + k) * ept)
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float wk = __shfl_sync(0xffffffffu, w, i + k);
+          acc.x += wk * a[k].x; acc.y += wk * a[k].y; acc.z += wk * a[k].z; acc.w += wk * a[k].w;
+        }
+      }
+      for (; i < nu; ++i) {
+        const float4 a = col ? *reinterpret_cast<const float4*>(base + size_t(i) * ept)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float wk = __shfl_sync(0xffffffffu, w, i);
+        acc.x += wk * a.x; acc.y += wk * a.y; acc.z += wk * a.z; acc.w += wk * a.w;
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
     const float inv = L > 0.f ? 1.0f / L : 0.0f;
-    for (int d = lane; d < g4; d += 32) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int u = u0; u < u1; ++u) {
-        const float w = expf(part_ml[(size_t(u) * num_heads + h) * 2] - M);
-        const float4 a = reinterpret_cast<const float4*>(part_acc + size_t(u) * ept +
-                                                         size_t(h) * head_dim)[d];
-        acc.x += w * a.x; acc.y += w * a.y; acc.z += w * a.z; acc.w += w * a.w;
-      }
-      out[d] = L > 0.f ? make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv)
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    if (col)
+      out[lane] = L > 0.f ? make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
   }
 }
 
