@@ -138,27 +138,32 @@ void SetAllAttnAttributes(size_t smem) {
   SetAttnAttr<4, 1>(smem); SetAttnAttr<4, 2>(smem);
 }
 
-constexpr size_t ScoreBf16Smem(int stages) { return stages * dsdk::kScoreBfStageBytes; }
+// Narrow-row scoring (128-byte row pieces, 4 CTAs per SM, 3-stage ring each)
+// serves bf16 summaries: their per-byte dependent add chain is twice fp32's
+// and needs more warps in flight (config 3: 2 CTAs x 5 stages 0.178 ms,
+// 3 x 3 0.149 ms, 4 x 3 0.145 ms).  For fp32 summaries score_kernel stays
+// (the narrow variant measured 0.282 vs 0.279 ms).
+constexpr int kScoreNarrowCtas = 4;
+constexpr int kScoreNarrowStages = 3;
 
-// bf16 scoring runs 4 CTAs per SM with a 3-stage ring each: the per-thread
-// dependent add chain is twice as long per byte as in fp32, so it needs more
-// warps in flight (measured at config 3: 2 CTAs x 5 stages 0.178 ms, 3 x 3
-// 0.149 ms, 4 x 3 0.145 ms).
-constexpr int kScoreBf16Ctas = 4;
-constexpr int kScoreBf16Stages = 3;
+template <typename T>
+constexpr size_t ScoreNarrowSmem() {
+  return kScoreNarrowStages * dsdk::ScoreRows<T>::kStageBytes;
+}
 
-void SetScoreBf16Attributes() {
-  Check(cudaFuncSetAttribute(dsdk::score_kernel_bf16<kScoreBf16Stages, kScoreBf16Ctas>,
+template <typename T>
+void SetScoreNarrowAttributes() {
+  Check(cudaFuncSetAttribute(dsdk::score_kernel_narrow<T, kScoreNarrowStages, kScoreNarrowCtas>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             int(ScoreBf16Smem(kScoreBf16Stages))),
+                             int(ScoreNarrowSmem<T>())),
         "smem attribute");
 }
 
-void LaunchScoreBf16(int num_sms, cudaStream_t st, const dsdk::StepPlan& plan, const float* q,
-                     const __nv_bfloat16* summ, int ept, float scale, float* scores, int part,
-                     int nparts) {
-  dsdk::score_kernel_bf16<kScoreBf16Stages, kScoreBf16Ctas>
-      <<<kScoreBf16Ctas * num_sms, dsdk::kScoreThreads, ScoreBf16Smem(kScoreBf16Stages), st>>>(
+template <typename T>
+void LaunchScoreNarrow(int num_sms, cudaStream_t st, const dsdk::StepPlan& plan, const float* q,
+                       const T* summ, int ept, float scale, float* scores, int part, int nparts) {
+  dsdk::score_kernel_narrow<T, kScoreNarrowStages, kScoreNarrowCtas>
+      <<<kScoreNarrowCtas * num_sms, dsdk::kScoreThreads, ScoreNarrowSmem<T>(), st>>>(
           plan, q, summ, ept, scale, scores, part, nparts);
 }
 
@@ -474,7 +479,8 @@ void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool cap
   const int comb_grid = std::max(1, std::min((pairs + 7) / 8, 8 * c->num_sms));
   const int nparts = timed ? 1 : kStepParts;
   if (timed) RecordEvent(c, 0, capturing);
-  const int score_ctas = (c->kv_format == DSD_KV_BF16 ? kScoreBf16Ctas : 2) * c->num_sms;
+  const int score_ctas =
+      (c->kv_format == DSD_KV_BF16 ? kScoreNarrowCtas : 2) * c->num_sms;
   dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, c->stream>>>(plan, c->cfg.top_k_pages,
                                                              target_units, score_ctas);
   if (nparts > 1) {
@@ -484,7 +490,7 @@ void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool cap
   for (int part = 0; part < nparts; ++part) {
     cudaStream_t st = part == 0 ? c->stream : c->stream2;
     if (c->kv_format == DSD_KV_BF16)
-      LaunchScoreBf16(c->num_sms, st, plan, d_q,
+      LaunchScoreNarrow(c->num_sms, st, plan, d_q,
                       static_cast<const __nv_bfloat16*>(c->summaries), c->ept, c->scale,
                       c->d_scores, part, nparts);
     else
@@ -893,7 +899,7 @@ int dsd_ctx_create_ex(int device, const dsd_model_config* config, const dsd_ctx_
       Check(cudaFuncSetAttribute(dsdk::score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)dsdk::kScoreSmem), "smem attribute");
       if (kv_format == DSD_KV_BF16) {
-        SetScoreBf16Attributes();
+        SetScoreNarrowAttributes<__nv_bfloat16>();
         SetAllAttnAttributesBf16(c->attn.smem);
       } else {
         SetAllAttnAttributes(c->attn.smem);

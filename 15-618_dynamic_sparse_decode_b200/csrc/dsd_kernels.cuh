@@ -503,22 +503,43 @@ __global__ void __launch_bounds__(kScoreThreads, 2) score_kernel(
   cp_async_wait<0>();
 }
 
-// bf16 summaries: the score_kernel scheme with 16-byte pieces of 8 bf16 per
-// row column (kCols = 8 per 64-element row chunk), 144-byte padded rows (the
-// 8 threads of a quarter warp read 8 different 16 B bank groups), the fp32
-// query chunk in its own region and more stages in flight (a stage holds half
-// the bytes).  Each bf16 element widens to fp32 exactly; the dot product is
-// the same sequential round-to-nearest chain as score_kernel.
-constexpr int kScoreBfRowStride = kScoreChunk + 8;  // bf16 elements per smem row
-constexpr size_t kScoreBfStageBytes =
-    size_t(kScoreTile) * kScoreBfRowStride * 2 + size_t(kScoreChunk) * 4;
+// Narrow-row scoring: the score_kernel scheme with 128-byte row pieces per
+// stage (32 fp32 or 64 bf16 elements, 8 columns of 16 bytes), 144-byte padded
+// shared-memory rows (the 8 threads of a quarter warp read 8 different 16 B
+// bank groups), the fp32 query piece in its own region, and small stages so
+// 4 CTAs fit on an SM: twice the warps of score_kernel to hide the
+// per-thread dependent add chain.  The dot product is the same sequential
+// round-to-nearest chain; bf16 elements widen to fp32 exactly.
+template <typename T>
+struct ScoreRows {
+  static constexpr int kEP = 16 / int(sizeof(T));          // elements per 16 B
+  static constexpr int kChunk = 128 / int(sizeof(T));      // elements per row piece
+  static constexpr int kStride = kChunk + kEP;             // smem row stride (elements)
+  static constexpr size_t kStageBytes =
+      size_t(kScoreTile) * kStride * sizeof(T) + size_t(kChunk) * 4;
+};
 
-template <int STAGES, int MINB>
-__global__ void __launch_bounds__(kScoreThreads, MINB) score_kernel_bf16(
-    StepPlan plan, const float* __restrict__ queries, const __nv_bfloat16* __restrict__ summaries,
-    int ept, float scale, float* __restrict__ scores, int part, int nparts) {
+// 16 bytes of summary -> fp32 elements
+__device__ __forceinline__ void widen16(const uint4 raw, const float*, float (&f)[4]) {
+  f[0] = __uint_as_float(raw.x); f[1] = __uint_as_float(raw.y);
+  f[2] = __uint_as_float(raw.z); f[3] = __uint_as_float(raw.w);
+}
+__device__ __forceinline__ void widen16(const uint4 raw, const __nv_bfloat16*, float (&f)[8]) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    f[2 * h] = __uint_as_float(w[h] << 16);              // bf16 -> fp32: exact
+    f[2 * h + 1] = __uint_as_float(w[h] & 0xffff0000u);
+  }
+}
+
+template <typename T, int STAGES, int MINB>
+__global__ void __launch_bounds__(kScoreThreads, MINB) score_kernel_narrow(
+    StepPlan plan, const float* __restrict__ queries, const T* __restrict__ summaries, int ept,
+    float scale, float* __restrict__ scores, int part, int nparts) {
+  using R = ScoreRows<T>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  constexpr int kCols = kScoreChunk / 8;                  // 16 B columns per row chunk
+  constexpr int kCols = R::kChunk / R::kEP;               // 8 columns of 16 B
   constexpr int kRowStep = kScoreThreads / kCols;
   constexpr int kRowsPerThread = kScoreTile / kRowStep;
 
@@ -531,8 +552,9 @@ __global__ void __launch_bounds__(kScoreThreads, MINB) score_kernel_bf16(
   const int tile_begin = plan.tile_off[r_begin];
   const int total_tiles = plan.tile_off[r_end];
   const int ts = plan.misc[1];
-  const int cw = summary_chunk(ept);          // elements of a page's summary per stage (>= 8)
-  const int nchunks = ept / cw;
+  const int cw = summary_chunk(ept);          // layout chunk (elements)
+  const int kc = min(R::kChunk, cw);          // elements of a row per stage (>= kEP)
+  const int nchunks = ept / kc;
   const size_t chunk_stride = size_t(128) * cw;
   const int col = tid % kCols;
   const int row0 = tid / kCols;
@@ -555,19 +577,20 @@ __global__ void __launch_bounds__(kScoreThreads, MINB) score_kernel_bf16(
   };
   auto issue = [&]() {
     if (ld_tile < total_tiles) {
-      unsigned char* st = smem_raw + size_t(ld_slot) * kScoreBfStageBytes;
-      __nv_bfloat16* rows = reinterpret_cast<__nv_bfloat16*>(st);
-      float* qst = reinterpret_cast<float*>(st + size_t(kScoreTile) * kScoreBfRowStride * 2);
-      if (col * 8 < cw) {
-        const size_t coff = size_t(ld_ch) * chunk_stride + col * 8;
+      unsigned char* st = smem_raw + size_t(ld_slot) * R::kStageBytes;
+      T* rows = reinterpret_cast<T*>(st);
+      float* qst = reinterpret_cast<float*>(st + size_t(kScoreTile) * R::kStride * sizeof(T));
+      const int e0 = ld_ch * kc;
+      if (col * R::kEP < kc) {
+        const size_t coff = size_t(e0 / cw) * chunk_stride + (e0 % cw) + col * R::kEP;
 #pragma unroll
         for (int j = 0; j < kRowsPerThread; ++j) {
           const int row = row0 + kRowStep * j;
           if (row < ld_nvalid)
-            cp_async16(rows + row * kScoreBfRowStride + col * 8, summaries + ld_off[j] + coff);
+            cp_async16(rows + row * R::kStride + col * R::kEP, summaries + ld_off[j] + coff);
         }
       }
-      if (tid * 4 < cw) cp_async16(qst + tid * 4, ld_q + size_t(ld_ch) * cw + tid * 4);
+      if (tid * 4 < kc) cp_async16(qst + tid * 4, ld_q + size_t(e0) + tid * 4);
       if (++ld_ch == nchunks) {
         ld_ch = 0;
         ld_tile += gridDim.x;
@@ -590,31 +613,31 @@ __global__ void __launch_bounds__(kScoreThreads, MINB) score_kernel_bf16(
     float acc = 0.0f;
     for (int ch = 0; ch < nchunks; ++ch) {
       cp_async_wait<STAGES - 2>();
-      __syncthreads();
+      __syncthreads();   // chunk `slot` landed for all threads; slot-1 is free again
       issue();
-      const unsigned char* st = smem_raw + size_t(slot) * kScoreBfStageBytes;
+      const unsigned char* st = smem_raw + size_t(slot) * R::kStageBytes;
       if (tid < nvalid) {
-        const uint4* srow = reinterpret_cast<const uint4*>(
-            reinterpret_cast<const __nv_bfloat16*>(st) + tid * kScoreBfRowStride);
+        const uint4* srow =
+            reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(st) + tid * R::kStride);
         const float4* qv =
-            reinterpret_cast<const float4*>(st + size_t(kScoreTile) * kScoreBfRowStride * 2);
-        auto step8 = [&](int i) {
-          const uint4 raw = srow[i];
-          const float4 a0 = qv[2 * i], a1 = qv[2 * i + 1];
-          const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-          const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            reinterpret_cast<const float4*>(st + size_t(kScoreTile) * R::kStride * sizeof(T));
+        auto piece = [&](int i) {
+          float f[R::kEP];
+          widen16(srow[i], static_cast<const T*>(nullptr), f);
 #pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            // bf16 -> fp32 is a 16-bit shift (exact)
-            acc = __fadd_rn(acc, __fmul_rn(a[2 * h], __uint_as_float(w[h] << 16)));
-            acc = __fadd_rn(acc, __fmul_rn(a[2 * h + 1], __uint_as_float(w[h] & 0xffff0000u)));
+          for (int h = 0; h < R::kEP / 4; ++h) {
+            const float4 a = qv[i * (R::kEP / 4) + h];
+            acc = __fadd_rn(acc, __fmul_rn(a.x, f[4 * h]));
+            acc = __fadd_rn(acc, __fmul_rn(a.y, f[4 * h + 1]));
+            acc = __fadd_rn(acc, __fmul_rn(a.z, f[4 * h + 2]));
+            acc = __fadd_rn(acc, __fmul_rn(a.w, f[4 * h + 3]));
           }
         };
-        if (cw == kScoreChunk) {
+        if (kc == R::kChunk) {
 #pragma unroll
-          for (int i = 0; i < kScoreChunk / 8; ++i) step8(i);
+          for (int i = 0; i < kCols; ++i) piece(i);
         } else {
-          for (int i = 0; i < cw / 8; ++i) step8(i);
+          for (int i = 0; i < kc / R::kEP; ++i) piece(i);
         }
       }
       slot = slot + 1 == STAGES ? 0 : slot + 1;
