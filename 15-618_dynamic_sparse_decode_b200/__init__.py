@@ -375,7 +375,9 @@ class SparseDecodeContext:
         req, q = _i32(request_ids), _f32(queries)
         if not hasattr(self, "_pending"):
             self._pending = []
-        n = np.array([self.request_num_pages(int(r)) for r in req])
+        # page counts size the debug results; other modes need none
+        n = (np.array([self.request_num_pages(int(r)) for r in req])
+             if output_mode == OUTPUT_DEBUG else np.zeros(1, np.int64))
         _check(self.lib.dsd_decode_step_begin(self.h, _ip(req), len(req), _fp(q), output_mode, 0))
         self._pending.append((len(req), output_mode, n))
 
