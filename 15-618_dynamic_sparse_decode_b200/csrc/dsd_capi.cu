@@ -241,6 +241,13 @@ struct dsd_ctx {
   cudaEvent_t ev_inputs = nullptr;  // the step input upload has been consumed
   int ev_set = 0;                   // stage-event set the next launch records into
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+  // split host I/O of a page-table step: the second request range's queries
+  // go up on copy_stream while the first range computes (ev_q1, waited on
+  // inside the graph), and the first range's outputs come back on
+  // copy_stream while the second range computes (ev_out0, recorded inside
+  // the graph)
+  cudaStream_t copy_stream = nullptr;
+  cudaEvent_t ev_part0_up = nullptr, ev_q1 = nullptr, ev_out0 = nullptr, ev_out0_done = nullptr;
 
   // pool: fp32 or bf16 elements (kv_format); summary_floats counts elements
   int kv_format = DSD_KV_F32;
@@ -303,6 +310,7 @@ struct dsd_ctx {
     float* out;
     bool timed;
     int ev_set;
+    bool split_io;
     cudaGraph_t graph;
     cudaGraphExec_t exec;
   };
@@ -470,7 +478,8 @@ void RecordEvent(dsd_ctx* c, int i, bool capturing) {
 // between the stages.
 constexpr int kStepParts = 2;
 
-void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool capturing = false) {
+void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool capturing = false,
+                bool split_io = false) {
   const dsdk::StepPlan& plan = c->plan;
   const int target_units = 8 * c->num_sms;
   const int H = c->cfg.num_heads, D = c->cfg.head_dim, P = c->cfg.page_size;
@@ -486,6 +495,9 @@ void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool cap
   if (nparts > 1) {
     Check(cudaEventRecord(c->ev_fork, c->stream), "fork");
     Check(cudaStreamWaitEvent(c->stream2, c->ev_fork, 0), "fork wait");
+    // the second range's queries arrive on copy_stream (recorded before launch)
+    if (split_io && capturing)
+      Check(cudaStreamWaitEvent(c->stream2, c->ev_q1, cudaEventWaitExternal), "query wait");
   }
   for (int part = 0; part < nparts; ++part) {
     cudaStream_t st = part == 0 ? c->stream : c->stream2;
@@ -512,6 +524,9 @@ void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool cap
                  c->d_part_acc, c->d_part_ml, H, D, P, c->scale, part, nparts);
     dsdk::combine_kernel<<<comb_grid, 256, 0, st>>>(plan, c->d_part_acc, c->d_part_ml, H, D,
                                                     d_out, part, nparts);
+    if (split_io && capturing && nparts > 1 && part == 0)
+      Check(cudaEventRecordWithFlags(c->ev_out0, c->stream, cudaEventRecordExternal),
+            "part output event");
   }
   if (nparts > 1) {
     Check(cudaEventRecord(c->ev_join, c->stream2), "join");
@@ -522,17 +537,20 @@ void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool cap
 }
 
 // Replays the step as a CUDA graph (captured on first use for this pointer pair).
-void LaunchStepGraph(dsd_ctx* c, const float* d_q, float* d_out, bool timed) {
+void LaunchStepGraph(dsd_ctx* c, const float* d_q, float* d_out, bool timed,
+                     bool split_io = false) {
+  split_io = split_io && !timed;
   for (auto& g : c->graphs) {
-    if (g.q == d_q && g.out == d_out && g.timed == timed && (!timed || g.ev_set == c->ev_set)) {
+    if (g.q == d_q && g.out == d_out && g.timed == timed && g.split_io == split_io &&
+        (!timed || g.ev_set == c->ev_set)) {
       Check(cudaGraphLaunch(g.exec, c->stream), "graph launch");
       return;
     }
   }
-  dsd_ctx::StepGraph g{d_q, d_out, timed, c->ev_set, nullptr, nullptr};
+  dsd_ctx::StepGraph g{d_q, d_out, timed, c->ev_set, split_io, nullptr, nullptr};
   Check(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
   try {
-    LaunchStep(c, d_q, d_out, timed, true);
+    LaunchStep(c, d_q, d_out, timed, true, split_io);
   } catch (...) {
     cudaGraph_t dead = nullptr;
     cudaStreamEndCapture(c->stream, &dead);
@@ -589,16 +607,73 @@ void UploadQueries(dsd_ctx* c, const float* queries, int batch) {
   Check(cudaEventRecord(c->ev_inputs, c->stream), "event record");
 }
 
+// Untimed page-table steps of at least two requests split their host I/O.
+bool SplitIo(int batch, int timing) { return timing == 0 && batch >= kStepParts; }
+
+// First request of the second range of a split step (part_range on the device).
+int SplitRow(int batch) { return int((long long)batch * 1 / kStepParts); }
+
+// UploadQueries for a page-table step whose host I/O is split: the header,
+// request list and the first range's queries go up on the context stream,
+// then (ordered after them, so they do not share the link) the second
+// range's queries on copy_stream, completing ev_q1, which the step graph
+// waits for before the second range's kernels.
+void UploadQueriesSplit(dsd_ctx* c, const float* queries, int batch) {
+  const size_t row = size_t(c->ept) * 4;
+  const int h0 = SplitRow(batch);
+  const bool direct = queries != QPtr(c) && IsPinnedHost(queries);
+  if (!direct && queries != QPtr(c)) std::memcpy(QPtr(c), queries, size_t(batch) * row);
+  const unsigned char* src1 =
+      direct ? reinterpret_cast<const unsigned char*>(queries) + size_t(h0) * row
+             : c->h_in + c->in_q_off + size_t(h0) * row;
+  if (direct) {
+    H2D(c, c->d_in, c->h_in, c->in_q_off);
+    H2D(c, c->d_in + c->in_q_off, queries, size_t(h0) * row);
+  } else {
+    H2D(c, c->d_in, c->h_in, c->in_q_off + size_t(h0) * row);
+  }
+  Check(cudaEventRecord(c->ev_part0_up, c->stream), "event record");
+  Check(cudaStreamWaitEvent(c->copy_stream, c->ev_part0_up, 0), "copy stream wait");
+  Check(cudaMemcpyAsync(c->d_in + c->in_q_off + size_t(h0) * row, src1,
+                        size_t(batch - h0) * row, cudaMemcpyHostToDevice, c->copy_stream),
+        "H2D copy");
+  CountH2D(c, size_t(batch - h0) * row);
+  Check(cudaEventRecord(c->ev_q1, c->copy_stream), "event record");
+  // the pinned staging is free again once both uploads are done
+  Check(cudaEventRecord(c->ev_inputs, c->copy_stream), "event record");
+}
+
+// Output copy of a split step: the first range's rows come back on
+// copy_stream as soon as the graph's first range is done (ev_out0), the
+// second range's on the context stream, which then waits for the first.
+void CopyOutputsSplit(dsd_ctx* c, float* h_out, int batch) {
+  const size_t row = size_t(c->ept) * 4;
+  const int h0 = SplitRow(batch);
+  Check(cudaStreamWaitEvent(c->copy_stream, c->ev_out0, 0), "copy stream wait");
+  Check(cudaMemcpyAsync(h_out, c->d_outputs, size_t(h0) * row, cudaMemcpyDeviceToHost,
+                        c->copy_stream), "D2H copy");
+  Check(cudaEventRecord(c->ev_out0_done, c->copy_stream), "event record");
+  D2H(c, reinterpret_cast<unsigned char*>(h_out) + size_t(h0) * row,
+      reinterpret_cast<const unsigned char*>(c->d_outputs) + size_t(h0) * row,
+      size_t(batch - h0) * row);
+  CountD2H(c, size_t(h0) * row);
+  Check(cudaStreamWaitEvent(c->stream, c->ev_out0_done, 0), "output join");
+}
+
 // Common tail of a host-facing step: launch, copy results back, unpack.
 void RunHostStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int output_mode,
                  int timing, float* outputs, float* scores, int32_t* selected,
-                 dsd_step_timing* out_timing) {
+                 dsd_step_timing* out_timing, bool split_io = false) {
   LaunchStepGraph(c, reinterpret_cast<const float*>(c->d_in + c->in_q_off), c->d_outputs,
-                  timing != 0);
+                  timing != 0, split_io);
   const size_t out_bytes = size_t(batch) * c->ept * sizeof(float);
   const bool direct_out = outputs && outputs != c->h_outputs && IsPinnedHost(outputs);
-  if (output_mode != DSD_OUTPUT_NONE && outputs)
-    D2H(c, direct_out ? outputs : c->h_outputs, c->d_outputs, out_bytes);
+  if (output_mode != DSD_OUTPUT_NONE && outputs) {
+    if (split_io)
+      CopyOutputsSplit(c, direct_out ? outputs : c->h_outputs, batch);
+    else
+      D2H(c, direct_out ? outputs : c->h_outputs, c->d_outputs, out_bytes);
+  }
   if (output_mode == DSD_OUTPUT_DEBUG) {
     if (scores && total_cand > 0)
       D2H(c, c->h_scores, c->d_scores, size_t(total_cand) * sizeof(float));
@@ -621,16 +696,20 @@ void RunHostStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int outpu
 // slot; records the slot's done event when everything (status word
 // included) has landed on the host.
 void EnqueueStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int output_mode,
-                 int timing) {
+                 int timing, bool split_io = false) {
   if (c->pend_count >= 2) Fail(DSD_EINVAL, "two decode steps are already pending");
   const int slot = (c->pend_head + c->pend_count) & 1;
   c->ev_set = slot;
   LaunchStepGraph(c, reinterpret_cast<const float*>(c->d_in + c->in_q_off), c->d_outputs,
-                  timing != 0);
+                  timing != 0, split_io);
   c->ev_set = 0;
   float* h_out = slot ? c->h_outputs1 : c->h_outputs;
-  if (output_mode != DSD_OUTPUT_NONE)
-    D2H(c, h_out, c->d_outputs, size_t(batch) * c->ept * sizeof(float));
+  if (output_mode != DSD_OUTPUT_NONE) {
+    if (split_io)
+      CopyOutputsSplit(c, h_out, batch);
+    else
+      D2H(c, h_out, c->d_outputs, size_t(batch) * c->ept * sizeof(float));
+  }
   if (output_mode == DSD_OUTPUT_DEBUG) {
     if (total_cand > 0)
       D2H(c, slot ? c->h_scores1 : c->h_scores, c->d_scores, size_t(total_cand) * sizeof(float));
@@ -828,6 +907,9 @@ int dsd_ctx_create_ex(int device, const dsd_model_config* config, const dsd_ctx_
       Check(cudaStreamCreateWithFlags(&c->stream2, cudaStreamNonBlocking), "stream");
       Check(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming), "event");
       Check(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming), "event");
+      Check(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking), "stream");
+      for (cudaEvent_t* e : {&c->ev_part0_up, &c->ev_q1, &c->ev_out0, &c->ev_out0_done})
+        Check(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "event");
 
       const size_t cap = size_t(opt.capacity_pages);
       const size_t el = c->kv_elem;
@@ -919,6 +1001,7 @@ int dsd_ctx_destroy(dsd_ctx* c) {
   if (!c) return DSD_OK;
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
+  if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
   for (auto& g : c->graphs) {
     if (g.exec) cudaGraphExecDestroy(g.exec);
     if (g.graph) cudaGraphDestroy(g.graph);
@@ -947,6 +1030,9 @@ int dsd_ctx_destroy(dsd_ctx* c) {
   if (c->ev_inputs) cudaEventDestroy(c->ev_inputs);
   if (c->ev_fork) cudaEventDestroy(c->ev_fork);
   if (c->ev_join) cudaEventDestroy(c->ev_join);
+  for (cudaEvent_t e : {c->ev_part0_up, c->ev_q1, c->ev_out0, c->ev_out0_done})
+    if (e) cudaEventDestroy(e);
+  if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
   if (c->stream2) cudaStreamDestroy(c->stream2);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
@@ -1493,8 +1579,10 @@ int dsd_decode_step(dsd_ctx* c, const int32_t* request_ids, int batch, const flo
     SetDevice(c);
     int tc = 0, ts = 0;
     PackSlots(c, request_ids, batch, &tc, &ts);
-    UploadQueries(c, queries, batch);
-    RunHostStep(c, batch, tc, ts, output_mode, timing, outputs, scores, selected, out_timing);
+    const bool split = SplitIo(batch, timing);
+    if (split) UploadQueriesSplit(c, queries, batch); else UploadQueries(c, queries, batch);
+    RunHostStep(c, batch, tc, ts, output_mode, timing, outputs, scores, selected, out_timing,
+                split);
   });
 }
 
@@ -1509,8 +1597,9 @@ int dsd_decode_step_begin(dsd_ctx* c, const int32_t* request_ids, int batch,
     SetDevice(c);
     int tc = 0, ts = 0;
     PackSlots(c, request_ids, batch, &tc, &ts);
-    UploadQueries(c, queries, batch);
-    EnqueueStep(c, batch, tc, ts, output_mode, timing);
+    const bool split = SplitIo(batch, timing);
+    if (split) UploadQueriesSplit(c, queries, batch); else UploadQueries(c, queries, batch);
+    EnqueueStep(c, batch, tc, ts, output_mode, timing, split);
   });
 }
 
