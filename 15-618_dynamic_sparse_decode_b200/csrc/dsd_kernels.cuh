@@ -30,7 +30,8 @@ namespace dsdk {
 
 // Storage element of the K/V pages and the summaries: fp32 (the parity
 // path) or bf16 (opt-in; arithmetic stays fp32, values round to nearest even
-// when stored).  get/put convert one element; load4/store4 four.
+// when stored).  get/put convert one element, store4 four, round/round4
+// give the value the storage will hold.
 template <typename T>
 struct Kv;
 template <>
@@ -38,9 +39,6 @@ struct Kv<float> {
   __device__ __forceinline__ static float get(const float* p, size_t i) { return p[i]; }
   __device__ __forceinline__ static float round(float v) { return v; }
   __device__ __forceinline__ static void put(float* p, size_t i, float v) { p[i] = v; }
-  __device__ __forceinline__ static float4 load4(const float* p) {
-    return *reinterpret_cast<const float4*>(p);
-  }
   __device__ __forceinline__ static void store4(float* p, float4 v) {
     *reinterpret_cast<float4*>(p) = v;
   }
@@ -54,12 +52,6 @@ struct Kv<__nv_bfloat16> {
     return __bfloat162float(__float2bfloat16_rn(v));
   }
   __device__ __forceinline__ static void put(T* p, size_t i, float v) { p[i] = __float2bfloat16_rn(v); }
-  __device__ __forceinline__ static float4 load4(const T* p) {
-    const uint2 raw = *reinterpret_cast<const uint2*>(p);
-    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
-    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
-    return make_float4(__low2float(a), __high2float(a), __low2float(b), __high2float(b));
-  }
   __device__ __forceinline__ static void store4(T* p, float4 v) {
     const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y);
     const __nv_bfloat162 b = __floats2bfloat162_rn(v.z, v.w);

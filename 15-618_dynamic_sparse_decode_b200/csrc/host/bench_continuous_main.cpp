@@ -13,7 +13,8 @@
 // with request_id % shard_world == shard_rank (one process per GPU),
 // 25 repeats (default 1): serve the workload this many times (a fresh
 // context each time) and print every repeat's tokens/s; the stats printed
-// are the median repeat's.
+// are the median repeat's.  26 kv_format (default 0 = fp32 pages, the
+// reference's; 1 = bf16 pages and summaries with fp32 arithmetic).
 #include <algorithm>
 #include <cstdlib>
 #include <vector>
@@ -109,6 +110,7 @@ int main(int argc, char** argv) try {
   const int shard_world = Arg(argc, argv, 23, 1);
   const int shard_rank = Arg(argc, argv, 24, 0);
   const int repeats = std::max(1, Arg(argc, argv, 25, 1));
+  o.kv_format = Arg(argc, argv, 26, 0);
   if (shard_world < 1 || shard_rank < 0 || shard_rank >= shard_world)
     throw std::invalid_argument("shard_rank must be in [0, shard_world)");
   const char* adm[] = {"cpu_cache", "direct_gpu_upload", "synthetic_gpu_prefill"};
@@ -132,6 +134,7 @@ int main(int argc, char** argv) try {
             << "\nbenchmark_mode=" << (bench_mode == 1 ? "dense_gpu" : "sparse")
             << "\ndevice_page_tables=" << o.device_page_tables << "\nshard_world=" << shard_world
             << "\nshard_rank=" << shard_rank << "\n";
+  std::cout << "kv_format=" << (o.kv_format ? "bf16" : "fp32") << "\n";
 
   const char* avail = bench_mode == 1 ? "continuous_dense_gpu_available" : "continuous_sparse_available";
   if (!dsd::SparseAttentionCudaAvailable()) {

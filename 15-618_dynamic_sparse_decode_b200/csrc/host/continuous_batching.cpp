@@ -264,7 +264,7 @@ ContinuousBatchStats RunContinuous(const ModelConfig& config,
   PagedKvCache cache(config, capacity, !metadata_only);
   SparseCudaContext ctx(cache, config, options.max_active_requests, max_cand, max_sel,
                         tables ? std::max(1, table_slots) : 0, tables ? max_pages : 0,
-                        options.device);
+                        options.device, options.kv_format);
   if (dense) detail::ThrowIf(dsd_set_attention_mode(ctx.handle(), 1));
   ctx.ResetDeviceTransferStats();
   const int ept = Ept(config);

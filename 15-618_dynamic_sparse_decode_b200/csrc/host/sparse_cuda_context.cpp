@@ -23,7 +23,7 @@ bool SparseAttentionCudaAvailable() { return dsd_available() != 0; }
 SparseCudaContext::SparseCudaContext(const PagedKvCache& cache, const ModelConfig& config,
                                      int max_batch_size, int max_total_candidates,
                                      int max_total_selected_pages, int max_requests,
-                                     int max_pages_per_request, int device)
+                                     int max_pages_per_request, int device, int kv_format)
     : cache_(&cache),
       config_(config),
       elements_per_token_(config.num_heads * config.head_dim),
@@ -38,7 +38,7 @@ SparseCudaContext::SparseCudaContext(const PagedKvCache& cache, const ModelConfi
   dsd_model_config mc{config.num_heads, config.head_dim, config.page_size, config.top_k_pages};
   dsd_ctx_options opt{cache.CapacityPages(), max_batch_size, max_total_candidates,
                       max_total_selected_pages, max_requests, max_pages_per_request};
-  ThrowIf(dsd_ctx_create(device, &mc, &opt, &ctx_));
+  ThrowIf(dsd_ctx_create_ex(device, &mc, &opt, kv_format, &ctx_));
   pool_.reset(new DevicePagePool(config, ctx_, cache.CapacityPages()));
   try {
     pool_->UploadActivePagesFromCache(cache);

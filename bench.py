@@ -376,7 +376,8 @@ def run_continuous(args):
         dist.barrier()
     spec = CONTINUOUS[args.workload]
     exe = os.path.join(ROOT, "15-618_dynamic_sparse_decode_b200", "bin", "dsd_continuous_bench")
-    argv = [str(x) for x in spec["argv"]] + [str(world), str(rank), str(spec.get("repeats", 1))]
+    argv = [str(x) for x in spec["argv"]] + [str(world), str(rank), str(spec.get("repeats", 1)),
+                                             "1" if args.kv == "bf16" else "0"]
     env = dict(os.environ, CUDA_VISIBLE_DEVICES=str(local))
     out = subprocess.run([exe, *argv], capture_output=True, text=True, env=env)
     if out.returncode != 0:
@@ -405,10 +406,12 @@ def run_continuous(args):
             "n_gpus": world, "steps": int(max(r["steps"] for r in ranks)), "warmup": 0,
             "ms_per_step": float(np.mean([r["avg_step_ms"] for r in ranks])),
             "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": (value / spec["published"] if spec.get("published") and world == 1
+            "vs_baseline": (value / spec["published"]
+                            if spec.get("published") and world == 1 and args.kv == "f32"
                             else None),
-            "dtype": "f32", "data": "synthetic (reference mt19937 workload generator)",
-            "config": {"workload": spec["desc"], "argv": argv,
+            "dtype": "bf16 pages, f32 arithmetic" if args.kv == "bf16" else "f32",
+            "data": "synthetic (reference mt19937 workload generator)",
+            "config": {"workload": spec["desc"], "kv_format": args.kv, "argv": argv,
                        "per_rank": [{k: round(v, 3) for k, v in r.items()} for r in ranks],
                        "timing": "host wall time of the serving loop per rank (admission, "
                                  "steps, appends, releases); max over ranks"},

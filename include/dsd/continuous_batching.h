@@ -47,6 +47,9 @@ struct ContinuousDecodeOptions {
   // CSR packing per step).  false = the reference's explicit-candidate RunBatch.
   bool device_page_tables = true;
   int device = 0;
+  // This build: page element format of the device pool (DSD_KV_F32, the
+  // reference's, or DSD_KV_BF16: bf16 pages and summaries, fp32 arithmetic).
+  int kv_format = 0;
 };
 
 struct ContinuousBatchStats {

@@ -55,10 +55,13 @@ class SparseCudaContext {
  public:
   // Uploads every active page of `cache` (K, V and its summaries verbatim).
   // max_requests / max_pages_per_request > 0 also create device request page
-  // tables for RunStep (the continuous-batching path).
+  // tables for RunStep (the continuous-batching path).  kv_format (this
+  // build) selects the device page format: DSD_KV_F32 (default, the
+  // reference's) or DSD_KV_BF16.
   SparseCudaContext(const PagedKvCache& cache, const ModelConfig& config, int max_batch_size,
                     int max_total_candidates, int max_total_selected_pages,
-                    int max_requests = 0, int max_pages_per_request = 0, int device = 0);
+                    int max_requests = 0, int max_pages_per_request = 0, int device = 0,
+                    int kv_format = 0);
   ~SparseCudaContext();
   SparseCudaContext(const SparseCudaContext&) = delete;
   SparseCudaContext& operator=(const SparseCudaContext&) = delete;

@@ -124,3 +124,25 @@ def test_bf16_continuous_serving(dsd, split_step, depth):
 def test_bf16_continuous_config4_shape(dsd):
     assert run_continuous(dsd, 32, 128, 16, 8, 12, 6, 8, 1024, 4096, 4, 10, 7,
                           kv_format=dsd.KV_BF16) > 5
+
+
+@pytest.mark.parametrize("admission", ["0", "1", "2"], ids=["cpu_cache", "direct", "synthetic"])
+def test_bf16_continuous_cli_serves_the_same_tokens(admission):
+    """dsd_continuous_bench with kv_format=1 (argv 26) serves the workload with
+    the same token accounting as the fp32 pool, in every admission mode."""
+    import os
+    import subprocess
+    from conftest import ROOT
+    exe = os.path.join(ROOT, "15-618_dynamic_sparse_decode_b200", "bin", "dsd_continuous_bench")
+    base = ["10", "4", "8", "40", "120", "3", "9", "7", "4", "16", "8", "3", admission,
+            "0", "0", "0", "0", "1", "1", "0", "1", "1", "1", "0", "1"]
+
+    def run(fmt):
+        out = subprocess.run([exe, *base, fmt], capture_output=True, text=True, timeout=600)
+        assert out.returncode == 0, out.stderr
+        return dict(l.split("=", 1) for l in out.stdout.splitlines() if "=" in l)
+
+    f32, bf16 = run("0"), run("1")
+    assert f32["kv_format"] == "fp32" and bf16["kv_format"] == "bf16"
+    assert int(bf16["total_generated_tokens"]) == int(f32["total_generated_tokens"]) > 0
+    assert float(bf16["continuous_sparse_tokens_per_second"]) > 0

@@ -259,3 +259,28 @@ def test_dense_baseline_matches_dense_cpu(dsd, orc, cfg, tol):
         assert float(np.abs(res["outputs"] - orc.dense_decode(b)).max()) <= tol
         ctx.set_dense(False)                                    # back to the sparse path
         check_against_oracle(orc, b, ctx.decode_batch(b.queries, b.cand_offsets, b.cand_ids), 1e-4)
+
+
+@pytest.mark.parametrize("batch", [1, 2, 3, 7])
+def test_step_io_split_by_request_range(dsd, orc, batch):
+    """Untimed page-table steps upload the second request range's queries and
+    download the first range's outputs on a copy stream; every batch size,
+    pinned or pageable, two steps in flight included, equals the oracle."""
+    torch = pytest.importorskip("torch")
+    b = orc.synthetic_batch(8, 32, 16, 4, batch, 100, 400, 31 + batch)
+    with make_ctx(dsd, b, tables=True) as ctx:
+        ctx.upload_pool(b.key_pool, b.value_pool, b.token_counts)
+        for r in range(b.batch):
+            ctx.set_request_pages(r, b.cand_ids[b.cand_offsets[r]:b.cand_offsets[r + 1]])
+        reqs = np.arange(b.batch)
+        check_against_oracle(orc, b, ctx.decode_step(reqs, b.queries), 1e-4)
+        _, _, out, _ = orc.sparse_decode(b)
+        q_pin = torch.empty(b.queries.shape, dtype=torch.float32, pin_memory=True).numpy()
+        q_pin[:] = b.queries
+        o_pin = torch.zeros(b.queries.shape, dtype=torch.float32, pin_memory=True).numpy()
+        ctx.decode_step(reqs, q_pin, output_mode=dsd.OUTPUT_OUTPUTS, out=o_pin)
+        assert float(np.abs(o_pin - out).max()) <= 1e-4
+        ctx.decode_step_begin(reqs, q_pin)
+        ctx.decode_step_begin(reqs, b.queries)
+        for _ in range(2):
+            assert float(np.abs(ctx.decode_step_end()["outputs"] - out).max()) <= 1e-4
