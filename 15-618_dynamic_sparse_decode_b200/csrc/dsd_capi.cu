@@ -1202,7 +1202,7 @@ int dsd_pool_prefill_synthetic(dsd_ctx* c, const int32_t* page_ids, const int32_
           static_cast<T*>(c->v_pool), static_cast<T*>(c->summaries), c->token_counts, c->live);
     });
     Check(cudaGetLastError(), "prefill kernel");
-    Sync(c);
+    // no wait: later users of the staging buffer are ordered on the same stream
     for (int i = 0; i < n; ++i) c->host_counts[page_ids[i]] = token_counts[i];
   });
 }

@@ -1503,6 +1503,21 @@ __device__ __forceinline__ float hash_to_unit(uint32_t x) {
   x ^= x >> 16;
   return static_cast<float>(static_cast<int>(x % 2001u) - 1000) / 1000.0f;
 }
+// (x % 2001 - 1000) / 1000 as a lookup: lut[i] holds (i - 1000) / 1000.0f,
+// computed once per block with the same IEEE round-to-nearest division.
+constexpr int kUnitLut = 2001;
+__device__ __forceinline__ void fill_unit_lut(float* lut) {
+  for (int i = threadIdx.x; i < kUnitLut; i += blockDim.x)
+    lut[i] = __fdiv_rn(static_cast<float>(i - 1000), 1000.0f);
+}
+__device__ __forceinline__ float hash_to_unit_lut(uint32_t x, const float* lut) {
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return lut[x % 2001u];
+}
 __device__ __forceinline__ float prompt_value(int request, int page_idx, int token, int element,
                                               int stream) {
   uint32_t x = 0x9e3779b9u;
@@ -1533,6 +1548,9 @@ __global__ void prefill_synthetic_kernel(const int* __restrict__ page_ids,
                                          T* __restrict__ summaries,
                                          int* __restrict__ token_counts,
                                          uint8_t* __restrict__ live) {
+  __shared__ float lut[kUnitLut];
+  fill_unit_lut(lut);
+  __syncthreads();
   const int i = blockIdx.x;
   const int page = page_ids[i];
   const int n = counts[i];
@@ -1541,11 +1559,12 @@ __global__ void prefill_synthetic_kernel(const int* __restrict__ page_ids,
   xr = combine_hash(xr, i, 0xc2b2ae35u);
   for (int e = threadIdx.x; e < ept; e += blockDim.x) {
     float sum = 0.0f;
+#pragma unroll 4
     for (int t = 0; t < n; ++t) {
       uint32_t x = combine_hash(xr, t, 0x27d4eb2fu);
       x = combine_hash(x, e, 0x165667b1u);
-      const float k = Kv<T>::round(hash_to_unit(combine_hash(x, 1, 0xd3a2646cu)));
-      const float v = hash_to_unit(combine_hash(x, 2, 0xd3a2646cu));
+      const float k = Kv<T>::round(hash_to_unit_lut(combine_hash(x, 1, 0xd3a2646cu), lut));
+      const float v = hash_to_unit_lut(combine_hash(x, 2, 0xd3a2646cu), lut);
       Kv<T>::put(key_pool, (size_t(page) * page_size + t) * ept + e, k);
       Kv<T>::put(value_pool, (size_t(page) * page_size + t) * ept + e, v);
       sum = __fadd_rn(sum, k);
