@@ -5,7 +5,8 @@ host with the oracle's restatement of the workload generator and decoded by
 the oracle: ids equal in order, scores bit for bit, outputs <= 1e-4.
 Size-independent properties cover the rest: every request selects exactly
 min(k, n) distinct pages of its own, and the outputs of the page-table step,
-the CSR step and the graph-replayed step agree bit for bit.
+the CSR step and the graph-replayed step agree bit for bit.  The same checks
+run on a bf16-page context against the oracle over the rounded values.
 """
 import numpy as np
 import pytest
@@ -18,13 +19,16 @@ pytestmark = pytest.mark.gpu
 SAMPLED = [0, 37]
 
 
-@pytest.fixture(scope="module")
-def cfg3(dsd):
+@pytest.fixture(scope="module", params=["f32", "bf16"])
+def cfg3(dsd, request):
+    bf16 = request.param == "bf16"
     ctx_lens = bench.workload_contexts()
-    ctx, cap, ids, counts = bench.build_workload(dsd, ctx_lens, 0)
+    ctx, cap, ids, counts = bench.build_workload(dsd, ctx_lens, 0,
+                                                 dsd.KV_BF16 if bf16 else dsd.KV_F32)
     q = bench.queries_host(dsd)
     res = ctx.decode_step(np.arange(bench.BATCH), q, output_mode=dsd.OUTPUT_DEBUG)
-    yield dict(ctx=ctx, ctx_lens=ctx_lens, cap=cap, ids=ids, counts=counts, q=q, res=res)
+    rnd = o.bf16_round if bf16 else (lambda a: a)
+    yield dict(ctx=ctx, ctx_lens=ctx_lens, cap=cap, ids=ids, counts=counts, q=q, res=res, rnd=rnd)
     ctx.close()
 
 
@@ -59,8 +63,9 @@ def test_sampled_requests_match_oracle(cfg3, r):
     own = request_pages(ctx_lens, cap, r)
     n_pages = len(own)
     base = int(own.min())
-    keys = o.normal_fill(bench.SEED, 1, (r << 40), n_tok * E).reshape(n_tok, E)
-    vals = o.normal_fill(bench.SEED, 2, (r << 40), n_tok * E).reshape(n_tok, E)
+    rnd = cfg3["rnd"]   # the stored format's rounding (identity for fp32 pages)
+    keys = rnd(o.normal_fill(bench.SEED, 1, (r << 40), n_tok * E).reshape(n_tok, E))
+    vals = rnd(o.normal_fill(bench.SEED, 2, (r << 40), n_tok * E).reshape(n_tok, E))
     kp = np.zeros((n_pages, P, E), np.float32)
     vp = np.zeros((n_pages, P, E), np.float32)
     tc = np.zeros(n_pages, np.int32)
@@ -71,7 +76,7 @@ def test_sampled_requests_match_oracle(cfg3, r):
         kp[loc, :t1 - t0] = keys[t0:t1]
         vp[loc, :t1 - t0] = vals[t0:t1]
         tc[loc] = t1 - t0
-        summ[loc] = o.page_summary(keys[t0:t1])
+        summ[loc] = rnd(o.page_summary(keys[t0:t1]))
     # device summaries of a few pages are the oracle's, bit for bit
     for j in (0, n_pages // 2, n_pages - 1):
         _, _, s, n = cfg3["ctx"].download_page(int(own[j]))
