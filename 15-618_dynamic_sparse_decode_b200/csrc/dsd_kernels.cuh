@@ -74,8 +74,19 @@ constexpr int kScoreChunk = 64;                     // floats of a summary row p
 constexpr int kScoreRowStride = kScoreChunk + 4;    // +16 B: conflict-free float4 rows
 constexpr int kScoreStages = 3;
 constexpr int kScoreThreads = kScoreTile;
-constexpr int kScoreRows = kScoreTile + 1;          // + the query chunk
-constexpr size_t kScoreSmem = size_t(kScoreStages) * kScoreRows * kScoreRowStride * sizeof(float);
+// small tiles (ts <= kScoreSmallTile candidates, small batches): the same
+// ring with 33-row stages, kScoreSmallStages deep, so more chunks are in
+// flight per dependent chain
+constexpr int kScoreSmallTile = 32;
+constexpr int kScoreSmallStages = 3;
+constexpr int kScoreSmallMult = 4;     // layout chunks per stage row (256 floats)
+constexpr size_t ScoreRingBytes(int tile, int stages, int mult) {
+  return size_t(stages) * (tile + 1) * (kScoreChunk * mult + 4) * sizeof(float);
+}
+constexpr size_t kScoreSmem = ScoreRingBytes(kScoreTile, kScoreStages, 1) >
+                                      ScoreRingBytes(kScoreSmallTile, kScoreSmallStages, kScoreSmallMult)
+                                  ? ScoreRingBytes(kScoreTile, kScoreStages, 1)
+                                  : ScoreRingBytes(kScoreSmallTile, kScoreSmallStages, kScoreSmallMult);
 
 constexpr int kAttnThreads = 256;
 constexpr int kAttnStages = 3;
@@ -373,21 +384,30 @@ __device__ __forceinline__ void cp_async_wait() {
 // Persistent CTAs over score tiles.  Thread t owns candidate t of the tile
 // and accumulates q[i]*s[i] for i = 0..E-1 in order with round-to-nearest
 // multiply and add (no FMA), exactly ScorePagesCpu's Dot.  The tile's
-// summary rows stream through a kScoreStages-deep shared-memory ring,
+// summary rows stream through a STAGES-deep shared-memory ring,
 // kScoreChunk floats per row per stage, filled by all threads with coalesced
 // 16-byte cp.async copies (one warp moves two 256 B row chunks per
-// instruction); row kScoreTile of every stage holds the query chunk.
+// instruction); row TILE of every stage holds the query chunk.  Tiles of up
+// to 128 candidates use 3 stages of one 64-float layout chunk per row.  When
+// the plan picked tiles of at most 32 candidates (small batches: a CTA runs a
+// few 4096-long chains) a stage row holds M = 4 layout chunks, so the
+// per-stage barrier and copy issue are paid once per 256 elements of the
+// chain instead of once per 64.
 // Thread t always copies rows t/kCols + kRowStep*j, column t%kCols, so it
 // keeps the page offsets of the tile it is loading in registers.
-__global__ void __launch_bounds__(kScoreThreads, 2) score_kernel(
-    StepPlan plan, const float* __restrict__ queries, const float* __restrict__ summaries,
-    int ept, float scale, float* __restrict__ scores, int part, int nparts) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
+template <int TILE, int STAGES, int M>
+__device__ __forceinline__ void score_tiles(
+    const StepPlan& plan, const float* __restrict__ queries, const float* __restrict__ summaries,
+    int ept, float scale, float* __restrict__ scores, int part, int nparts,
+    unsigned char* smem_raw) {
   float* stage_base = reinterpret_cast<float*>(smem_raw);
-  constexpr int kCols = kScoreChunk / 4;                  // float4 columns per row chunk
+  // M layout chunks (of kScoreChunk floats, each its own 256 B run) per stage row
+  constexpr int kCols = kScoreChunk * M / 4;              // float4 columns per stage row
   constexpr int kRowStep = kScoreThreads / kCols;         // rows one pass of the CTA covers
-  constexpr int kRowsPerThread = (kScoreRows + kRowStep - 1) / kRowStep;
-  constexpr int kStageFloats = kScoreRows * kScoreRowStride;
+  constexpr int kRows = TILE + 1;                          // + the query chunk
+  constexpr int kRowsPerThread = (kRows + kRowStep - 1) / kRowStep;
+  constexpr int kStride = kScoreChunk * M + 4;             // +16 B: conflict-free float4 rows
+  constexpr int kStageFloats = kRows * kStride;
 
   const int tid = threadIdx.x;
   const int B = plan.hdr[0];
@@ -399,12 +419,12 @@ __global__ void __launch_bounds__(kScoreThreads, 2) score_kernel(
   const int total_tiles = plan.tile_off[r_end];
   const int ts = plan.misc[1];
   const int cw = summary_chunk(ept);          // floats of a page's summary per stage
-  const int nchunks = ept / cw;
+  const int nchunks = ept / (cw * M);        // M > 1 only when cw == kScoreChunk
   const size_t chunk_stride = size_t(128) * cw;
   const int col = tid % kCols;
   const int row0 = tid / kCols;
 
-  // ---- loader state (runs kScoreStages-1 chunks ahead of the compute)
+  // ---- loader state (runs STAGES-1 chunks ahead of the compute)
   int ld_tile = tile_begin + blockIdx.x, ld_ch = 0, ld_slot = 0, ld_nvalid = 0;
   const float* ld_q = queries;
   size_t ld_off[kRowsPerThread];
@@ -425,16 +445,17 @@ __global__ void __launch_bounds__(kScoreThreads, 2) score_kernel(
     if (ld_tile < total_tiles) {
       const int len = cw;
       float* st = stage_base + size_t(ld_slot) * kStageFloats;
-      if (col * 4 < len) {
-        const size_t coff = size_t(ld_ch) * chunk_stride + col * 4;
-        const size_t qoff = size_t(ld_ch) * cw + col * 4;
+      if (col * 4 < len * M) {
+        const size_t coff =
+            size_t(ld_ch * M + col / (kScoreChunk / 4)) * chunk_stride + (col % (kScoreChunk / 4)) * 4;
+        const size_t qoff = size_t(ld_ch) * cw * M + col * 4;
 #pragma unroll
         for (int j = 0; j < kRowsPerThread; ++j) {
           const int row = row0 + kRowStep * j;
           if (row < ld_nvalid) {
-            cp_async16(st + row * kScoreRowStride + col * 4, summaries + ld_off[j] + coff);
-          } else if (row == kScoreTile) {
-            cp_async16(st + row * kScoreRowStride + col * 4, ld_q + qoff);
+            cp_async16(st + row * kStride + col * 4, summaries + ld_off[j] + coff);
+          } else if (row == TILE) {
+            cp_async16(st + row * kStride + col * 4, ld_q + qoff);
           }
         }
       }
@@ -445,12 +466,12 @@ __global__ void __launch_bounds__(kScoreThreads, 2) score_kernel(
       }
     }
     cp_async_commit();
-    ld_slot = ld_slot + 1 == kScoreStages ? 0 : ld_slot + 1;
+    ld_slot = ld_slot + 1 == STAGES ? 0 : ld_slot + 1;
   };
 
   load_tile();
 #pragma unroll 1
-  for (int i = 0; i < kScoreStages - 1; ++i) issue();
+  for (int i = 0; i < STAGES - 1; ++i) issue();
 
   int slot = 0;
   for (int tile = tile_begin + blockIdx.x; tile < total_tiles; tile += gridDim.x) {
@@ -459,17 +480,17 @@ __global__ void __launch_bounds__(kScoreThreads, 2) score_kernel(
     const int nvalid = min(ts, plan.n_cand[r] - c0);
     float acc = 0.0f;
     for (int ch = 0; ch < nchunks; ++ch) {
-      cp_async_wait<kScoreStages - 2>();
+      cp_async_wait<STAGES - 2>();
       __syncthreads();   // chunk `slot` landed for all threads; slot-1 is free again
       issue();
       const int len = cw;
       const float* st = stage_base + size_t(slot) * kStageFloats;
       if (tid < nvalid) {
-        const float4* srow = reinterpret_cast<const float4*>(st + tid * kScoreRowStride);
-        const float4* qv = reinterpret_cast<const float4*>(st + kScoreTile * kScoreRowStride);
+        const float4* srow = reinterpret_cast<const float4*>(st + tid * kStride);
+        const float4* qv = reinterpret_cast<const float4*>(st + TILE * kStride);
         if (len == kScoreChunk) {
 #pragma unroll
-          for (int i = 0; i < kScoreChunk / 4; ++i) {
+          for (int i = 0; i < kScoreChunk * M / 4; ++i) {
             const float4 a = qv[i];
             const float4 b = srow[i];
             acc = __fadd_rn(acc, __fmul_rn(a.x, b.x));
@@ -488,11 +509,26 @@ __global__ void __launch_bounds__(kScoreThreads, 2) score_kernel(
           }
         }
       }
-      slot = slot + 1 == kScoreStages ? 0 : slot + 1;
+      slot = slot + 1 == STAGES ? 0 : slot + 1;
     }
     if (tid < nvalid) scores[plan.score_off[r] + c0 + tid] = __fmul_rn(acc, scale);
   }
   cp_async_wait<0>();
+}
+
+__global__ void __launch_bounds__(kScoreThreads, 2) score_kernel(
+    StepPlan plan, const float* __restrict__ queries, const float* __restrict__ summaries,
+    int ept, float scale, float* __restrict__ scores, int part, int nparts) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  if (plan.misc[1] > kScoreSmallTile)
+    score_tiles<kScoreTile, kScoreStages, 1>(plan, queries, summaries, ept, scale, scores, part,
+                                             nparts, smem_raw);
+  else if (summary_chunk(ept) == kScoreChunk && (ept / kScoreChunk) % kScoreSmallMult == 0)
+    score_tiles<kScoreSmallTile, kScoreSmallStages, kScoreSmallMult>(
+        plan, queries, summaries, ept, scale, scores, part, nparts, smem_raw);
+  else
+    score_tiles<kScoreSmallTile, kScoreSmallStages, 1>(plan, queries, summaries, ept, scale,
+                                                       scores, part, nparts, smem_raw);
 }
 
 // Narrow-row scoring: the score_kernel scheme with 128-byte row pieces per
