@@ -181,8 +181,9 @@ def run_reference(args):
 
 # ---------------------------------------------------------------- our arm
 
-def build_workload(dsd, ctx_lens, device, kv_format=0):
-    """Allocates the pool, generates K/V on device, sets the request page tables."""
+def build_workload(dsd, ctx_lens, device, kv_format=0, global_ids=None):
+    """Allocates the pool, generates K/V on device, sets the request page tables.
+    Local request r holds the data of global request global_ids[r] (default r)."""
     pages_per = (ctx_lens + P - 1) // P
     cap = int(pages_per.sum())
     ctx = dsd.SparseDecodeContext(H, D, P, K_TOP, cap, BATCH, cap, BATCH * K_TOP,
@@ -197,7 +198,7 @@ def build_workload(dsd, ctx_lens, device, kv_format=0):
         table.append(ids)
         page_ids.append(ids)
         counts.append(np.minimum(P, n_tok - np.arange(n_pages) * P).astype(np.int32))
-        reqs.append(np.full(n_pages, r, np.int32))
+        reqs.append(np.full(n_pages, r if global_ids is None else int(global_ids[r]), np.int32))
         first.append((np.arange(n_pages) * P).astype(np.int32))
     ctx.generate_normal(np.concatenate(page_ids), np.concatenate(counts), np.concatenate(reqs),
                         np.concatenate(first), SEED)
@@ -206,10 +207,11 @@ def build_workload(dsd, ctx_lens, device, kv_format=0):
     return ctx, cap, np.concatenate(page_ids), np.concatenate(counts)
 
 
-def queries_host(dsd):
+def queries_host(dsd, global_ids=None):
     q = np.empty((BATCH, E), np.float32)
     for r in range(BATCH):
-        q[r] = dsd.generate_normal_host(SEED, 0, dsd.normal_index(r, 0, E), E)
+        g = r if global_ids is None else int(global_ids[r])
+        q[r] = dsd.generate_normal_host(SEED, 0, dsd.normal_index(g, 0, E), E)
     return q
 
 
@@ -224,11 +226,20 @@ def run_ours(args):
     if not dsd.available():
         raise RuntimeError("no sm_100 GPU visible")
     torch.cuda.set_device(local)
-    ctx_lens = workload_contexts()
+    global BATCH
+    gids = None
+    if args.strong:
+        # strong scaling: the --batch requests in total, rank g serving the
+        # requests with id % world == g (each with its single-GPU data)
+        gids = np.arange(args.batch)[rank::world]
+        ctx_lens = workload_contexts(args.batch)[gids]
+        BATCH = len(gids)
+    else:
+        ctx_lens = workload_contexts()
     bf16 = args.kv == "bf16"
     ctx, cap, all_ids, all_counts = build_workload(dsd, ctx_lens, local,
-                                                   dsd.KV_BF16 if bf16 else dsd.KV_F32)
-    qh = queries_host(dsd)
+                                                   dsd.KV_BF16 if bf16 else dsd.KV_F32, gids)
+    qh = queries_host(dsd, gids)
     reqs = np.arange(BATCH, dtype=np.int32)
 
     # algorithmic bytes of one step (exact selected token count from a debug step)
@@ -307,10 +318,13 @@ def run_ours(args):
     line = {
         "metric": "sparse decode tokens/s", "value": world * BATCH / (ms_step * 1e-3),
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
         "dtype": "bf16 pages, f32 arithmetic" if bf16 else "f32",
         "data": "synthetic (device-generated N(0,1) Irwin-Hall, seed 7)",
-        "config": {"workload": "config3: batch 64/GPU, ctx U{16384..32768}, H32 D128 P16 k64",
+        "config": {"workload": ("config3: batch %d in total (strong), ctx U{16384..32768}, H32 D128 "
+                                "P16 k64" % args.batch) if args.strong else
+                               "config3: batch 64/GPU, ctx U{16384..32768}, H32 D128 P16 k64",
                    "kv_format": args.kv, "requests_per_gpu": BATCH, "candidate_pages_per_gpu": C,
                    "selected_pages_per_gpu": S, "selected_tokens_per_gpu": T_sel,
                    "step_bytes_per_gpu": step_bytes,
@@ -440,6 +454,9 @@ def main():
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="requests per GPU (default: the config-3 batch of 64; smaller only "
                          "for profiling captures)")
+    ap.add_argument("--strong", action="store_true",
+                    help="config 3 strong scaling: --batch requests in total, sharded by "
+                         "request id over the ranks (default: weak, --batch per GPU)")
     ap.add_argument("--kv", default="f32", choices=["f32", "bf16"],
                     help="page format of the config-3 step: f32 (the reference's, default) or "
                          "the opt-in bf16 pages (reported separately, never the headline)")
