@@ -21,7 +21,7 @@ LIB_PATH = os.path.join(PKG_DIR, "libdsd_b200.so")
 
 DSD_OK, DSD_EINVAL, DSD_ERANGE, DSD_ENOMEM, DSD_ECUDA, DSD_ETIMEOUT, DSD_EUNAVAILABLE = range(7)
 OUTPUT_NONE, OUTPUT_OUTPUTS, OUTPUT_DEBUG = 0, 1, 2
-KV_F32, KV_BF16 = 0, 1
+KV_F32, KV_BF16, KV_FP8 = 0, 1, 2
 
 _I32P = ctypes.POINTER(ctypes.c_int32)
 _F32P = ctypes.POINTER(ctypes.c_float)
@@ -191,9 +191,9 @@ class SparseDecodeContext:
     def __init__(self, num_heads, head_dim, page_size, top_k_pages, capacity_pages, max_batch,
                  max_candidates, max_selected, max_requests=0, max_pages_per_request=0,
                  device=0, kv_format=KV_F32):
-        """kv_format: KV_F32 (the reference's fp32 pages) or KV_BF16 (pages and
-        summaries stored as bf16, arithmetic in fp32; payloads in and
-        downloads out stay float32 arrays)."""
+        """kv_format: KV_F32 (the reference's fp32 pages), KV_BF16 or KV_FP8
+        (pages and summaries stored as bf16 / fp8 e4m3, arithmetic in fp32;
+        payloads in and downloads out stay float32 arrays)."""
         self.lib = load_library()
         self.cfg = ModelConfig(num_heads, head_dim, page_size, top_k_pages)
         self.opt = CtxOptions(capacity_pages, max_batch, max_candidates, max_selected,

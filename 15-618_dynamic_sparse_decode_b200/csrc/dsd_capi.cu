@@ -84,6 +84,17 @@ T* PinnedAlloc(size_t count, const char* what) {
 
 size_t AlignUp(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// fp8 e4m3 (1 sign, 4 exponent bits with bias 7, 3 mantissa bits; S.1111.111
+// is NaN, no infinities) to float, exactly.
+float Fp8E4m3ToFloat(unsigned char b) {
+  const int sign = b >> 7, exp = (b >> 3) & 15, man = b & 7;
+  float v;
+  if (exp == 15 && man == 7) v = std::nanf("");
+  else if (exp == 0) v = std::ldexp(static_cast<float>(man), -9);        // subnormal: m/8 * 2^-6
+  else v = std::ldexp(static_cast<float>(8 + man), exp - 10);           // (1 + m/8) * 2^(e-7)
+  return sign ? -v : v;
+}
+
 
 // Attention launch shape: NV float4 per lane, LP = D/(4*NV) lanes per head,
 // SLOTS items per thread, tokens per stage and dynamic shared memory.
@@ -92,21 +103,23 @@ struct AttnShape {
   size_t smem = 0;
 };
 
-AttnShape MakeAttnShape(int num_heads, int head_dim, int page_size, bool bf16 = false) {
+AttnShape MakeAttnShape(int num_heads, int head_dim, int page_size, int elem_bytes = 4) {
   AttnShape a;
   const int ept = num_heads * head_dim;
-  if (bf16) {
-    // 16-byte vectors of 8 bf16: NV = 2 for head_dim >= 16, 1 for head_dim 8
-    const int G = head_dim / 8;
-    a.nv = G >= 2 ? 2 : 1;
+  if (elem_bytes < 4) {
+    // 16-byte vectors of VE = 16/elem_bytes elements, at most 16 elements per
+    // lane: bf16 NV = 2 (head_dim >= 16) or 1 (head_dim 8); fp8 NV = 1
+    const int VE = 16 / elem_bytes;
+    const int G = head_dim / VE;
+    a.nv = std::max(1, std::min(G, 16 / VE));
     const int items = num_heads * (G / a.nv);
     const int slots = (items + dsdk::kAttnThreads - 1) / dsdk::kAttnThreads;
     if (slots > 4) Fail(DSD_EINVAL, "num_heads*head_dim is too large for the attention kernel");
     a.slots = slots <= 1 ? 1 : slots <= 2 ? 2 : 4;
     // 32 KiB stages, as many as fit in ~200 KiB (at most 8)
-    a.tps = std::max(1, std::min({page_size, 65536 / (2 * ept * 2),
+    a.tps = std::max(1, std::min({page_size, 65536 / (2 * ept * elem_bytes),
                                   dsdk::kAttnBfRegTokens}));
-    const size_t stage = size_t(2) * a.tps * ept * 2;
+    const size_t stage = size_t(2) * a.tps * ept * elem_bytes;
     a.nstages = int(std::max<size_t>(2, std::min<size_t>(8, (200u << 10) / stage)));
     a.smem = size_t(a.nstages) * (stage + 16);
     return a;
@@ -167,31 +180,39 @@ void LaunchScoreNarrow(int num_sms, cudaStream_t st, const dsdk::StepPlan& plan,
           plan, q, summ, ept, scale, scores, part, nparts);
 }
 
-template <int NV, int S>
-void SetAttnAttrBf16(size_t smem) {
-  Check(cudaFuncSetAttribute(dsdk::attn_kernel_bf16<NV, S>,
+template <typename T, int NV, int S>
+void SetAttnAttrNarrow(size_t smem) {
+  Check(cudaFuncSetAttribute(dsdk::attn_kernel_narrow<T, NV, S>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
         "smem attribute");
 }
 
-// bf16 pages: NV = 1 serves head_dim 8 (<= 1024 items), NV = 2 the rest (<= 512).
-void SetAllAttnAttributesBf16(size_t smem) {
-  SetAttnAttrBf16<1, 1>(smem); SetAttnAttrBf16<1, 2>(smem); SetAttnAttrBf16<1, 4>(smem);
-  SetAttnAttrBf16<2, 1>(smem); SetAttnAttrBf16<2, 2>(smem);
+// bf16 pages: NV = 1 serves head_dim 8 (<= 1024 items), NV = 2 the rest (<= 512);
+// fp8 pages: NV = 1 (head_dim 16: <= 512 items, 32..128: <= 256).
+template <typename T>
+void SetAllAttnAttributesNarrow(size_t smem) {
+  SetAttnAttrNarrow<T, 1, 1>(smem); SetAttnAttrNarrow<T, 1, 2>(smem);
+  if constexpr (sizeof(T) == 2) {
+    SetAttnAttrNarrow<T, 1, 4>(smem);
+    SetAttnAttrNarrow<T, 2, 1>(smem); SetAttnAttrNarrow<T, 2, 2>(smem);
+  }
 }
 
-void LaunchAttnBf16(const AttnShape& a, int grid, cudaStream_t st, const dsdk::StepPlan& plan,
-                    const float* q, const __nv_bfloat16* k, const __nv_bfloat16* v, const int* tc,
-                    const int* sel, float* pacc, float* pml, int H, int D, int P, float scale,
-                    int part, int nparts) {
+template <typename T>
+void LaunchAttnNarrow(const AttnShape& a, int grid, cudaStream_t st, const dsdk::StepPlan& plan,
+                      const float* q, const T* k, const T* v, const int* tc, const int* sel,
+                      float* pacc, float* pml, int H, int D, int P, float scale, int part,
+                      int nparts) {
 #define DSD_ATTN_CASE(NV, S)                                                                  \
   if (a.nv == NV && a.slots == S) {                                                           \
-    dsdk::attn_kernel_bf16<NV, S><<<grid, dsdk::kAttnBfThreads, a.smem, st>>>(                \
+    dsdk::attn_kernel_narrow<T, NV, S><<<grid, dsdk::kAttnBfThreads, a.smem, st>>>(           \
         plan, q, k, v, tc, sel, pacc, pml, H, D, P, a.tps, a.nstages, scale, part, nparts);   \
     return;                                                                                   \
   }
-  DSD_ATTN_CASE(1, 1) DSD_ATTN_CASE(1, 2) DSD_ATTN_CASE(1, 4)
-  DSD_ATTN_CASE(2, 1) DSD_ATTN_CASE(2, 2)
+  DSD_ATTN_CASE(1, 1) DSD_ATTN_CASE(1, 2)
+  if constexpr (sizeof(T) == 2) {
+    DSD_ATTN_CASE(1, 4) DSD_ATTN_CASE(2, 1) DSD_ATTN_CASE(2, 2)
+  }
 #undef DSD_ATTN_CASE
   Fail(DSD_EINVAL, "unsupported attention shape");
 }
@@ -249,7 +270,7 @@ struct dsd_ctx {
   cudaStream_t copy_stream = nullptr;
   cudaEvent_t ev_part0_up = nullptr, ev_q1 = nullptr, ev_out0 = nullptr, ev_out0_done = nullptr;
 
-  // pool: fp32 or bf16 elements (kv_format); summary_floats counts elements
+  // pool: fp32, bf16 or fp8 e4m3 elements (kv_format); summary_floats counts elements
   int kv_format = DSD_KV_F32;
   size_t kv_elem = 4;
   void* k_pool = nullptr;
@@ -332,6 +353,7 @@ struct dsd_ctx {
 template <typename F>
 void WithKv(const dsd_ctx* c, F&& f) {
   if (c->kv_format == DSD_KV_BF16) f(KvTag<__nv_bfloat16>{});
+  else if (c->kv_format == DSD_KV_FP8) f(KvTag<__nv_fp8_e4m3>{});
   else f(KvTag<float>{});
 }
 
@@ -489,7 +511,7 @@ void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool cap
   const int nparts = timed ? 1 : kStepParts;
   if (timed) RecordEvent(c, 0, capturing);
   const int score_ctas =
-      (c->kv_format == DSD_KV_BF16 ? kScoreNarrowCtas : 2) * c->num_sms;
+      (c->kv_format != DSD_KV_F32 ? kScoreNarrowCtas : 2) * c->num_sms;
   dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, c->stream>>>(plan, c->cfg.top_k_pages,
                                                              target_units, score_ctas);
   if (nparts > 1) {
@@ -501,23 +523,30 @@ void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool cap
   }
   for (int part = 0; part < nparts; ++part) {
     cudaStream_t st = part == 0 ? c->stream : c->stream2;
-    if (c->kv_format == DSD_KV_BF16)
-      LaunchScoreNarrow(c->num_sms, st, plan, d_q,
-                      static_cast<const __nv_bfloat16*>(c->summaries), c->ept, c->scale,
-                      c->d_scores, part, nparts);
-    else
+    if (c->kv_format == DSD_KV_F32) {
       dsdk::score_kernel<<<2 * c->num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, st>>>(
           plan, d_q, static_cast<const float*>(c->summaries), c->ept, c->scale, c->d_scores,
           part, nparts);
+    } else {
+      WithKv(c, [&](auto tag) {
+        using T = typename decltype(tag)::type;
+        if constexpr (!std::is_same<T, float>::value)
+          LaunchScoreNarrow(c->num_sms, st, plan, d_q, static_cast<const T*>(c->summaries),
+                            c->ept, c->scale, c->d_scores, part, nparts);
+      });
+    }
     if (timed) RecordEvent(c, 1, capturing);
     dsdk::select_kernel<<<sel_grid, dsdk::kSelectThreads, dsdk::kSelectSmem, st>>>(
         plan, c->d_scores, c->d_selected, part, nparts);
     if (timed) RecordEvent(c, 2, capturing);
-    if (c->kv_format == DSD_KV_BF16)
-      LaunchAttnBf16(c->attn, c->num_sms, st, plan, d_q,
-                     static_cast<const __nv_bfloat16*>(c->k_pool),
-                     static_cast<const __nv_bfloat16*>(c->v_pool), c->token_counts, c->d_selected,
-                     c->d_part_acc, c->d_part_ml, H, D, P, c->scale, part, nparts);
+    if (c->kv_format != DSD_KV_F32)
+      WithKv(c, [&](auto tag) {
+        using T = typename decltype(tag)::type;
+        if constexpr (!std::is_same<T, float>::value)
+          LaunchAttnNarrow(c->attn, c->num_sms, st, plan, d_q, static_cast<const T*>(c->k_pool),
+                           static_cast<const T*>(c->v_pool), c->token_counts, c->d_selected,
+                           c->d_part_acc, c->d_part_ml, H, D, P, c->scale, part, nparts);
+      });
     else
       LaunchAttn(c->attn, c->num_sms, st, plan, d_q, static_cast<const float*>(c->k_pool),
                  static_cast<const float*>(c->v_pool), c->token_counts, c->d_selected,
@@ -864,9 +893,12 @@ int dsd_ctx_create_ex(int device, const dsd_model_config* config, const dsd_ctx_
                       int kv_format, dsd_ctx** out) {
   return Guard([&]() {
     if (!config || !options || !out) Fail(DSD_EINVAL, "null argument");
-    if (kv_format != DSD_KV_F32 && kv_format != DSD_KV_BF16) Fail(DSD_EINVAL, "unknown kv_format");
+    if (kv_format != DSD_KV_F32 && kv_format != DSD_KV_BF16 && kv_format != DSD_KV_FP8)
+      Fail(DSD_EINVAL, "unknown kv_format");
     if (kv_format == DSD_KV_BF16 && config->head_dim < 8)
       Fail(DSD_EINVAL, "bf16 pages need head_dim >= 8");
+    if (kv_format == DSD_KV_FP8 && config->head_dim < 16)
+      Fail(DSD_EINVAL, "fp8 pages need head_dim >= 16");
     *out = nullptr;
     const dsd_model_config cfg = *config;
     const dsd_ctx_options opt = *options;
@@ -897,8 +929,8 @@ int dsd_ctx_create_ex(int device, const dsd_model_config* config, const dsd_ctx_
       c->ept = ept;
       c->num_sms = prop.multiProcessorCount;
       c->kv_format = kv_format;
-      c->kv_elem = kv_format == DSD_KV_BF16 ? 2 : 4;
-      c->attn = MakeAttnShape(cfg.num_heads, D, cfg.page_size, kv_format == DSD_KV_BF16);
+      c->kv_elem = kv_format == DSD_KV_BF16 ? 2 : kv_format == DSD_KV_FP8 ? 1 : 4;
+      c->attn = MakeAttnShape(cfg.num_heads, D, cfg.page_size, int(c->kv_elem));
       c->scale = 1.0f / std::sqrt(static_cast<float>(D));
       Check(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream");
       for (auto& e : c->ev) Check(cudaEventCreate(&e), "event");
@@ -982,7 +1014,10 @@ int dsd_ctx_create_ex(int device, const dsd_model_config* config, const dsd_ctx_
                                  (int)dsdk::kScoreSmem), "smem attribute");
       if (kv_format == DSD_KV_BF16) {
         SetScoreNarrowAttributes<__nv_bfloat16>();
-        SetAllAttnAttributesBf16(c->attn.smem);
+        SetAllAttnAttributesNarrow<__nv_bfloat16>(c->attn.smem);
+      } else if (kv_format == DSD_KV_FP8) {
+        SetScoreNarrowAttributes<__nv_fp8_e4m3>();
+        SetAllAttnAttributesNarrow<__nv_fp8_e4m3>(c->attn.smem);
       } else {
         SetAllAttnAttributes(c->attn.smem);
       }
@@ -1378,20 +1413,20 @@ int dsd_download_page(dsd_ctx* c, int page_id, float* keys, float* values, float
     SetDevice(c);
     const size_t pf = size_t(c->cfg.page_size) * c->ept;
     const size_t el = c->kv_elem;
-    const bool bf16 = c->kv_format == DSD_KV_BF16;
-    // bf16 pools land in 16-bit host words and widen to fp32 after the sync
-    std::vector<uint16_t> hk(bf16 && keys ? pf : 0), hv(bf16 && values ? pf : 0),
-        hs(bf16 && summary ? size_t(c->ept) : 0);
+    const bool narrow = c->kv_format != DSD_KV_F32;
+    // bf16 / fp8 pools land in host bytes and widen to fp32 after the sync
+    std::vector<unsigned char> hk(narrow && keys ? pf * el : 0), hv(narrow && values ? pf * el : 0),
+        hs(narrow && summary ? size_t(c->ept) * el : 0);
     const auto* kp = static_cast<const unsigned char*>(c->k_pool);
     const auto* vp = static_cast<const unsigned char*>(c->v_pool);
-    if (keys) D2H(c, bf16 ? static_cast<void*>(hk.data()) : keys, kp + size_t(page_id) * pf * el,
-                  pf * el);
-    if (values) D2H(c, bf16 ? static_cast<void*>(hv.data()) : values,
+    if (keys) D2H(c, narrow ? static_cast<void*>(hk.data()) : keys,
+                  kp + size_t(page_id) * pf * el, pf * el);
+    if (values) D2H(c, narrow ? static_cast<void*>(hv.data()) : values,
                     vp + size_t(page_id) * pf * el, pf * el);
     if (summary) {
       // gather the page's NC chunks of CW elements (stride 128*CW) into one row
       const int cw = dsdk::summary_chunk(c->ept);
-      Check(cudaMemcpy2DAsync(bf16 ? static_cast<void*>(hs.data()) : summary, size_t(cw) * el,
+      Check(cudaMemcpy2DAsync(narrow ? static_cast<void*>(hs.data()) : summary, size_t(cw) * el,
                               static_cast<const unsigned char*>(c->summaries) +
                                   dsdk::summary_row_base(page_id, c->ept) * el,
                               size_t(128) * cw * el, size_t(cw) * el, size_t(c->ept / cw),
@@ -1400,13 +1435,21 @@ int dsd_download_page(dsd_ctx* c, int page_id, float* keys, float* values, float
     }
     if (token_count) D2H(c, token_count, c->token_counts + page_id, 4);
     Sync(c);
-    auto widen = [](const std::vector<uint16_t>& src, float* dst) {
-      for (size_t i = 0; i < src.size(); ++i) {
-        const uint32_t b = uint32_t(src[i]) << 16;
-        std::memcpy(dst + i, &b, 4);
+    const bool fp8 = c->kv_format == DSD_KV_FP8;
+    auto widen = [&](const std::vector<unsigned char>& src, float* dst) {
+      const size_t n = src.size() / el;
+      for (size_t i = 0; i < n; ++i) {
+        if (fp8) {
+          dst[i] = Fp8E4m3ToFloat(src[i]);
+        } else {
+          uint16_t h;
+          std::memcpy(&h, src.data() + 2 * i, 2);
+          const uint32_t b = uint32_t(h) << 16;
+          std::memcpy(dst + i, &b, 4);
+        }
       }
     };
-    if (bf16) {
+    if (narrow) {
       if (keys) widen(hk, keys);
       if (values) widen(hv, values);
       if (summary) widen(hs, summary);

@@ -23,6 +23,8 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -59,6 +61,32 @@ struct Kv<__nv_bfloat16> {
     raw.x = *reinterpret_cast<const uint32_t*>(&a);
     raw.y = *reinterpret_cast<const uint32_t*>(&b);
     *reinterpret_cast<uint2*>(p) = raw;
+  }
+  __device__ __forceinline__ static float4 round4(float4 v) {
+    return make_float4(round(v.x), round(v.y), round(v.z), round(v.w));
+  }
+};
+template <>
+struct Kv<__nv_fp8_e4m3> {
+  using T = __nv_fp8_e4m3;
+  __device__ __forceinline__ static uint8_t enc(float v) {
+    return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+  }
+  __device__ __forceinline__ static float dec(uint8_t b) {
+    const __half_raw hr = __nv_cvt_fp8_to_halfraw(b, __NV_E4M3);
+    return __half2float(*reinterpret_cast<const __half*>(&hr));
+  }
+  __device__ __forceinline__ static float get(const T* p, size_t i) {
+    return dec(reinterpret_cast<const uint8_t*>(p)[i]);
+  }
+  __device__ __forceinline__ static float round(float v) { return dec(enc(v)); }
+  __device__ __forceinline__ static void put(T* p, size_t i, float v) {
+    reinterpret_cast<uint8_t*>(p)[i] = enc(v);
+  }
+  __device__ __forceinline__ static void store4(T* p, float4 v) {
+    const uint32_t w = uint32_t(enc(v.x)) | (uint32_t(enc(v.y)) << 8) |
+                       (uint32_t(enc(v.z)) << 16) | (uint32_t(enc(v.w)) << 24);
+    *reinterpret_cast<uint32_t*>(p) = w;
   }
   __device__ __forceinline__ static float4 round4(float4 v) {
     return make_float4(round(v.x), round(v.y), round(v.z), round(v.w));
@@ -561,6 +589,21 @@ __device__ __forceinline__ void widen16(const uint4 raw, const __nv_bfloat16*, f
   }
 }
 
+// two fp8 e4m3 (low byte first) -> float2, exact (through half)
+__device__ __forceinline__ float2 fp8x2_to_float2(uint32_t pair) {
+  const __half2_raw hr =
+      __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(pair & 0xffffu), __NV_E4M3);
+  return __half22float2(*reinterpret_cast<const __half2*>(&hr));
+}
+__device__ __forceinline__ void widen16(const uint4 raw, const __nv_fp8_e4m3*, float (&f)[16]) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    const float2 lo = fp8x2_to_float2(w[h]), hi = fp8x2_to_float2(w[h] >> 16);
+    f[4 * h] = lo.x; f[4 * h + 1] = lo.y; f[4 * h + 2] = hi.x; f[4 * h + 3] = hi.y;
+  }
+}
+
 template <typename T, int STAGES, int MINB>
 __global__ void __launch_bounds__(kScoreThreads, MINB) score_kernel_narrow(
     StepPlan plan, const float* __restrict__ queries, const T* __restrict__ summaries, int ept,
@@ -581,7 +624,10 @@ __global__ void __launch_bounds__(kScoreThreads, MINB) score_kernel_narrow(
   const int total_tiles = plan.tile_off[r_end];
   const int ts = plan.misc[1];
   const int cw = summary_chunk(ept);          // layout chunk (elements)
-  const int kc = min(R::kChunk, cw);          // elements of a row per stage (>= kEP)
+  // elements of a row per stage (>= kEP): a full 128-byte piece when it tiles
+  // the row (it may span several layout chunks, each its own run)
+  const int kc = ept % R::kChunk == 0 ? R::kChunk : min(R::kChunk, cw);
+  const int cw_log2 = __ffs(cw) - 1;          // cw is a power of two
   const int nchunks = ept / kc;
   const size_t chunk_stride = size_t(128) * cw;
   const int col = tid % kCols;
@@ -610,7 +656,8 @@ __global__ void __launch_bounds__(kScoreThreads, MINB) score_kernel_narrow(
       float* qst = reinterpret_cast<float*>(st + size_t(kScoreTile) * R::kStride * sizeof(T));
       const int e0 = ld_ch * kc;
       if (col * R::kEP < kc) {
-        const size_t coff = size_t(e0 / cw) * chunk_stride + (e0 % cw) + col * R::kEP;
+        const int e = e0 + col * R::kEP;
+        const size_t coff = size_t(e >> cw_log2) * chunk_stride + (e & (cw - 1));
 #pragma unroll
         for (int j = 0; j < kRowsPerThread; ++j) {
           const int row = row0 + kRowStep * j;
@@ -1067,12 +1114,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(
 constexpr int kAttnBfThreads = kAttnThreads + 32;
 constexpr int kAttnBfRegTokens = 4;                 // tokens per bf16 stage (V held in registers)
 
-// 8 bf16 -> 4 float2 (elements 2h, 2h+1); widening is exact (16-bit shift / mask)
-__device__ __forceinline__ void unpack_bf16x8(const uint4 raw, float2 (&f)[4]) {
+// 16 bytes of page elements -> float2 pairs (elements 2h, 2h+1); widening is
+// exact.  bf16: a 16-bit shift / mask; fp8 e4m3: via half (exact).
+__device__ __forceinline__ void unpack16(const uint4 raw, const __nv_bfloat16*, float2 (&f)[4]) {
   const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
   for (int h = 0; h < 4; ++h)
     f[h] = make_float2(__uint_as_float(w[h] << 16), __uint_as_float(w[h] & 0xffff0000u));
+}
+__device__ __forceinline__ void unpack16(const uint4 raw, const __nv_fp8_e4m3*, float2 (&f)[8]) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    f[2 * h] = fp8x2_to_float2(w[h]);
+    f[2 * h + 1] = fp8x2_to_float2(w[h] >> 16);
+  }
 }
 
 // The bf16 attention keeps its softmax in base 2: logits are scaled by
@@ -1087,22 +1143,24 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-template <int NV, int SLOTS>
-__global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_bf16(
-    StepPlan plan, const float* __restrict__ queries, const __nv_bfloat16* __restrict__ key_pool,
-    const __nv_bfloat16* __restrict__ value_pool, const int* __restrict__ token_counts,
+template <typename T, int NV, int SLOTS>
+__global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_narrow(
+    StepPlan plan, const float* __restrict__ queries, const T* __restrict__ key_pool,
+    const T* __restrict__ value_pool, const int* __restrict__ token_counts,
     const int* __restrict__ selected, float* __restrict__ part_acc, float* __restrict__ part_ml,
     int num_heads, int head_dim, int page_size, int tps, int nstages, float scale, int part,
     int nparts) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   constexpr int kConsumerWarps = kAttnThreads / 32;
   const int ept = num_heads * head_dim;
-  const int vec = ept >> 3;                       // 16-byte vectors per token row
-  const int G = head_dim >> 3;                    // vectors per head
+  constexpr int VE = 16 / int(sizeof(T));         // elements per 16-byte vector
+  constexpr int VP = VE / 2;                      // float2 pairs per vector
+  const int vec = ept / VE;                       // 16-byte vectors per token row
+  const int G = head_dim / VE;                    // vectors per head
   const int LP = G / NV;                          // lanes per head
   const size_t stage_elems = size_t(2) * tps * ept;
-  __nv_bfloat16* stages = reinterpret_cast<__nv_bfloat16*>(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + nstages * stage_elems * 2);
+  T* stages = reinterpret_cast<T*>(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + nstages * stage_elems * sizeof(T));
   uint64_t* empty = full + nstages;
 
   const int tid = threadIdx.x;
@@ -1138,8 +1196,8 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_bf16(
         const uint32_t use = g / nstages;
         if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, status)) break;
         const int nt = min(tps, w.n - w.t0);
-        const uint32_t bytes = uint32_t(nt) * uint32_t(ept) * 2u;
-        __nv_bfloat16* st = stages + size_t(s) * stage_elems;
+        const uint32_t bytes = uint32_t(nt) * uint32_t(ept) * uint32_t(sizeof(T));
+        T* st = stages + size_t(s) * stage_elems;
         const size_t src = size_t(w.page) * page_elems + size_t(w.t0) * ept;
         mbar_arrive_expect_tx(&full[s], 2u * bytes);
         bulk_g2s(st, key_pool + src, bytes, &full[s]);
@@ -1165,7 +1223,7 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_bf16(
   // warp holds page j's count) and this thread's query pieces are loaded one
   // unit ahead, so no global-load latency sits between two units.
   // Query element pairs (2x, 2x+1) are float2 for the packed f32x2 math.
-  float2 nq[SLOTS][NV][4];
+  float2 nq[SLOTS][NV][VP];
   auto unit_info = [&](int uu, int& rr, int& pb, int& pe) {
     attn_unit_range(plan, B, ppu, uu, &rr, &pb, &pe);
     const float4* qrow = reinterpret_cast<const float4*>(queries + size_t(rr) * ept);
@@ -1173,11 +1231,13 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_bf16(
     for (int m = 0; m < SLOTS; ++m) {
 #pragma unroll
       for (int j = 0; j < NV; ++j) {
-        const float4 a = ok[m] ? __ldg(qrow + 2 * colv[m][j]) : make_float4(0.f, 0.f, 0.f, 0.f);
-        const float4 b =
-            ok[m] ? __ldg(qrow + 2 * colv[m][j] + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
-        nq[m][j][0] = make_float2(a.x, a.y); nq[m][j][1] = make_float2(a.z, a.w);
-        nq[m][j][2] = make_float2(b.x, b.y); nq[m][j][3] = make_float2(b.z, b.w);
+#pragma unroll
+        for (int h = 0; h < VE / 4; ++h) {
+          const float4 a =
+              ok[m] ? __ldg(qrow + (VE / 4) * colv[m][j] + h) : make_float4(0.f, 0.f, 0.f, 0.f);
+          nq[m][j][2 * h] = make_float2(a.x, a.y);
+          nq[m][j][2 * h + 1] = make_float2(a.z, a.w);
+        }
       }
     }
     return pb + lane < pe ? min(__ldg(token_counts + __ldg(selected + pb + lane)), page_size) : 0;
@@ -1190,14 +1250,14 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_bf16(
   bool alive = true;
   for (int u = unit_begin + blockIdx.x; u < total_units && alive; u += gridDim.x) {
     const int p_begin = nx_pb, p_end = nx_pe, cnt = nx_cnt;
-    float2 q[SLOTS][NV][4], acc[SLOTS][NV][4];
+    float2 q[SLOTS][NV][VP], acc[SLOTS][NV][VP];
     float mrun[SLOTS], lrun[SLOTS];
 #pragma unroll
     for (int m = 0; m < SLOTS; ++m) {
 #pragma unroll
       for (int j = 0; j < NV; ++j) {
 #pragma unroll
-        for (int x = 0; x < 4; ++x) {
+        for (int x = 0; x < VP; ++x) {
           q[m][j][x] = nq[m][j][x];
           acc[m][j][x] = make_float2(0.f, 0.f);
         }
@@ -1231,10 +1291,10 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_bf16(
 #pragma unroll
               for (int j = 0; j < NV; ++j) {
                 vreg[m][t][j] = vst[size_t(t) * vec + colv[m][j]];
-                float2 kk[4];
-                unpack_bf16x8(kst[size_t(t) * vec + colv[m][j]], kk);
+                float2 kk[VP];
+                unpack16(kst[size_t(t) * vec + colv[m][j]], static_cast<const T*>(nullptr), kk);
 #pragma unroll
-                for (int x = 0; x < 4; ++x) d2 = __ffma2_rn(q[m][j][x], kk[x], d2);
+                for (int x = 0; x < VP; ++x) d2 = __ffma2_rn(q[m][j][x], kk[x], d2);
               }
               logit[m][t] = d2.x + d2.y;
             }
@@ -1265,7 +1325,7 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_bf16(
 #pragma unroll
           for (int j = 0; j < NV; ++j)
 #pragma unroll
-            for (int x = 0; x < 4; ++x) acc[m][j][x] = __fmul2_rn(acc[m][j][x], alpha2);
+            for (int x = 0; x < VP; ++x) acc[m][j][x] = __fmul2_rn(acc[m][j][x], alpha2);
 #pragma unroll
           for (int t = 0; t < kAttnBfRegTokens; ++t) {
             if (t < nt) {
@@ -1274,10 +1334,10 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_bf16(
               const float2 beta2 = make_float2(beta, beta);
 #pragma unroll
               for (int j = 0; j < NV; ++j) {
-                float2 vv[4];
-                unpack_bf16x8(vreg[m][t][j], vv);
+                float2 vv[VP];
+                unpack16(vreg[m][t][j], static_cast<const T*>(nullptr), vv);
 #pragma unroll
-                for (int x = 0; x < 4; ++x) acc[m][j][x] = __ffma2_rn(beta2, vv[x], acc[m][j][x]);
+                for (int x = 0; x < VP; ++x) acc[m][j][x] = __ffma2_rn(beta2, vv[x], acc[m][j][x]);
               }
             }
           }
@@ -1292,10 +1352,11 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_bf16(
       float4* pa = reinterpret_cast<float4*>(part_acc + size_t(u) * ept);
 #pragma unroll
       for (int j = 0; j < NV; ++j) {
-        pa[2 * colv[m][j]] =
-            make_float4(acc[m][j][0].x, acc[m][j][0].y, acc[m][j][1].x, acc[m][j][1].y);
-        pa[2 * colv[m][j] + 1] =
-            make_float4(acc[m][j][2].x, acc[m][j][2].y, acc[m][j][3].x, acc[m][j][3].y);
+#pragma unroll
+        for (int h = 0; h < VE / 4; ++h)
+          pa[(VE / 4) * colv[m][j] + h] = make_float4(acc[m][j][2 * h].x, acc[m][j][2 * h].y,
+                                                      acc[m][j][2 * h + 1].x,
+                                                      acc[m][j][2 * h + 1].y);
       }
       const int item = tid + kAttnThreads * m;
       if (item % LP == 0) {

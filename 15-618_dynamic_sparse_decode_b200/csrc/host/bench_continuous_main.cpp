@@ -14,7 +14,7 @@
 // 25 repeats (default 1): serve the workload this many times (a fresh
 // context each time) and print every repeat's tokens/s; the stats printed
 // are the median repeat's.  26 kv_format (default 0 = fp32 pages, the
-// reference's; 1 = bf16 pages and summaries with fp32 arithmetic).
+// reference's; 1 = bf16, 2 = fp8 e4m3 pages and summaries, fp32 arithmetic).
 #include <algorithm>
 #include <cstdlib>
 #include <vector>
@@ -134,7 +134,8 @@ int main(int argc, char** argv) try {
             << "\nbenchmark_mode=" << (bench_mode == 1 ? "dense_gpu" : "sparse")
             << "\ndevice_page_tables=" << o.device_page_tables << "\nshard_world=" << shard_world
             << "\nshard_rank=" << shard_rank << "\n";
-  std::cout << "kv_format=" << (o.kv_format ? "bf16" : "fp32") << "\n";
+  std::cout << "kv_format="
+            << (o.kv_format == 2 ? "fp8" : o.kv_format == 1 ? "bf16" : "fp32") << "\n";
 
   const char* avail = bench_mode == 1 ? "continuous_dense_gpu_available" : "continuous_sparse_available";
   if (!dsd::SparseAttentionCudaAvailable()) {

@@ -236,9 +236,9 @@ def run_ours(args):
         BATCH = len(gids)
     else:
         ctx_lens = workload_contexts()
-    bf16 = args.kv == "bf16"
-    ctx, cap, all_ids, all_counts = build_workload(dsd, ctx_lens, local,
-                                                   dsd.KV_BF16 if bf16 else dsd.KV_F32, gids)
+    fmt = {"f32": dsd.KV_F32, "bf16": dsd.KV_BF16, "fp8": dsd.KV_FP8}[args.kv]
+    bf16 = fmt != dsd.KV_F32          # a narrow (opt-in) page format
+    ctx, cap, all_ids, all_counts = build_workload(dsd, ctx_lens, local, fmt, gids)
     qh = queries_host(dsd, gids)
     reqs = np.arange(BATCH, dtype=np.int32)
 
@@ -249,7 +249,7 @@ def run_ours(args):
     C = cap
     S = int(dbg["selected"].size)
     T_sel = int(page_tokens[dbg["selected"]].sum())
-    el = 2 if bf16 else 4                                       # bytes per stored element
+    el = {dsd.KV_F32: 4, dsd.KV_BF16: 2, dsd.KV_FP8: 1}[fmt]    # bytes per stored element
     score_bytes = el * E * C + 4 * E * BATCH + 4 * C           # summaries + queries + ids/scores
     attn_bytes = 2 * el * E * T_sel + 4 * E * BATCH + 4 * S     # selected K/V + queries + ids
     step_bytes = (el * E * C + 2 * el * E * T_sel + 8 * E * BATCH
@@ -320,7 +320,7 @@ def run_ours(args):
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
-        "dtype": "bf16 pages, f32 arithmetic" if bf16 else "f32",
+        "dtype": args.kv + " pages, f32 arithmetic" if bf16 else "f32",
         "data": "synthetic (device-generated N(0,1) Irwin-Hall, seed 7)",
         "config": {"workload": ("config3: batch %d in total (strong), ctx U{16384..32768}, H32 D128 "
                                 "P16 k64" % args.batch) if args.strong else
@@ -391,7 +391,7 @@ def run_continuous(args):
     spec = CONTINUOUS[args.workload]
     exe = os.path.join(ROOT, "15-618_dynamic_sparse_decode_b200", "bin", "dsd_continuous_bench")
     argv = [str(x) for x in spec["argv"]] + [str(world), str(rank), str(spec.get("repeats", 1)),
-                                             "1" if args.kv == "bf16" else "0"]
+                                             {"f32": "0", "bf16": "1", "fp8": "2"}[args.kv]]
     env = dict(os.environ, CUDA_VISIBLE_DEVICES=str(local))
     out = subprocess.run([exe, *argv], capture_output=True, text=True, env=env)
     if out.returncode != 0:
@@ -423,7 +423,7 @@ def run_continuous(args):
             "vs_baseline": (value / spec["published"]
                             if spec.get("published") and world == 1 and args.kv == "f32"
                             else None),
-            "dtype": "bf16 pages, f32 arithmetic" if args.kv == "bf16" else "f32",
+            "dtype": args.kv + " pages, f32 arithmetic" if args.kv != "f32" else "f32",
             "data": "synthetic (reference mt19937 workload generator)",
             "config": {"workload": spec["desc"], "kv_format": args.kv, "argv": argv,
                        "per_rank": [{k: round(v, 3) for k, v in r.items()} for r in ranks],
@@ -457,9 +457,9 @@ def main():
     ap.add_argument("--strong", action="store_true",
                     help="config 3 strong scaling: --batch requests in total, sharded by "
                          "request id over the ranks (default: weak, --batch per GPU)")
-    ap.add_argument("--kv", default="f32", choices=["f32", "bf16"],
-                    help="page format of the config-3 step: f32 (the reference's, default) or "
-                         "the opt-in bf16 pages (reported separately, never the headline)")
+    ap.add_argument("--kv", default="f32", choices=["f32", "bf16", "fp8"],
+                    help="page format: f32 (the reference's, default) or "
+                         "the opt-in bf16 / fp8 e4m3 pages (reported separately, never the headline)")
     args = ap.parse_args()
     BATCH = args.batch
     if args.impl == "reference":

@@ -101,10 +101,13 @@ int dsd_ctx_destroy(dsd_ctx* ctx);
  * rounded once, and a running-mean update reads the stored bf16 mean.  No
  * reference counterpart: the reference pool is fp32 only
  * (src/device_page_pool.cpp:241-284); the host API (float payloads in, float
- * downloads out) is the same for both formats. */
+ * downloads out) is the same for every format.  DSD_KV_FP8 follows the same
+ * rules with fp8 e4m3 storage (a quarter of the fp32 bytes). */
 #define DSD_KV_F32 0
 #define DSD_KV_BF16 1
-/* dsd_ctx_create with an explicit page format (bf16 needs head_dim >= 8).
+#define DSD_KV_FP8 2   /* fp8 e4m3 (saturating, round to nearest even); head_dim >= 16 */
+/* dsd_ctx_create with an explicit page format (bf16 needs head_dim >= 8,
+ * fp8 head_dim >= 16).
  * dsd_ctx_device_pointers then returns the pools as raw storage of that
  * format (cast the float pointers to __nv_bfloat16* for DSD_KV_BF16). */
 int dsd_ctx_create_ex(int device, const dsd_model_config* config, const dsd_ctx_options* options,

@@ -187,13 +187,14 @@ def running_mean_append(summary: np.ndarray, key: np.ndarray, old_count: int) ->
     return s
 
 
-# ---------------------------------------------------------------- bf16 page format
-# The opt-in bf16 page format has no reference counterpart (the reference pool
-# is fp32 only).  Its contract is stated here so the fp32 oracle can check it:
-# every stored K, V and summary element is the fp32 value rounded to nearest
-# even bf16; a page summary is AppendPage's fp32 mean of the ROUNDED keys,
-# rounded once; a running-mean update applies AppendToken's fp32 formula to
-# the stored (bf16) mean and the rounded key, then rounds.  Scoring and
+# ---------------------------------------------------------------- bf16 / fp8 page formats
+# The opt-in bf16 and fp8 e4m3 page formats have no reference counterpart (the
+# reference pool is fp32 only).  Their contract is stated here so the fp32
+# oracle can check it: every stored K, V and summary element is the fp32 value
+# rounded to nearest even in the format (fp8 saturating at +-448); a page
+# summary is AppendPage's fp32 mean of the ROUNDED keys, rounded once; a
+# running-mean update applies AppendToken's fp32 formula to the stored mean
+# and the rounded key, then rounds.  Scoring and
 # attention are the fp32 oracle run over those stored values.
 
 def bf16_round(a: np.ndarray) -> np.ndarray:
@@ -201,6 +202,38 @@ def bf16_round(a: np.ndarray) -> np.ndarray:
     u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
     r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
     return r.astype(np.uint32).view(np.float32).reshape(np.shape(a))
+
+
+def fp8_round(a: np.ndarray) -> np.ndarray:
+    """Round float32 values to the nearest fp8 e4m3 value (ties to even,
+    saturating at +-448; 3 mantissa bits, exponents -6..8, subnormal quantum
+    2^-9), as float32."""
+    x = np.ascontiguousarray(a, np.float32).astype(np.float64)
+    mag = np.abs(x)
+    _, e2 = np.frexp(mag)                      # mag = m * 2^e2, m in [0.5, 1)
+    q = np.exp2(np.maximum(e2 - 1, -6) - 3)    # spacing of e4m3 values near mag
+    r = np.minimum(np.rint(mag / q) * q, 448.0)
+    r[mag == 0] = 0.0
+    return np.copysign(r, x).astype(np.float32).reshape(np.shape(a))
+
+
+def stored_round(kv_format: int):
+    """The rounding a page format applies on store (0 fp32, 1 bf16, 2 fp8 e4m3)."""
+    return {0: lambda v: np.asarray(v, np.float32), 1: bf16_round, 2: fp8_round}[kv_format]
+
+
+def stored_batch(b: Batch, rnd) -> Batch:
+    """The batch as a context with rounding `rnd` on store holds it (pools
+    rounded, summaries recomputed from the rounded keys and rounded)."""
+    kp = rnd(b.key_pool)
+    vp = rnd(b.value_pool)
+    summ = np.zeros_like(b.summaries)
+    for p in range(b.capacity):
+        n = int(b.token_counts[p])
+        if n > 0:
+            summ[p] = rnd(page_summary(kp[p, :n]))
+    return Batch(b.num_heads, b.head_dim, b.page_size, b.top_k, kp, vp, summ,
+                 b.token_counts.copy(), b.queries, b.cand_offsets, b.cand_ids)
 
 
 def page_summary_bf16(keys: np.ndarray) -> np.ndarray:
@@ -212,17 +245,8 @@ def running_mean_append_bf16(summary: np.ndarray, key: np.ndarray, old_count: in
 
 
 def bf16_batch(b: Batch) -> Batch:
-    """The batch as a bf16-page context stores it (pools rounded, summaries
-    recomputed from the rounded keys); queries and candidates unchanged."""
-    kp = bf16_round(b.key_pool)
-    vp = bf16_round(b.value_pool)
-    summ = np.zeros_like(b.summaries)
-    for p in range(b.capacity):
-        n = int(b.token_counts[p])
-        if n > 0:
-            summ[p] = bf16_round(page_summary(kp[p, :n]))
-    return Batch(b.num_heads, b.head_dim, b.page_size, b.top_k, kp, vp, summ,
-                 b.token_counts.copy(), b.queries, b.cand_offsets, b.cand_ids)
+    """The batch as a bf16-page context stores it; queries and candidates unchanged."""
+    return stored_batch(b, bf16_round)
 
 
 def deterministic_token_vector(count, request_id, decode_step, stream) -> np.ndarray:

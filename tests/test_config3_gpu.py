@@ -6,7 +6,7 @@ the oracle: ids equal in order, scores bit for bit, outputs <= 1e-4.
 Size-independent properties cover the rest: every request selects exactly
 min(k, n) distinct pages of its own, and the outputs of the page-table step,
 the CSR step and the graph-replayed step agree bit for bit.  The same checks
-run on a bf16-page context against the oracle over the rounded values.
+run on bf16- and fp8-page contexts against the oracle over the rounded values.
 """
 import numpy as np
 import pytest
@@ -19,15 +19,14 @@ pytestmark = pytest.mark.gpu
 SAMPLED = [0, 37]
 
 
-@pytest.fixture(scope="module", params=["f32", "bf16"])
+@pytest.fixture(scope="module", params=[0, 1, 2], ids=["f32", "bf16", "fp8"])
 def cfg3(dsd, request):
-    bf16 = request.param == "bf16"
+    fmt = request.param
     ctx_lens = bench.workload_contexts()
-    ctx, cap, ids, counts = bench.build_workload(dsd, ctx_lens, 0,
-                                                 dsd.KV_BF16 if bf16 else dsd.KV_F32)
+    ctx, cap, ids, counts = bench.build_workload(dsd, ctx_lens, 0, fmt)
     q = bench.queries_host(dsd)
     res = ctx.decode_step(np.arange(bench.BATCH), q, output_mode=dsd.OUTPUT_DEBUG)
-    rnd = o.bf16_round if bf16 else (lambda a: a)
+    rnd = o.stored_round(fmt)
     yield dict(ctx=ctx, ctx_lens=ctx_lens, cap=cap, ids=ids, counts=counts, q=q, res=res, rnd=rnd)
     ctx.close()
 

@@ -21,9 +21,9 @@ pytestmark = pytest.mark.gpu
 class HostMirror:
     """PagePool + PagedKvCache bookkeeping with flat pools (oracle formulas)."""
 
-    def __init__(self, cap, P, E, bf16=False):
-        # bf16: the stored-format rounding of a bf16-page context
-        self.rnd = o.bf16_round if bf16 else (lambda a: np.asarray(a, np.float32))
+    def __init__(self, cap, P, E, kv_format=0):
+        # the rounding the context's page format applies on store
+        self.rnd = o.stored_round(kv_format)
         self.free = list(range(cap))           # pops from the back: LIFO
         self.kp = np.zeros((cap, P, E), np.float32)
         self.vp = np.zeros((cap, P, E), np.float32)
@@ -75,7 +75,7 @@ def run_continuous(dsd, H, D, P, K, n_req, max_active, window, pmin, pmax, dmin,
     max_pages = int(max(pages_for(int(a)) + pages_for(int(b)) for a, b in zip(pt, ds)))
     cap = min(int(sum(pages_for(int(a)) + pages_for(int(b)) for a, b in zip(pt, ds))),
               max_active * max_pages)
-    host = HostMirror(cap, P, E, bf16=kv_format == dsd.KV_BF16)
+    host = HostMirror(cap, P, E, kv_format)
     ctx = dsd.SparseDecodeContext(H, D, P, K, cap, max_active, max_active * max_pages,
                                   max_active * min(K, max_pages), max_requests=max_active,
                                   max_pages_per_request=max_pages, kv_format=kv_format)

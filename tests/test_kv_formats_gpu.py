@@ -1,11 +1,11 @@
-"""The opt-in bf16 page format vs the oracle (GPU).
+"""The opt-in bf16 and fp8 e4m3 page formats vs the oracle (GPU).
 
-A bf16-page context stores K, V and summaries rounded to nearest-even bf16
-and computes in fp32.  The checker is the fp32 oracle run over what such a
-context must store (oracle.bf16_batch / bf16_round / page_summary_bf16 /
-running_mean_append_bf16): stored values bit for bit, selected ids equal in
-order, scores bit for bit, outputs <= 1e-4 max-abs.  The fp32 format stays
-the default and the reference-parity path; nothing here changes it.
+Such a context stores K, V and summaries rounded to nearest even in the
+format (fp8 saturating) and computes in fp32.  The checker is the fp32
+oracle run over what the context must store (oracle.stored_batch /
+stored_round): stored values bit for bit, selected ids equal in order,
+scores bit for bit, outputs <= 1e-4 max-abs.  The fp32 format stays the
+default and the reference-parity path; nothing here changes it.
 """
 import numpy as np
 import pytest
@@ -16,13 +16,20 @@ from test_shapes_gpu import random_batch
 
 pytestmark = pytest.mark.gpu
 
+FORMATS = {"bf16": 1, "fp8": 2}     # DSD_KV_BF16, DSD_KV_FP8
 
-def bf16_ctx(dsd, b, top_k=None, **kw):
+
+@pytest.fixture(params=sorted(FORMATS))
+def fmt(request):
+    return FORMATS[request.param]
+
+
+def narrow_ctx(dsd, b, fmt, top_k=None, **kw):
     k = b.top_k if top_k is None else top_k
     n = np.diff(b.cand_offsets)
     opts = dict(capacity_pages=b.capacity, max_batch=max(1, b.batch),
                 max_candidates=max(1, int(n.sum())),
-                max_selected=max(1, int(np.minimum(n, k).sum())), kv_format=dsd.KV_BF16)
+                max_selected=max(1, int(np.minimum(n, k).sum())), kv_format=fmt)
     opts.update(kw)
     return dsd.SparseDecodeContext(b.num_heads, b.head_dim, b.page_size, k, **opts)
 
@@ -43,11 +50,11 @@ CASES = [
 
 
 @pytest.mark.parametrize("name,cfg", CASES, ids=[c[0] for c in CASES])
-def test_bf16_decode_matches_oracle_on_stored_values(dsd, name, cfg):
+def test_decode_matches_oracle_on_stored_values(dsd, fmt, name, cfg):
     b = o.synthetic_batch(*cfg)
-    ref = o.bf16_batch(b)
-    with bf16_ctx(dsd, b) as ctx:
-        assert ctx.lib.dsd_ctx_kv_format(ctx.h) == dsd.KV_BF16
+    ref = o.stored_batch(b, o.stored_round(fmt))
+    with narrow_ctx(dsd, b, fmt) as ctx:
+        assert ctx.lib.dsd_ctx_kv_format(ctx.h) == fmt
         ctx.upload_pool(b.key_pool, b.value_pool, b.token_counts)
         for p in range(0, b.capacity, max(1, b.capacity // 16)):
             k, v, s, n = ctx.download_page(p)
@@ -58,10 +65,10 @@ def test_bf16_decode_matches_oracle_on_stored_values(dsd, name, cfg):
         check(ctx.decode_batch(b.queries, b.cand_offsets, b.cand_ids), ref)
 
 
-def test_bf16_dense_mode(dsd):
+def test_dense_mode(dsd, fmt):
     b = o.synthetic_batch(8, 32, 16, 4, 6, 40, 300, 3)
-    ref = o.bf16_batch(b)
-    with bf16_ctx(dsd, b, max_selected=len(b.cand_ids)) as ctx:
+    ref = o.stored_batch(b, o.stored_round(fmt))
+    with narrow_ctx(dsd, b, fmt, max_selected=len(b.cand_ids)) as ctx:
         ctx.upload_pool(b.key_pool, b.value_pool, b.token_counts)
         ctx.set_dense(True)
         res = ctx.decode_batch(b.queries, b.cand_offsets, b.cand_ids)
@@ -70,44 +77,51 @@ def test_bf16_dense_mode(dsd):
 
 @pytest.mark.parametrize("H,D,P", [(4, 8, 16), (16, 16, 4), (64, 128, 2), (8, 64, 32), (3, 32, 1)],
                          ids=["d8", "d16", "e8192", "p32", "p1_h3"])
-def test_bf16_head_and_page_shapes(dsd, H, D, P):
+def test_head_and_page_shapes(dsd, fmt, H, D, P):
+    if fmt == FORMATS["fp8"] and D < 16:
+        pytest.skip("fp8 pages need head_dim >= 16")
     rng = np.random.default_rng(H * 1000 + D * 10 + P)
     b = random_batch(rng, H, D, P, 5, [3, 17, 40, 9])
-    with bf16_ctx(dsd, b) as ctx:
+    with narrow_ctx(dsd, b, fmt) as ctx:
         ctx.upload_pool(b.key_pool, b.value_pool, b.token_counts)
-        check(ctx.decode_batch(b.queries, b.cand_offsets, b.cand_ids), o.bf16_batch(b))
+        check(ctx.decode_batch(b.queries, b.cand_offsets, b.cand_ids),
+              o.stored_batch(b, o.stored_round(fmt)))
 
 
-def test_bf16_rejects_head_dim_4(dsd):
+def test_rejects_small_head_dim(dsd):
     with pytest.raises(dsd.InvalidArgument):
-        dsd.SparseDecodeContext(4, 4, 8, 2, 8, 1, 8, 2, kv_format=dsd.KV_BF16)
+        dsd.SparseDecodeContext(4, 4, 8, 2, 8, 1, 8, 2, kv_format=FORMATS["bf16"])
+    with pytest.raises(dsd.InvalidArgument):
+        dsd.SparseDecodeContext(4, 8, 8, 2, 8, 1, 8, 2, kv_format=FORMATS["fp8"])
 
 
-def test_bf16_generators_round_on_store(dsd):
+def test_generators_round_on_store(dsd, fmt):
     E, P = 64, 8
-    with dsd.SparseDecodeContext(4, 16, P, 3, 16, 4, 64, 12, kv_format=dsd.KV_BF16) as ctx:
+    rnd = o.stored_round(fmt)
+    summary = lambda keys: rnd(o.page_summary(rnd(keys)))
+    with dsd.SparseDecodeContext(4, 16, P, 3, 16, 4, 64, 12, kv_format=fmt) as ctx:
         ctx.prefill_synthetic([5, 6, 7], [8, 8, 3], request_id=11)
         ctx.generate_normal([3, 4], [8, 5], [2, 2], [0, 8], seed=9)
         for i, (pid, n) in enumerate([(5, 8), (6, 8), (7, 3)]):
             k, v, s, cnt = ctx.download_page(pid)
             ek = o.synthetic_prompt(11, i, n, E, 1)
             assert cnt == n
-            assert np.array_equal(k[:n], o.bf16_round(ek))
-            assert np.array_equal(v[:n], o.bf16_round(o.synthetic_prompt(11, i, n, E, 2)))
-            assert np.array_equal(s.view(np.uint32), o.page_summary_bf16(ek).view(np.uint32))
+            assert np.array_equal(k[:n], rnd(ek))
+            assert np.array_equal(v[:n], rnd(o.synthetic_prompt(11, i, n, E, 2)))
+            assert np.array_equal(s.view(np.uint32), summary(ek).view(np.uint32))
         for pid, first, n in ((3, 0, 8), (4, 8, 5)):
             k, v, s, cnt = ctx.download_page(pid)
             ek = o.normal_fill(9, 1, (2 << 40) + first * E, n * E).reshape(n, E)
-            assert np.array_equal(k[:n], o.bf16_round(ek))
-            assert np.array_equal(s.view(np.uint32), o.page_summary_bf16(ek).view(np.uint32))
-        # synthetic decode tokens: running mean over the stored bf16 mean
+            assert np.array_equal(k[:n], rnd(ek))
+            assert np.array_equal(s.view(np.uint32), summary(ek).view(np.uint32))
+        # synthetic decode tokens: running mean over the stored mean
         ctx.append_tokens_synthetic([7, 7], [3, 4], [11, 11], [0, 1])
         k, v, s, cnt = ctx.download_page(7)
-        summ = o.page_summary_bf16(o.synthetic_prompt(11, 2, 3, E, 1))
+        summ = summary(o.synthetic_prompt(11, 2, 3, E, 1))
         for off, step in ((3, 0), (4, 1)):
             key = o.synthetic_decode(11, step, E, 1)
-            assert np.array_equal(k[off], o.bf16_round(key))
-            summ = o.running_mean_append_bf16(summ, key, off)
+            assert np.array_equal(k[off], rnd(key))
+            summ = rnd(o.running_mean_append(summ, rnd(key), off))
         assert cnt == 5 and np.array_equal(s.view(np.uint32), summ.view(np.uint32))
         ctx.free_pages([7])
         _, _, s, _ = ctx.download_page(7)
@@ -116,20 +130,20 @@ def test_bf16_generators_round_on_store(dsd):
 
 @pytest.mark.parametrize("split_step,depth", [(False, 1), (True, 2)],
                          ids=["sync_step", "two_steps_in_flight"])
-def test_bf16_continuous_serving(dsd, split_step, depth):
+def test_continuous_serving(dsd, fmt, split_step, depth):
     assert run_continuous(dsd, 4, 16, 8, 3, 10, 4, 6, 20, 60, 3, 10, 7, split_step, depth,
-                          kv_format=dsd.KV_BF16) > 5
+                          kv_format=fmt) > 5
 
 
-def test_bf16_continuous_config4_shape(dsd):
+def test_continuous_config4_shape(dsd, fmt):
     assert run_continuous(dsd, 32, 128, 16, 8, 12, 6, 8, 1024, 4096, 4, 10, 7,
-                          kv_format=dsd.KV_BF16) > 5
+                          kv_format=fmt) > 5
 
 
 @pytest.mark.parametrize("admission", ["0", "1", "2"], ids=["cpu_cache", "direct", "synthetic"])
-def test_bf16_continuous_cli_serves_the_same_tokens(admission):
-    """dsd_continuous_bench with kv_format=1 (argv 26) serves the workload with
-    the same token accounting as the fp32 pool, in every admission mode."""
+def test_continuous_cli_serves_the_same_tokens(admission):
+    """dsd_continuous_bench with kv_format 1 or 2 (argv 26) serves the workload
+    with the same token accounting as the fp32 pool, in every admission mode."""
     import os
     import subprocess
     from conftest import ROOT
@@ -142,7 +156,10 @@ def test_bf16_continuous_cli_serves_the_same_tokens(admission):
         assert out.returncode == 0, out.stderr
         return dict(l.split("=", 1) for l in out.stdout.splitlines() if "=" in l)
 
-    f32, bf16 = run("0"), run("1")
-    assert f32["kv_format"] == "fp32" and bf16["kv_format"] == "bf16"
-    assert int(bf16["total_generated_tokens"]) == int(f32["total_generated_tokens"]) > 0
-    assert float(bf16["continuous_sparse_tokens_per_second"]) > 0
+    f32 = run("0")
+    assert f32["kv_format"] == "fp32" and int(f32["total_generated_tokens"]) > 0
+    for code, name in (("1", "bf16"), ("2", "fp8")):
+        r = run(code)
+        assert r["kv_format"] == name
+        assert int(r["total_generated_tokens"]) == int(f32["total_generated_tokens"])
+        assert float(r["continuous_sparse_tokens_per_second"]) > 0
