@@ -31,7 +31,7 @@
 namespace dsdk {
 
 // Storage element of the K/V pages and the summaries: fp32 (the parity
-// path) or bf16 (opt-in; arithmetic stays fp32, values round to nearest even
+// path), bf16 or fp8 e4m3 (opt-in; arithmetic stays fp32, values round to nearest even
 // when stored).  get/put convert one element, store4 four, round/round4
 // give the value the storage will hold.
 template <typename T>
@@ -560,12 +560,12 @@ __global__ void __launch_bounds__(kScoreThreads, 2) score_kernel(
 }
 
 // Narrow-row scoring: the score_kernel scheme with 128-byte row pieces per
-// stage (32 fp32 or 64 bf16 elements, 8 columns of 16 bytes), 144-byte padded
+// stage (32 fp32, 64 bf16 or 128 fp8 elements, 8 columns of 16 bytes), 144-byte padded
 // shared-memory rows (the 8 threads of a quarter warp read 8 different 16 B
 // bank groups), the fp32 query piece in its own region, and small stages so
 // 4 CTAs fit on an SM: twice the warps of score_kernel to hide the
 // per-thread dependent add chain.  The dot product is the same sequential
-// round-to-nearest chain; bf16 elements widen to fp32 exactly.
+// round-to-nearest chain; bf16 and fp8 elements widen to fp32 exactly.
 template <typename T>
 struct ScoreRows {
   static constexpr int kEP = 16 / int(sizeof(T));          // elements per 16 B
@@ -1102,17 +1102,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(
   }
 }
 
-// bf16 pages: split-K flash decode with 16-byte vectors of 8 bf16 (a head's
-// D/8 vectors over LP = D/(8*NV) lanes, so the 8 lanes of a quarter warp
-// read 128 contiguous bytes of one row) and fp32 queries, logits, softmax
-// and partials.  Warp-specialised: kAttnThreads consumer threads plus one
+// bf16 / fp8 pages: split-K flash decode with 16-byte vectors of VE = 8 bf16
+// or 16 fp8 elements (a head's D/VE vectors over LP = D/(VE*NV) lanes, so the
+// 8 lanes of a quarter warp read 128 contiguous bytes of one row) and fp32
+// queries, logits, softmax and partials.  Warp-specialised: kAttnThreads consumer threads plus one
 // producer warp whose lane 0 walks the CTA's units and keeps `nstages`
 // stages (tps K rows then tps V rows of one page, two cp.async.bulk copies)
 // in flight.  Consumers release a stage through its `empty` mbarrier (one
 // arrival per consumer warp), so refills never wait for a CTA-wide barrier
 // and the producer's page-table loads stay off the consumers' path.
 constexpr int kAttnBfThreads = kAttnThreads + 32;
-constexpr int kAttnBfRegTokens = 4;                 // tokens per bf16 stage (V held in registers)
+constexpr int kAttnBfRegTokens = 4;                 // tokens per narrow stage (V held in registers)
 
 // 16 bytes of page elements -> float2 pairs (elements 2h, 2h+1); widening is
 // exact.  bf16: a 16-bit shift / mask; fp8 e4m3: via half (exact).
@@ -1131,7 +1131,7 @@ __device__ __forceinline__ void unpack16(const uint4 raw, const __nv_fp8_e4m3*, 
   }
 }
 
-// The bf16 attention keeps its softmax in base 2: logits are scaled by
+// The narrow-page attention keeps its softmax in base 2: logits are scaled by
 // log2(e) and weights come from the hardware 2^x approximation
 // (ex2.approx.ftz, relative error ~2^-22); m is stored back in natural-log
 // units.  2^(x*log2 e) = e^x, so the outputs are the same softmax.
