@@ -398,11 +398,15 @@ void EnsureStage(dsd_ctx* c, size_t bytes) {
 bool IsPinnedHost(const void* p);
 bool IsPinnedHostPtr(const void* p) { return IsPinnedHost(p); }
 
-constexpr size_t kUploadChunk = size_t(16) << 20;   // bytes per pinned chunk
-constexpr int kUploadWorkers = 4;
+constexpr size_t kUploadChunk = size_t(4) << 20;    // bytes per pinned chunk
+// host threads staging a large pageable upload (about half the cores, 2..8)
+int UploadWorkers() {
+  const int hw = static_cast<int>(std::thread::hardware_concurrency());
+  return std::max(2, std::min(8, hw / 2));
+}
 
-// Host -> device copy of a large pageable buffer: kUploadWorkers threads each
-// copy 16 MiB chunks into their two pinned buffers and DMA them on their own
+// Host -> device copy of a large pageable buffer: UploadWorkers() threads each
+// copy 4 MiB chunks into their two pinned buffers and DMA them on their own
 // stream, so host copies and PCIe transfers overlap.  The context stream
 // then waits for every worker stream.  Pinned or small sources go directly.
 void BulkH2D(dsd_ctx* c, void* dst, const void* src, size_t bytes) {
@@ -412,7 +416,7 @@ void BulkH2D(dsd_ctx* c, void* dst, const void* src, size_t bytes) {
     return;
   }
   if (c->uploaders.empty()) {
-    c->uploaders.resize(kUploadWorkers);
+    c->uploaders.resize(static_cast<size_t>(UploadWorkers()));
     for (auto& u : c->uploaders) {
       Check(cudaStreamCreateWithFlags(&u.stream, cudaStreamNonBlocking), "upload stream");
       for (int b = 0; b < 2; ++b) {
