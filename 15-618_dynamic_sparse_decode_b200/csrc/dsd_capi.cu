@@ -409,12 +409,23 @@ int UploadWorkers() {
 // copy 4 MiB chunks into their two pinned buffers and DMA them on their own
 // stream, so host copies and PCIe transfers overlap.  The context stream
 // then waits for every worker stream.  Pinned or small sources go directly.
-void BulkH2D(dsd_ctx* c, void* dst, const void* src, size_t bytes) {
-  if (bytes == 0) return;
-  if (bytes < 2 * kUploadChunk || IsPinnedHostPtr(src)) {
-    H2D(c, dst, src, bytes);
-    return;
+struct UploadSegment {
+  void* dst;
+  const void* src;
+  size_t bytes;
+};
+
+void BulkH2D(dsd_ctx* c, const std::vector<UploadSegment>& in) {
+  // small or pinned segments go directly; the rest share one worker pass
+  std::vector<UploadSegment> segs;
+  for (const auto& g : in) {
+    if (g.bytes == 0) continue;
+    if (g.bytes < 2 * kUploadChunk || IsPinnedHostPtr(g.src))
+      H2D(c, g.dst, g.src, g.bytes);
+    else
+      segs.push_back(g);
   }
+  if (segs.empty()) return;
   if (c->uploaders.empty()) {
     c->uploaders.resize(static_cast<size_t>(UploadWorkers()));
     for (auto& u : c->uploaders) {
@@ -429,7 +440,14 @@ void BulkH2D(dsd_ctx* c, void* dst, const void* src, size_t bytes) {
   cudaEvent_t ready;
   Check(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming), "event");
   Check(cudaEventRecord(ready, c->stream), "event record");
-  const size_t nchunks = (bytes + kUploadChunk - 1) / kUploadChunk;
+  // chunk list over all segments: (segment, offset)
+  std::vector<std::pair<size_t, size_t>> chunks;
+  size_t total = 0;
+  for (size_t k = 0; k < segs.size(); ++k) {
+    for (size_t off = 0; off < segs[k].bytes; off += kUploadChunk) chunks.emplace_back(k, off);
+    total += segs[k].bytes;
+  }
+  const size_t nchunks = chunks.size();
   std::vector<std::string> errors(c->uploaders.size());
   std::vector<std::thread> pool;
   for (size_t w = 0; w < c->uploaders.size(); ++w) {
@@ -442,14 +460,15 @@ void BulkH2D(dsd_ctx* c, void* dst, const void* src, size_t bytes) {
       }
       int b = 0;
       for (size_t i = w; i < nchunks; i += c->uploaders.size(), b ^= 1) {
-        const size_t off = i * kUploadChunk;
-        const size_t len = std::min(kUploadChunk, bytes - off);
+        const UploadSegment& g = segs[chunks[i].first];
+        const size_t off = chunks[i].second;
+        const size_t len = std::min(kUploadChunk, g.bytes - off);
         if (cudaEventSynchronize(u.done[b]) != cudaSuccess) {
           errors[w] = "upload event wait failed";
           return;
         }
-        std::memcpy(u.pinned[b], static_cast<const unsigned char*>(src) + off, len);
-        if (cudaMemcpyAsync(static_cast<unsigned char*>(dst) + off, u.pinned[b], len,
+        std::memcpy(u.pinned[b], static_cast<const unsigned char*>(g.src) + off, len);
+        if (cudaMemcpyAsync(static_cast<unsigned char*>(g.dst) + off, u.pinned[b], len,
                             cudaMemcpyHostToDevice, u.stream) != cudaSuccess ||
             cudaEventRecord(u.done[b], u.stream) != cudaSuccess) {
           errors[w] = "upload copy failed";
@@ -465,7 +484,7 @@ void BulkH2D(dsd_ctx* c, void* dst, const void* src, size_t bytes) {
   for (auto& u : c->uploaders)
     for (int b = 0; b < 2; ++b)
       Check(cudaStreamWaitEvent(c->stream, u.done[b], 0), "upload join");
-  c->stats.h2d_bytes += bytes;
+  c->stats.h2d_bytes += total;
   c->stats.h2d_calls += nchunks;
   c->stats.h2d_large_calls += nchunks;
 }
@@ -1173,8 +1192,8 @@ int dsd_pool_upload_pages(dsd_ctx* c, const int32_t* page_ids, const int32_t* to
       }
       const size_t meta_bytes = meta.size() * sizeof(long long);
       EnsureStage(c, meta_off + meta_bytes);
-      BulkH2D(c, c->d_stage, keys + tok0 * c->ept, payload);
-      BulkH2D(c, c->d_stage + payload, values + tok0 * c->ept, payload);
+      BulkH2D(c, {{c->d_stage, keys + tok0 * c->ept, payload},
+                  {c->d_stage + payload, values + tok0 * c->ept, payload}});
       H2D(c, c->d_stage + meta_off, meta.data(), meta_bytes);
       const long long* d_off = reinterpret_cast<const long long*>(c->d_stage + meta_off);
       const int* d_ids = reinterpret_cast<const int*>(d_off + np);
