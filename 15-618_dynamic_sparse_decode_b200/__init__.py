@@ -305,8 +305,8 @@ class SparseDecodeContext:
         _check(self.lib.dsd_reset_transfer_stats(self.h))
 
     # ---- decode
-    def _results(self, batch, total_cand, total_sel, output_mode):
-        out = np.zeros((batch, self.ept), np.float32)
+    def _results(self, batch, total_cand, total_sel, output_mode, alloc_out=True):
+        out = np.zeros((batch, self.ept), np.float32) if alloc_out else None
         scores = np.zeros(max(1, total_cand), np.float32) if output_mode == OUTPUT_DEBUG else None
         sel = np.zeros(max(1, total_sel), np.int32) if output_mode == OUTPUT_DEBUG else None
         return out, scores, sel
@@ -381,10 +381,14 @@ class SparseDecodeContext:
         _check(self.lib.dsd_decode_step_begin(self.h, _ip(req), len(req), _fp(q), output_mode, 0))
         self._pending.append((len(req), output_mode, n))
 
-    def decode_step_end(self):
+    def decode_step_end(self, out=None):
+        """Waits for the oldest pending step; `out` (float32 [B][H*D]) receives
+        its outputs when given, else a new array does."""
         B, mode, n = self._pending.pop(0)
         total_sel = int(np.minimum(n, self.cfg.top_k_pages).sum())
-        out, scores, sel = self._results(B, int(n.sum()), total_sel, mode)
+        res_out, scores, sel = self._results(B, int(n.sum()), total_sel, mode,
+                                             alloc_out=out is None)
+        out = res_out if out is None else out
         _check(self.lib.dsd_decode_step_end(self.h, _fp(out), _fp(scores), _ip(sel), None))
         return dict(outputs=out, scores=None if scores is None else scores[: int(n.sum())],
                     selected=None if sel is None else sel[:total_sel])

@@ -269,6 +269,15 @@ struct dsd_ctx {
   // the graph)
   cudaStream_t copy_stream = nullptr;
   cudaEvent_t ev_part0_up = nullptr, ev_q1 = nullptr, ev_out0 = nullptr, ev_out0_done = nullptr;
+  // steps queued with dsd_decode_step_begin use per-slot device input/output
+  // buffers (slot 0: d_in / d_outputs / plan, slot 1: d_in1 / d_outputs1 /
+  // plan1): a slot's upload and result copies run on copy_stream, so they
+  // overlap the other slot's kernels on the context stream
+  unsigned char* d_in1 = nullptr;
+  float* d_outputs1 = nullptr;
+  cudaStream_t up_stream = nullptr;   // uploads of queued steps (results use copy_stream)
+  dsdk::StepPlan plan1{};
+  cudaEvent_t ev_in_ready[2] = {}, ev_graph_done[2] = {}, ev_out_read[2] = {};
 
   // pool: fp32, bf16 or fp8 e4m3 elements (kv_format); summary_floats counts elements
   int kv_format = DSD_KV_F32;
@@ -327,6 +336,7 @@ struct dsd_ctx {
   // graph reads the batch from the device header, so one graph serves every
   // batch size and composition
   struct StepGraph {
+    const dsdk::StepPlan* plan;
     const float* q;
     float* out;
     bool timed;
@@ -523,9 +533,8 @@ void RecordEvent(dsd_ctx* c, int i, bool capturing) {
 // between the stages.
 constexpr int kStepParts = 2;
 
-void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool capturing = false,
-                bool split_io = false) {
-  const dsdk::StepPlan& plan = c->plan;
+void LaunchStep(dsd_ctx* c, const dsdk::StepPlan& plan, const float* d_q, float* d_out,
+                bool timed, bool capturing = false, bool split_io = false) {
   const int target_units = 8 * c->num_sms;
   const int H = c->cfg.num_heads, D = c->cfg.head_dim, P = c->cfg.page_size;
   const int sel_grid = std::max(1, std::min(c->opt.max_batch, 2 * c->num_sms));
@@ -590,19 +599,20 @@ void LaunchStep(dsd_ctx* c, const float* d_q, float* d_out, bool timed, bool cap
 
 // Replays the step as a CUDA graph (captured on first use for this pointer pair).
 void LaunchStepGraph(dsd_ctx* c, const float* d_q, float* d_out, bool timed,
-                     bool split_io = false) {
+                     bool split_io = false, const dsdk::StepPlan* plan = nullptr) {
   split_io = split_io && !timed;
+  if (!plan) plan = &c->plan;
   for (auto& g : c->graphs) {
-    if (g.q == d_q && g.out == d_out && g.timed == timed && g.split_io == split_io &&
-        (!timed || g.ev_set == c->ev_set)) {
+    if (g.plan == plan && g.q == d_q && g.out == d_out && g.timed == timed &&
+        g.split_io == split_io && (!timed || g.ev_set == c->ev_set)) {
       Check(cudaGraphLaunch(g.exec, c->stream), "graph launch");
       return;
     }
   }
-  dsd_ctx::StepGraph g{d_q, d_out, timed, c->ev_set, split_io, nullptr, nullptr};
+  dsd_ctx::StepGraph g{plan, d_q, d_out, timed, c->ev_set, split_io, nullptr, nullptr};
   Check(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
   try {
-    LaunchStep(c, d_q, d_out, timed, true, split_io);
+    LaunchStep(c, *plan, d_q, d_out, timed, true, split_io);
   } catch (...) {
     cudaGraph_t dead = nullptr;
     cudaStreamEndCapture(c->stream, &dead);
@@ -716,6 +726,8 @@ void CopyOutputsSplit(dsd_ctx* c, float* h_out, int batch) {
 void RunHostStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int output_mode,
                  int timing, float* outputs, float* scores, int32_t* selected,
                  dsd_step_timing* out_timing, bool split_io = false) {
+  // queued (begin/end) steps may still be copying results out of d_outputs
+  for (cudaEvent_t e : c->ev_out_read) Check(cudaStreamWaitEvent(c->stream, e, 0), "wait");
   LaunchStepGraph(c, reinterpret_cast<const float*>(c->d_in + c->in_q_off), c->d_outputs,
                   timing != 0, split_io);
   const size_t out_bytes = size_t(batch) * c->ept * sizeof(float);
@@ -744,33 +756,64 @@ void RunHostStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int outpu
   }
 }
 
-// Queues the step and its result copies into the pinned staging of a free
-// slot; records the slot's done event when everything (status word
-// included) has landed on the host.
-void EnqueueStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int output_mode,
-                 int timing, bool split_io = false) {
+// Queues a step in a free slot: the step input goes up on up_stream into the
+// slot's device buffer (after the slot's previous step has consumed it), the
+// context stream runs the step graph once its input has landed and the
+// slot's previous outputs have been read, and the results (status word
+// included) come back on copy_stream into the slot's pinned staging; the
+// slot's done event marks the end.  Uploads and downloads use separate
+// streams, so the next step's upload does not queue behind this step's
+// download: one slot's copies overlap the other slot's kernels.
+void EnqueueStep(dsd_ctx* c, const float* queries, int batch, int total_cand, int total_sel,
+                 int output_mode, int timing) {
   if (c->pend_count >= 2) Fail(DSD_EINVAL, "two decode steps are already pending");
   const int slot = (c->pend_head + c->pend_count) & 1;
+  unsigned char* din = slot ? c->d_in1 : c->d_in;
+  float* dout = slot ? c->d_outputs1 : c->d_outputs;
+  const dsdk::StepPlan* plan = slot ? &c->plan1 : &c->plan;
+  cudaStream_t cs = c->copy_stream, us = c->up_stream;
+  const size_t qbytes = size_t(batch) * c->ept * 4;
+  // input
+  Check(cudaStreamWaitEvent(us, c->ev_graph_done[slot], 0), "slot wait");
+  const bool direct = queries != QPtr(c) && IsPinnedHost(queries);
+  if (!direct && queries != QPtr(c)) std::memcpy(QPtr(c), queries, qbytes);
+  Check(cudaMemcpyAsync(din, c->h_in, direct ? c->in_q_off : c->in_q_off + qbytes,
+                        cudaMemcpyHostToDevice, us), "H2D copy");
+  if (direct)
+    Check(cudaMemcpyAsync(din + c->in_q_off, queries, qbytes, cudaMemcpyHostToDevice, us),
+          "H2D copy");
+  CountH2D(c, c->in_q_off + qbytes);
+  Check(cudaEventRecord(c->ev_inputs, us), "event record");
+  Check(cudaEventRecord(c->ev_in_ready[slot], us), "event record");
+  // the step
+  Check(cudaStreamWaitEvent(c->stream, c->ev_in_ready[slot], 0), "input wait");
+  Check(cudaStreamWaitEvent(c->stream, c->ev_out_read[slot], 0), "output wait");
+  const int other = slot ^ 1;
+  if (c->pend_count > 0 && c->pend[other].output_mode == DSD_OUTPUT_DEBUG)
+    // scores and selected ids live in one device buffer: the other slot's copy first
+    Check(cudaStreamWaitEvent(c->stream, c->ev_out_read[other], 0), "output wait");
   c->ev_set = slot;
-  LaunchStepGraph(c, reinterpret_cast<const float*>(c->d_in + c->in_q_off), c->d_outputs,
-                  timing != 0, split_io);
+  LaunchStepGraph(c, reinterpret_cast<const float*>(din + c->in_q_off), dout, timing != 0,
+                  false, plan);
   c->ev_set = 0;
+  Check(cudaEventRecord(c->ev_graph_done[slot], c->stream), "event record");
+  // results
+  Check(cudaStreamWaitEvent(cs, c->ev_graph_done[slot], 0), "result wait");
   float* h_out = slot ? c->h_outputs1 : c->h_outputs;
-  if (output_mode != DSD_OUTPUT_NONE) {
-    if (split_io)
-      CopyOutputsSplit(c, h_out, batch);
-    else
-      D2H(c, h_out, c->d_outputs, size_t(batch) * c->ept * sizeof(float));
-  }
+  auto d2h = [&](void* dst, const void* src, size_t bytes) {
+    if (bytes == 0) return;
+    Check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, cs), "D2H copy");
+    CountD2H(c, bytes);
+  };
+  if (output_mode != DSD_OUTPUT_NONE) d2h(h_out, dout, qbytes);
   if (output_mode == DSD_OUTPUT_DEBUG) {
-    if (total_cand > 0)
-      D2H(c, slot ? c->h_scores1 : c->h_scores, c->d_scores, size_t(total_cand) * sizeof(float));
-    if (total_sel > 0)
-      D2H(c, slot ? c->h_selected1 : c->h_selected, c->d_selected, size_t(total_sel) * sizeof(int));
+    d2h(slot ? c->h_scores1 : c->h_scores, c->d_scores, size_t(total_cand) * sizeof(float));
+    d2h(slot ? c->h_selected1 : c->h_selected, c->d_selected, size_t(total_sel) * sizeof(int));
   }
-  Check(cudaMemcpyAsync(c->h_status, c->d_status, sizeof(int), cudaMemcpyDeviceToHost, c->stream),
+  Check(cudaMemcpyAsync(c->h_status, c->d_status, sizeof(int), cudaMemcpyDeviceToHost, cs),
         "status read");
-  Check(cudaEventRecord(c->ev[4 + slot], c->stream), "event record");
+  Check(cudaEventRecord(c->ev_out_read[slot], cs), "event record");
+  Check(cudaEventRecord(c->ev[4 + slot], cs), "event record");
   c->pend[slot] = dsd_ctx::PendingStep{true, batch, total_cand, total_sel, output_mode, timing};
   ++c->pend_count;
 }
@@ -963,7 +1006,10 @@ int dsd_ctx_create_ex(int device, const dsd_model_config* config, const dsd_ctx_
       Check(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming), "event");
       Check(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming), "event");
       Check(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking), "stream");
-      for (cudaEvent_t* e : {&c->ev_part0_up, &c->ev_q1, &c->ev_out0, &c->ev_out0_done})
+      Check(cudaStreamCreateWithFlags(&c->up_stream, cudaStreamNonBlocking), "stream");
+      for (cudaEvent_t* e : {&c->ev_part0_up, &c->ev_q1, &c->ev_out0, &c->ev_out0_done,
+                             &c->ev_in_ready[0], &c->ev_in_ready[1], &c->ev_graph_done[0],
+                             &c->ev_graph_done[1], &c->ev_out_read[0], &c->ev_out_read[1]})
         Check(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "event");
 
       const size_t cap = size_t(opt.capacity_pages);
@@ -1032,6 +1078,15 @@ int dsd_ctx_create_ex(int device, const dsd_model_config* config, const dsd_ctx_
       p.unit_off = q; q += mb + 1;
       p.misc = q;
       p.status = c->d_status;
+      if (opt.max_requests > 0) {
+        // second slot of queued steps: own input / output buffers, shared plan arrays
+        c->d_in1 = DeviceAlloc<unsigned char>(c->in_bytes, "step input (slot 1)");
+        c->d_outputs1 = DeviceAlloc<float>(size_t(mb) * ept, "outputs (slot 1)");
+        c->plan1 = p;
+        c->plan1.hdr = reinterpret_cast<const int*>(c->d_in1);
+        c->plan1.req = reinterpret_cast<const int*>(c->d_in1 + c->in_req_off);
+        c->plan1.cand_ids = reinterpret_cast<const int*>(c->d_in1 + c->in_ids_off);
+      }
 
       Check(cudaFuncSetAttribute(dsdk::score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)dsdk::kScoreSmem), "smem attribute");
@@ -1060,6 +1115,7 @@ int dsd_ctx_destroy(dsd_ctx* c) {
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
   if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
+  if (c->up_stream) cudaStreamSynchronize(c->up_stream);
   for (auto& g : c->graphs) {
     if (g.exec) cudaGraphExecDestroy(g.exec);
     if (g.graph) cudaGraphDestroy(g.graph);
@@ -1073,7 +1129,8 @@ int dsd_ctx_destroy(dsd_ctx* c) {
     if (u.stream) cudaStreamDestroy(u.stream);
   }
   void* dev[] = {c->k_pool, c->v_pool, c->summaries, c->token_counts, c->live, c->table,
-                 c->table_n, c->d_in, c->d_scores, c->d_selected, c->d_outputs, c->d_part_acc,
+                 c->table_n, c->d_in, c->d_in1, c->d_outputs1, c->d_scores, c->d_selected,
+                 c->d_outputs, c->d_part_acc,
                  c->d_part_ml, c->d_planbuf, c->d_status, c->d_stage};
   for (void* p : dev)
     if (p) cudaFree(p);
@@ -1088,9 +1145,12 @@ int dsd_ctx_destroy(dsd_ctx* c) {
   if (c->ev_inputs) cudaEventDestroy(c->ev_inputs);
   if (c->ev_fork) cudaEventDestroy(c->ev_fork);
   if (c->ev_join) cudaEventDestroy(c->ev_join);
-  for (cudaEvent_t e : {c->ev_part0_up, c->ev_q1, c->ev_out0, c->ev_out0_done})
+  for (cudaEvent_t e : {c->ev_part0_up, c->ev_q1, c->ev_out0, c->ev_out0_done, c->ev_in_ready[0],
+                        c->ev_in_ready[1], c->ev_graph_done[0], c->ev_graph_done[1],
+                        c->ev_out_read[0], c->ev_out_read[1]})
     if (e) cudaEventDestroy(e);
   if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
+  if (c->up_stream) cudaStreamDestroy(c->up_stream);
   if (c->stream2) cudaStreamDestroy(c->stream2);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
@@ -1663,9 +1723,7 @@ int dsd_decode_step_begin(dsd_ctx* c, const int32_t* request_ids, int batch,
     SetDevice(c);
     int tc = 0, ts = 0;
     PackSlots(c, request_ids, batch, &tc, &ts);
-    const bool split = SplitIo(batch, timing);
-    if (split) UploadQueriesSplit(c, queries, batch); else UploadQueries(c, queries, batch);
-    EnqueueStep(c, batch, tc, ts, output_mode, timing, split);
+    EnqueueStep(c, queries, batch, tc, ts, output_mode, timing);
   });
 }
 
