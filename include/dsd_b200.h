@@ -222,8 +222,10 @@ int dsd_decode_step(dsd_ctx* ctx, const int32_t* request_ids, int batch, const f
  * end waits for the OLDEST pending step and returns its results (copied out
  * of the context's pinned staging).  Work the caller queues on this context
  * in between (token appends, frees, the next begin) runs after the step on
- * the GPU.  Up to two steps may be pending; pinned caller queries passed to
- * begin must stay unchanged until the step ends. */
+ * the GPU.  Up to two steps may be pending; they alternate between two device
+ * input/output slots whose uploads and result copies run on their own
+ * streams, so one step's copies overlap the other's kernels.  Pinned caller
+ * queries passed to begin must stay unchanged until the step ends. */
 int dsd_decode_step_begin(dsd_ctx* ctx, const int32_t* request_ids, int batch,
                           const float* queries, int output_mode, int timing);
 int dsd_decode_step_end(dsd_ctx* ctx, float* outputs, float* scores, int32_t* selected,
