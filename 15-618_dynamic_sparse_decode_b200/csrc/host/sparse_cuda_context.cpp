@@ -142,6 +142,7 @@ SparseBatchCudaResult SparseCudaContext::Run(const std::vector<const RequestStat
           sel_off[static_cast<std::size_t>(r)] + std::max(0, std::min(config_.top_k_pages, n));
     }
     total_cand = offsets_.back();
+    ThrowIf(dsd_step_staging_wait(ctx_));   // a queued step may still read the staging
     PackQueries(requests);
   }
   const int total_sel = sel_off.back();
