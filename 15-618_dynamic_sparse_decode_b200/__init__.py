@@ -171,6 +171,17 @@ def _fp(a):
     return None if a is None else a.ctypes.data_as(_F32P)
 
 
+def _out_buffer(out, rows, cols):
+    """A caller-supplied result buffer: C-contiguous float32 with room for
+    rows x cols values (the library writes exactly that many)."""
+    if not (isinstance(out, np.ndarray) and out.dtype == np.float32 and
+            out.flags["C_CONTIGUOUS"] and out.size >= rows * cols):
+        raise InvalidArgument(int(DSD_EINVAL),
+                              f"out must be a C-contiguous float32 array of at least "
+                              f"{rows}x{cols} values")
+    return out
+
+
 def available() -> bool:
     return bool(load_library().dsd_available())
 
@@ -361,8 +372,8 @@ class SparseDecodeContext:
             n = np.zeros(1, np.int64)
             total_sel = 0
             scores = sel = None
-            if out is None:
-                out = np.zeros((B, self.ept), np.float32)
+            out = (np.zeros((B, self.ept), np.float32) if out is None
+                   else _out_buffer(out, B, self.ept))
         t = StepTiming()
         _check(self.lib.dsd_decode_step(self.h, _ip(req), B, _fp(q), output_mode, int(timing),
                                         _fp(out), _fp(scores), _ip(sel), ctypes.byref(t)))
@@ -388,7 +399,7 @@ class SparseDecodeContext:
         total_sel = int(np.minimum(n, self.cfg.top_k_pages).sum())
         res_out, scores, sel = self._results(B, int(n.sum()), total_sel, mode,
                                              alloc_out=out is None)
-        out = res_out if out is None else out
+        out = res_out if out is None else _out_buffer(out, B, self.ept)
         _check(self.lib.dsd_decode_step_end(self.h, _fp(out), _fp(scores), _ip(sel), None))
         return dict(outputs=out, scores=None if scores is None else scores[: int(n.sum())],
                     selected=None if sel is None else sel[:total_sel])

@@ -284,3 +284,10 @@ def test_step_io_split_by_request_range(dsd, orc, batch):
         ctx.decode_step_begin(reqs, b.queries)
         for _ in range(2):
             assert float(np.abs(ctx.decode_step_end()["outputs"] - out).max()) <= 1e-4
+        # a result buffer too small or of the wrong type is refused before any copy
+        with pytest.raises(dsd.InvalidArgument):
+            ctx.decode_step(reqs, q_pin, output_mode=dsd.OUTPUT_OUTPUTS,
+                            out=np.zeros((batch, b.ept - 1), np.float32))
+        with pytest.raises(dsd.InvalidArgument):
+            ctx.decode_step(reqs, q_pin, output_mode=dsd.OUTPUT_OUTPUTS,
+                            out=np.zeros((batch, b.ept), np.float64))
