@@ -864,6 +864,41 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(StepPlan plan,
     }
     __syncthreads();
 
+    int* out = selected + plan.sel_off[r];
+    if (k <= 64) {
+      // ---- up to 64 winners: one warp sorts them in registers (bitonic,
+      // descending), lane l holding elements l and l + 32, zero-padded; no
+      // block barriers
+      if (tid < 32) {
+        unsigned long long v[2] = {tid < k ? keys[tid] : 0ULL,
+                                   tid + 32 < k ? keys[tid + 32] : 0ULL};
+#pragma unroll
+        for (int size = 2; size <= 64; size <<= 1) {
+#pragma unroll
+          for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            if (stride == 32) {
+              // partners are the lane's two elements; size is 64, so descending
+              if (v[0] < v[1]) { const unsigned long long t = v[0]; v[0] = v[1]; v[1] = t; }
+            } else {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int e = h * 32 + tid;
+                const unsigned long long pv = __shfl_xor_sync(0xffffffffu, v[h], stride);
+                const bool desc = (e & size) == 0;
+                const bool lower = (tid & stride) == 0;
+                const bool keep_max = desc == lower;
+                v[h] = keep_max ? (v[h] > pv ? v[h] : pv) : (v[h] < pv ? v[h] : pv);
+              }
+            }
+          }
+        }
+        if (tid < k) out[tid] = ~static_cast<int>(v[0] & 0xffffffffULL);
+        if (tid + 32 < k) out[tid + 32] = ~static_cast<int>(v[1] & 0xffffffffULL);
+      }
+      __syncthreads();
+      continue;
+    }
+
     // ---- bitonic sort (descending) of the k winners, padded with zero keys
     int m = 1;
     while (m < k) m <<= 1;
@@ -885,7 +920,6 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(StepPlan plan,
         __syncthreads();
       }
     }
-    int* out = selected + plan.sel_off[r];
     for (int i = tid; i < k; i += blockDim.x) out[i] = ~static_cast<int>(keys[i] & 0xffffffffULL);
     __syncthreads();
   }
