@@ -25,15 +25,32 @@ _F = ctypes.POINTER(ctypes.c_float)
 _I = ctypes.POINTER(ctypes.c_int)
 
 
+def reference_root() -> str | None:
+    """Where the reference sources are: $REF_ROOT, else the ``reference_path``
+    recorded in the repository's BASELINE.json; None when neither exists."""
+    root = os.environ.get("REF_ROOT")
+    if not root:
+        try:
+            import json
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                root = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            root = None
+    return root if root and os.path.isdir(os.path.join(root, "src")) else None
+
+
 def build(with_reference: bool | None = None) -> None:
     """Compile the restatement (and, when the reference sources exist, _ref)."""
     targets = ["oracle"]
-    ref_root = os.environ.get("REF_ROOT", "/root/reference")
+    ref_root = reference_root()
     if with_reference is None:
-        with_reference = os.path.isdir(os.path.join(ref_root, "src"))
+        with_reference = ref_root is not None
     if with_reference:
-        targets.append("ref")
-    subprocess.run(["make", "-s", "-C", HERE, f"REF_ROOT={ref_root}", *targets], check=True)
+        if ref_root is None:
+            raise RuntimeError("reference sources not found: set REF_ROOT")
+        targets += ["ref", "ref_tests"]
+    extra = [f"REF_ROOT={ref_root}"] if ref_root else []
+    subprocess.run(["make", "-s", "-C", HERE, *extra, *targets], check=True)
 
 
 _lib = None
@@ -84,6 +101,10 @@ def ref():
         R.ref_batch_dense_cpu.argtypes = [ctypes.c_void_p, _F]
         R.ref_batch_time_sparse_cpu.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
         R.ref_batch_time_sparse_cpu.restype = ctypes.c_double
+        R.ref_batch_time_dense_cpu.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
+        R.ref_batch_time_dense_cpu.restype = ctypes.c_double
+        R.ref_deterministic_token_vector.argtypes = [ctypes.c_int] * 4 + [_F]
+        R.ref_continuous_workload.argtypes = [ctypes.c_int] * 9 + [_I, _I, _I, _I, _F, _F, _F]
         _ref = R
     return _ref
 
@@ -249,10 +270,18 @@ def bf16_batch(b: Batch) -> Batch:
     return stored_batch(b, bf16_round)
 
 
-def deterministic_token_vector(count, request_id, decode_step, stream) -> np.ndarray:
+def deterministic_token_vector(count, request_id, decode_step, stream, fn=None) -> np.ndarray:
+    """DeterministicTokenVector (src/continuous_batching.cpp:52-59) restated;
+    ``fn`` swaps in another implementation with the same C signature."""
     out = np.zeros(count, np.float32)
-    lib().orc_deterministic_token_vector(count, request_id, decode_step, stream, fp(out))
+    (fn or lib().orc_deterministic_token_vector)(count, request_id, decode_step, stream, fp(out))
     return out
+
+
+def ref_deterministic_token_vector(count, request_id, decode_step, stream) -> np.ndarray:
+    """The reference's own DeterministicTokenVector (needs _ref)."""
+    return deterministic_token_vector(count, request_id, decode_step, stream,
+                                      ref().ref_deterministic_token_vector)
 
 
 def synthetic_prompt(request, page_idx, n, ept, stream) -> np.ndarray:
@@ -274,29 +303,30 @@ def normal_fill(seed: int, kind: int, first_index: int, count: int) -> np.ndarra
 
 
 def continuous_workload(num_heads, head_dim, num_requests, arrival_window, min_prompt,
-                        max_prompt, min_decode, max_decode, seed, with_payloads=True):
-    """BuildSyntheticContinuousWorkload restated; specs in (arrival, id) order."""
-    L = lib()
+                        max_prompt, min_decode, max_decode, seed, with_payloads=True, fn=None):
+    """BuildSyntheticContinuousWorkload (src/continuous_batching.cpp:336-381)
+    restated; specs in (arrival, id) order.  ``fn`` swaps in another
+    implementation with the same C signature (the reference's, for pinning)."""
+    call = fn or lib().orc_continuous_workload
     ids, arr, pt, ds = (np.zeros(num_requests, np.int32) for _ in range(4))
+    args = (num_heads, head_dim, num_requests, arrival_window, min_prompt, max_prompt,
+            min_decode, max_decode, seed, ip(ids), ip(arr), ip(pt), ip(ds))
+    call(*args, None, None, None)    # sizes first
     if not with_payloads:
-        L.orc_continuous_workload(num_heads, head_dim, num_requests, arrival_window, min_prompt,
-                                  max_prompt, min_decode, max_decode, seed, ip(ids), ip(arr),
-                                  ip(pt), ip(ds), None, None, None)
         return dict(request_ids=ids, arrival_steps=arr, prompt_tokens=pt, decode_steps=ds)
-    # first pass for the sizes, second for the payloads
-    L.orc_continuous_workload(num_heads, head_dim, num_requests, arrival_window, min_prompt,
-                              max_prompt, min_decode, max_decode, seed, ip(ids), ip(arr), ip(pt),
-                              ip(ds), None, None, None)
     e = num_heads * head_dim
     total = int(pt.sum())
     pk = np.zeros((total, e), np.float32)
     pv = np.zeros((total, e), np.float32)
     q = np.zeros((num_requests, e), np.float32)
-    L.orc_continuous_workload(num_heads, head_dim, num_requests, arrival_window, min_prompt,
-                              max_prompt, min_decode, max_decode, seed, ip(ids), ip(arr), ip(pt),
-                              ip(ds), fp(pk), fp(pv), fp(q))
+    call(*args, fp(pk), fp(pv), fp(q))
     return dict(request_ids=ids, arrival_steps=arr, prompt_tokens=pt, decode_steps=ds,
                 prompt_keys=pk, prompt_values=pv, initial_queries=q)
+
+
+def ref_continuous_workload(*args, **kw):
+    """The reference's own BuildSyntheticContinuousWorkload (needs _ref)."""
+    return continuous_workload(*args, fn=ref().ref_continuous_workload, **kw)
 
 
 class RefBatch:
@@ -343,3 +373,6 @@ class RefBatch:
 
     def time_sparse_cpu(self, iterations: int, n_threads: int) -> float:
         return self.R.ref_batch_time_sparse_cpu(self.h, iterations, n_threads)
+
+    def time_dense_cpu(self, iterations: int, n_threads: int) -> float:
+        return self.R.ref_batch_time_dense_cpu(self.h, iterations, n_threads)

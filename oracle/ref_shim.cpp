@@ -135,4 +135,29 @@ double ref_batch_time_sparse_cpu(void* handle, int iterations, int n_threads) {
   return std::chrono::duration<double, std::milli>(t1 - t0).count() / std::max(1, iterations);
 }
 
+// Same for the reference dense_cpu step (DecodePipeline::RunDenseStep,
+// src/decode_pipeline.cpp:47-51): every token of every candidate page.
+double ref_batch_time_dense_cpu(void* handle, int iterations, int n_threads) {
+  auto* rb = static_cast<RefBatch*>(handle);
+  dsd::DecodePipeline pipeline(rb->config);
+  const int batch = static_cast<int>(rb->batch.requests.size());
+  n_threads = std::max(1, std::min(n_threads, batch));
+  const auto t0 = std::chrono::steady_clock::now();
+  for (int it = 0; it < iterations; ++it) {
+    std::vector<std::thread> pool;
+    for (int t = 0; t < n_threads; ++t) {
+      pool.emplace_back([&, t]() {
+        for (int r = t; r < batch; r += n_threads) {
+          volatile float sink =
+              pipeline.RunDenseStep(rb->batch.cache, rb->batch.requests[r]).output[0];
+          (void)sink;
+        }
+      });
+    }
+    for (auto& th : pool) th.join();
+  }
+  const auto t1 = std::chrono::steady_clock::now();
+  return std::chrono::duration<double, std::milli>(t1 - t0).count() / std::max(1, iterations);
+}
+
 }  // extern "C"

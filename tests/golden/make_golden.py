@@ -51,9 +51,45 @@ def digest(a: np.ndarray) -> str:
     return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
 
 
+# Continuous workload generator (src/continuous_batching.cpp:44-59, :336-381):
+# (name, (num_heads, head_dim, requests, arrival_window, min_prompt, max_prompt,
+#         min_decode, max_decode, seed), payload hashes?)
+CONTINUOUS_CASES = [
+    ("cont_small", (2, 4, 20, 10, 3, 9, 1, 4, 7), True),
+    ("cont_mid", (4, 8, 48, 16, 17, 80, 2, 12, 11), True),
+    # BASELINE config 4 (`dsd_continuous_bench 128 32 64 1024 4096 16 64 7 32 128 16 8`):
+    # the spec arrays only (the payloads are ~10.7 GB)
+    ("cont_cfg4", (32, 128, 128, 64, 1024, 4096, 16, 64, 7), False),
+]
+# DeterministicTokenVector(count, request, decode_step, stream)
+TOKEN_CASES = [(4096, 0, 1, 0), (4096, 5, 0, 1), (4096, 127, 63, 2), (128, 3, 7, 0),
+               (4096, 1000, 255, 1)]
+SPEC_FIELDS = ["request_ids", "arrival_steps", "prompt_tokens", "decode_steps"]
+PAYLOAD_FIELDS = ["prompt_keys", "prompt_values", "initial_queries"]
+
+
+def make_continuous():
+    out = {}
+    for name, cfg, payloads in CONTINUOUS_CASES:
+        w = o.ref_continuous_workload(*cfg, with_payloads=payloads)
+        out[f"{name}_config"] = np.array(cfg, np.int64)
+        for f in SPEC_FIELDS:
+            out[f"{name}_{f}"] = w[f]
+        if payloads:
+            for f in PAYLOAD_FIELDS:
+                out[f"{name}_sha256_{f}"] = np.array(digest(w[f]))
+        print(f"{name}: {len(w['request_ids'])} requests, "
+              f"{int(w['prompt_tokens'].sum())} prompt tokens")
+    out["tokens_cases"] = np.array(TOKEN_CASES, np.int64)
+    out["tokens_sha256"] = np.array([digest(o.ref_deterministic_token_vector(*t))
+                                     for t in TOKEN_CASES])
+    np.savez_compressed(os.path.join(HERE, "continuous_workload.npz"), **out)
+
+
 def main():
     if not o.ref_available():
         o.build(with_reference=True)
+    make_continuous()
     for name, cfg in CASES:
         rb = o.RefBatch(*cfg)
         b = rb.export()
