@@ -118,7 +118,7 @@ AttnShape MakeAttnShape(int num_heads, int head_dim, int page_size, int elem_byt
     a.slots = slots <= 1 ? 1 : slots <= 2 ? 2 : 4;
     // 32 KiB stages, as many as fit in ~200 KiB (at most 8)
     a.tps = std::max(1, std::min({page_size, 65536 / (2 * ept * elem_bytes),
-                                  dsdk::kAttnBfRegTokens}));
+                                  dsdk::attn_narrow_reg_tokens(a.slots)}));
     const size_t stage = size_t(2) * a.tps * ept * elem_bytes;
     a.nstages = int(std::max<size_t>(2, std::min<size_t>(8, (200u << 10) / stage)));
     a.smem = size_t(a.nstages) * (stage + 16);

@@ -205,6 +205,37 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   return true;
 }
 
+// Bounded wait that also gives up as soon as another warp of the CTA has
+// raised *abort (a shared flag): the timeout of one waiter then ends every
+// waiter's loop within one poll instead of one budget each.  On its own
+// expiry it sets the timeout status bit and raises *abort.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, int* status,
+                                                   volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long start = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort) return false;
+    if (clock64() - start > kWaitBudgetCycles) {
+      atomicOr(status, kStatusTimeout);
+      *abort = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+// After an abort: waits (bounded) for the copies of the last `nstages`
+// issues of a ring to land, so that no bulk copy still writes into this
+// CTA's shared memory when the CTA exits.  `issued` = stages issued so far;
+// issue i went to stage i % nstages with phase parity (i / nstages) & 1, and
+// only the latest issue of each stage can still be in flight.
+__device__ __forceinline__ void drain_ring(uint64_t* full, uint32_t issued, int nstages,
+                                           int* status) {
+  const uint32_t first = issued > uint32_t(nstages) ? issued - uint32_t(nstages) : 0u;
+  for (uint32_t i = first; i < issued; ++i)
+    mbar_wait(&full[i % uint32_t(nstages)], (i / uint32_t(nstages)) & 1u, status);
+}
+
 // Self-test of the bounded wait: one thread waits on a barrier phase that
 // nothing completes (no copy is issued, no thread arrives) with a small
 // budget.  The wait gives up, sets the timeout bit and the kernel returns.
@@ -1016,7 +1047,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(
 
   AttnWalk w{unit_begin + static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x), 0, 0, 0, 0,
              0, false};
+  uint32_t issued = 0;                            // thread 0: stages issued
   auto issue = [&](int s) {
+    ++issued;
     const int nt = min(tps, w.n - w.t0);
     const uint32_t bytes = uint32_t(nt) * uint32_t(ept) * 4u;
     float* st = stages + size_t(s) * stage_floats;
@@ -1068,7 +1101,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(
       const int n = min(__ldg(token_counts + page), page_size);
       for (int t0 = 0; t0 < n; t0 += tps, ++g) {
         const int s = g % kAttnStages;
-        if (!mbar_wait(&full[s], (g / kAttnStages) & 1, status)) { alive = false; break; }
+        // Each thread waits with its own budget; a thread that gives up still
+        // runs the stage (its shuffles need every lane) and the abort is
+        // decided for the whole CTA at the stage's closing barrier.
+        const bool gave_up = !mbar_wait(&full[s], (g / kAttnStages) & 1, status);
         const int nt = min(tps, n - t0);
         const float4* kst = reinterpret_cast<const float4*>(stages + size_t(s) * stage_floats);
         const float4* vst = kst + size_t(tps) * vec;
@@ -1112,7 +1148,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(
           lrun[m] = l;
           mrun[m] = cmax;
         }
-        __syncthreads();  // every thread is done with stage s
+        // every thread is done with stage s; a timeout anywhere stops the CTA
+        if (__syncthreads_or(gave_up)) { alive = false; break; }
         if (tid == 0) {
           if (attn_walk_next(w, plan, B, total_units, ppu, tps, page_size, selected, token_counts))
             issue(s);
@@ -1134,6 +1171,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(
       }
     }
   }
+  if (!alive && tid == 0) drain_ring(full, issued, kAttnStages, status);
 }
 
 // bf16 / fp8 pages: split-K flash decode with 16-byte vectors of VE = 8 bf16
@@ -1147,6 +1185,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(
 // and the producer's page-table loads stay off the consumers' path.
 constexpr int kAttnBfThreads = kAttnThreads + 32;
 constexpr int kAttnBfRegTokens = 4;                 // tokens per narrow stage (V held in registers)
+__host__ __device__ constexpr int attn_narrow_reg_tokens(int slots) {
+  return slots == 1 ? kAttnBfRegTokens : 1;
+}
 
 // 16 bytes of page elements -> float2 pairs (elements 2h, 2h+1); widening is
 // exact.  bf16: a 16-bit shift / mask; fp8 e4m3: via half (exact).
@@ -1186,6 +1227,10 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_narrow(
     int nparts) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   constexpr int kConsumerWarps = kAttnThreads / 32;
+  // tokens per stage held in registers: fewer when a thread serves several
+  // heads, so that V, q and the accumulators of all its slots stay within the
+  // 168 registers a thread of a 9-warp CTA can have (3 warps per SM sub-partition)
+  constexpr int RT = attn_narrow_reg_tokens(SLOTS);
   const int ept = num_heads * head_dim;
   constexpr int VE = 16 / int(sizeof(T));         // elements per 16-byte vector
   constexpr int VP = VE / 2;                      // float2 pairs per vector
@@ -1196,6 +1241,7 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_narrow(
   T* stages = reinterpret_cast<T*>(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + nstages * stage_elems * sizeof(T));
   uint64_t* empty = full + nstages;
+  __shared__ volatile int abort;                  // raised by the first waiter that gives up
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -1206,6 +1252,7 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_narrow(
       mbar_init(&empty[s], kConsumerWarps);
     }
     fence_barrier_init();
+    abort = 0;
   }
   __syncthreads();
 
@@ -1223,12 +1270,13 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_narrow(
       const size_t page_elems = size_t(page_size) * ept;
       AttnWalk w{unit_begin + static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x), 0, 0,
                  0, 0, 0, false};
-      for (uint32_t g = 0;; ++g) {
+      uint32_t g = 0;
+      for (;; ++g) {
         if (!attn_walk_next(w, plan, B, total_units, ppu, tps, page_size, selected, token_counts))
           break;
         const int s = g % nstages;
         const uint32_t use = g / nstages;
-        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, status)) break;
+        if (use > 0 && !mbar_wait_or_abort(&empty[s], (use - 1) & 1, status, &abort)) break;
         const int nt = min(tps, w.n - w.t0);
         const uint32_t bytes = uint32_t(nt) * uint32_t(ept) * uint32_t(sizeof(T));
         T* st = stages + size_t(s) * stage_elems;
@@ -1237,6 +1285,14 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_narrow(
         bulk_g2s(st, key_pool + src, bytes, &full[s]);
         bulk_g2s(st + size_t(tps) * ept, value_pool + src, bytes, &full[s]);
       }
+      // Normal end: stay until the consumers have released the last stages,
+      // so that an abort raised by a consumer after the last issue is seen.
+      // On an abort, no copy may still be writing shared memory at exit.
+      const uint32_t first = g > uint32_t(nstages) ? g - uint32_t(nstages) : 0u;
+      for (uint32_t i = first; i < g && !abort; ++i)
+        mbar_wait_or_abort(&empty[i % uint32_t(nstages)], (i / uint32_t(nstages)) & 1u, status,
+                           &abort);
+      if (abort) drain_ring(full, g, nstages, status);
     }
     return;
   }
@@ -1305,7 +1361,10 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_narrow(
       const int n = __shfl_sync(0xffffffffu, cnt, p - p_begin);
       for (int t0 = 0; t0 < n; t0 += tps, ++g) {
         const int s = g % nstages;
-        if (!mbar_wait(&full[s], (g / nstages) & 1, status)) { alive = false; break; }
+        // the warp leaves together (its shuffles need every lane), and the
+        // shared flag takes the other warps and the producer with it
+        const bool got = mbar_wait_or_abort(&full[s], (g / nstages) & 1, status, &abort);
+        if (!__all_sync(0xffffffffu, got)) { abort = 1; alive = false; break; }
         const int nt = min(tps, n - t0);
         const uint4* kst = reinterpret_cast<const uint4*>(stages + size_t(s) * stage_elems);
         const uint4* vst = kst + size_t(tps) * vec;
@@ -1314,12 +1373,12 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_narrow(
         // reduction, the softmax and the V accumulation.  A stage is held only
         // for its shared-memory reads and the partial dot products, so more of
         // the ring stays in flight.
-        uint4 vreg[SLOTS][kAttnBfRegTokens][NV];
-        float logit[SLOTS][kAttnBfRegTokens];
+        uint4 vreg[SLOTS][RT][NV];
+        float logit[SLOTS][RT];
 #pragma unroll
         for (int m = 0; m < SLOTS; ++m) {
 #pragma unroll
-          for (int t = 0; t < kAttnBfRegTokens; ++t) {
+          for (int t = 0; t < RT; ++t) {
             if (t < nt) {
               float2 d2 = make_float2(0.f, 0.f);
 #pragma unroll
@@ -1339,7 +1398,7 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_narrow(
 #pragma unroll
         for (int m = 0; m < SLOTS; ++m) {
 #pragma unroll
-          for (int t = 0; t < kAttnBfRegTokens; ++t) {
+          for (int t = 0; t < RT; ++t) {
             if (t < nt) {
               float d = logit[m][t];
               for (int o = LP >> 1; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
@@ -1351,7 +1410,7 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_narrow(
         for (int m = 0; m < SLOTS; ++m) {
           float cmax = mrun[m];
 #pragma unroll
-          for (int t = 0; t < kAttnBfRegTokens; ++t)
+          for (int t = 0; t < RT; ++t)
             if (t < nt) cmax = fmaxf(cmax, logit[m][t]);
           const float alpha = fast_exp2(mrun[m] - cmax);
           float l = lrun[m] * alpha;
@@ -1361,7 +1420,7 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_narrow(
 #pragma unroll
             for (int x = 0; x < VP; ++x) acc[m][j][x] = __fmul2_rn(acc[m][j][x], alpha2);
 #pragma unroll
-          for (int t = 0; t < kAttnBfRegTokens; ++t) {
+          for (int t = 0; t < RT; ++t) {
             if (t < nt) {
               const float beta = fast_exp2(logit[m][t] - cmax);
               l += beta;

@@ -127,43 +127,82 @@ def dist_env():
 
 # ---------------------------------------------------------------- reference arm
 
-def cpu_sample(steps, warmup):
-    """Reference sparse_cpu on CPU_SAMPLE_REQUESTS requests of the config-3 shape."""
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_sample(steps, warmup, with_dense=True):
+    """The reference's own CPU decode paths (oracle/_ref, compiled unchanged)
+    on CPU_SAMPLE_REQUESTS requests of the config-3 shape built by the
+    reference's BuildSyntheticBatch:
+      sparse_cpu on every host thread: each step decodes one request per
+                 thread (thread t takes request t mod 4 of the sample; the
+                 sample is read-only and shared), `steps` steps timed;
+      sparse_cpu on one thread: the 4 requests once each;
+      dense_cpu on one thread: one request (every token of its context).
+    Falls back to the oracle's restatement ("port") without oracle/_ref."""
     from oracle import oracle as o
     if not o.ref_available():
         o.build()
     kind = "reference" if o.ref_available() else "port"
-    threads = max(1, min(CPU_SAMPLE_REQUESTS, os.cpu_count() or 1))
+    threads = host_threads()
+    n = CPU_SAMPLE_REQUESTS
+    res = {"kind": kind, "cores": threads, "host_logical_cpus": os.cpu_count(),
+           "cpu_model": cpu_model()}
     if kind == "reference":
-        rb = o.RefBatch(H, D, P, K_TOP, CPU_SAMPLE_REQUESTS, CTX_LO, CTX_HI, SEED)
-        for _ in range(warmup):
-            rb.time_sparse_cpu(1, threads)
-        ms = [rb.time_sparse_cpu(1, threads) for _ in range(steps)]
+        rb = o.RefBatch(H, D, P, K_TOP, n, CTX_LO, CTX_HI, SEED)
+        for _ in range(max(1, warmup)):
+            rb.time_cpu(threads, threads)
+        ms = sum(rb.time_cpu(threads, threads) for _ in range(steps))
+        res["ms_per_step"] = ms / steps
+        res["value"] = steps * threads / (ms * 1e-3)
+        res["single_thread_sparse_cpu"] = n / (rb.time_cpu(n, 1) * 1e-3)
+        if with_dense:
+            res["single_thread_dense_cpu"] = 1 / (rb.time_cpu(1, 1, dense=True) * 1e-3)
         rb.close()
     else:
-        b = o.synthetic_batch(H, D, P, K_TOP, CPU_SAMPLE_REQUESTS, CTX_LO, CTX_HI, SEED)
-        for _ in range(warmup):
-            o.sparse_decode(b, n_threads=threads)
-        ms = []
+        b = o.synthetic_batch(H, D, P, K_TOP, n, CTX_LO, CTX_HI, SEED)
+        t_ = min(threads, n)
+        o.sparse_decode(b, n_threads=t_)
+        t0 = time.perf_counter()
         for _ in range(steps):
-            t0 = time.perf_counter()
-            o.sparse_decode(b, n_threads=threads)
-            ms.append((time.perf_counter() - t0) * 1e3)
-    ms_step = float(np.mean(ms))
-    return {
-        "value": CPU_SAMPLE_REQUESTS / (ms_step / 1e3), "unit": "tokens/s", "cores": threads,
-        "kind": kind, "ms_per_step": ms_step,
-        "sample": (f"{CPU_SAMPLE_REQUESTS} requests of the config-3 shape (ctx U{{{CTX_LO}.."
-                   f"{CTX_HI}}}, H{H} D{D} P{P} k{K_TOP}, reference BuildSyntheticBatch seed {SEED}),"
-                   f" sparse_cpu RunNaiveSparseStep, requests over {threads} host threads"),
-    }
+            o.sparse_decode(b, n_threads=t_)
+        ms = (time.perf_counter() - t0) * 1e3
+        res.update(cores=t_, ms_per_step=ms / steps, value=steps * n / (ms * 1e-3))
+        t0 = time.perf_counter()
+        o.sparse_decode(b, n_threads=1)
+        res["single_thread_sparse_cpu"] = n / (time.perf_counter() - t0)
+    res["unit"] = "tokens/s"
+    res["sample"] = (f"{n} requests of the config-3 shape (ctx U{{{CTX_LO}..{CTX_HI}}}, H{H} D{D} "
+                     f"P{P} k{K_TOP}, reference BuildSyntheticBatch seed {SEED}); value: "
+                     f"sparse_cpu RunNaiveSparseStep, one request per host thread per step on "
+                     f"{res['cores']} threads; single_thread_*: the same requests (sparse_cpu, "
+                     f"all {n}) and one request (dense_cpu RunDenseStep) on one thread")
+    return res
+
+
+CPU_KEYS = ("value", "unit", "cores", "kind", "sample", "host_logical_cpus", "cpu_model",
+            "single_thread_sparse_cpu", "single_thread_dense_cpu")
 
 
 def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
         return
-    cb = cpu_sample(args.steps, args.warmup)
+    cb = cpu_sample(args.steps, args.warmup, with_dense=False)
     line = {
         "impl": "reference", "metric": "sparse decode tokens/s", "value": cb["value"],
         "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -172,7 +211,7 @@ def run_reference(args):
         "config": {"workload": "config3 sample (host)", "requests": CPU_SAMPLE_REQUESTS,
                    "context": [CTX_LO, CTX_HI], "num_heads": H, "head_dim": D, "page_size": P,
                    "top_k_pages": K_TOP},
-        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "cpu_baseline": {k: cb[k] for k in CPU_KEYS if k in cb},
         "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -372,8 +411,8 @@ def run_ours(args):
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cb = cpu_sample(1, 0)
-        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        cb = cpu_sample(3, 1)
+        line["cpu_baseline"] = {k: cb[k] for k in CPU_KEYS if k in cb}
     if rank == 0:
         print(json.dumps(line), flush=True)
     ctx.close()

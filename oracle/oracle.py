@@ -99,10 +99,8 @@ def ref():
         R.ref_batch_export.argtypes = [ctypes.c_void_p, _F, _F, _F, _I, _F, _I, _I]
         R.ref_batch_sparse_cpu.argtypes = [ctypes.c_void_p, _I, _F, _F]
         R.ref_batch_dense_cpu.argtypes = [ctypes.c_void_p, _F]
-        R.ref_batch_time_sparse_cpu.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
-        R.ref_batch_time_sparse_cpu.restype = ctypes.c_double
-        R.ref_batch_time_dense_cpu.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
-        R.ref_batch_time_dense_cpu.restype = ctypes.c_double
+        R.ref_batch_time_cpu.argtypes = [ctypes.c_void_p] + [ctypes.c_int] * 3
+        R.ref_batch_time_cpu.restype = ctypes.c_double
         R.ref_deterministic_token_vector.argtypes = [ctypes.c_int] * 4 + [_F]
         R.ref_continuous_workload.argtypes = [ctypes.c_int] * 9 + [_I, _I, _I, _I, _F, _F, _F]
         _ref = R
@@ -371,8 +369,6 @@ class RefBatch:
         self.R.ref_batch_dense_cpu(self.h, fp(out))
         return out
 
-    def time_sparse_cpu(self, iterations: int, n_threads: int) -> float:
-        return self.R.ref_batch_time_sparse_cpu(self.h, iterations, n_threads)
-
-    def time_dense_cpu(self, iterations: int, n_threads: int) -> float:
-        return self.R.ref_batch_time_dense_cpu(self.h, iterations, n_threads)
+    def time_cpu(self, items: int, n_threads: int, dense: bool = False) -> float:
+        """Wall ms of `items` reference steps (request i % batch) on n_threads."""
+        return self.R.ref_batch_time_cpu(self.h, items, n_threads, int(dense))

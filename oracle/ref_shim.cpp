@@ -109,55 +109,34 @@ void ref_batch_dense_cpu(void* handle, float* outputs) {
   }
 }
 
-// Times `iterations` passes of the reference sparse_cpu step over the whole
-// batch, requests spread over n_threads host threads (the reference code is
-// single threaded per request; requests are independent).  Returns ms per pass.
-double ref_batch_time_sparse_cpu(void* handle, int iterations, int n_threads) {
+// Times `items` reference decode steps spread over n_threads host threads:
+// item i decodes request (i mod batch) of the batch, so a small resident
+// sample keeps every thread busy without materialising more requests (the
+// reference code is single threaded per request; requests are independent).
+// dense = 0: DecodePipeline::RunNaiveSparseStep (sparse_cpu,
+// src/decode_pipeline.cpp:13-46); dense = 1: DecodePipeline::RunDenseStep
+// (dense_cpu, src/decode_pipeline.cpp:47-51).  Returns the wall ms.
+double ref_batch_time_cpu(void* handle, int items, int n_threads, int dense) {
   auto* rb = static_cast<RefBatch*>(handle);
   dsd::DecodePipeline pipeline(rb->config);
   const int batch = static_cast<int>(rb->batch.requests.size());
-  n_threads = std::max(1, std::min(n_threads, batch));
+  n_threads = std::max(1, std::min(n_threads, items));
   const auto t0 = std::chrono::steady_clock::now();
-  for (int it = 0; it < iterations; ++it) {
-    std::vector<std::thread> pool;
-    for (int t = 0; t < n_threads; ++t) {
-      pool.emplace_back([&, t]() {
-        for (int r = t; r < batch; r += n_threads) {
-          volatile float sink =
-              pipeline.RunNaiveSparseStep(rb->batch.cache, rb->batch.requests[r]).output.output[0];
-          (void)sink;
-        }
-      });
-    }
-    for (auto& th : pool) th.join();
+  std::vector<std::thread> pool;
+  for (int t = 0; t < n_threads; ++t) {
+    pool.emplace_back([&, t]() {
+      for (int i = t; i < items; i += n_threads) {
+        const auto& req = rb->batch.requests[static_cast<std::size_t>(i % batch)];
+        volatile float sink = dense ? pipeline.RunDenseStep(rb->batch.cache, req).output[0]
+                                    : pipeline.RunNaiveSparseStep(rb->batch.cache, req)
+                                          .output.output[0];
+        (void)sink;
+      }
+    });
   }
+  for (auto& th : pool) th.join();
   const auto t1 = std::chrono::steady_clock::now();
-  return std::chrono::duration<double, std::milli>(t1 - t0).count() / std::max(1, iterations);
-}
-
-// Same for the reference dense_cpu step (DecodePipeline::RunDenseStep,
-// src/decode_pipeline.cpp:47-51): every token of every candidate page.
-double ref_batch_time_dense_cpu(void* handle, int iterations, int n_threads) {
-  auto* rb = static_cast<RefBatch*>(handle);
-  dsd::DecodePipeline pipeline(rb->config);
-  const int batch = static_cast<int>(rb->batch.requests.size());
-  n_threads = std::max(1, std::min(n_threads, batch));
-  const auto t0 = std::chrono::steady_clock::now();
-  for (int it = 0; it < iterations; ++it) {
-    std::vector<std::thread> pool;
-    for (int t = 0; t < n_threads; ++t) {
-      pool.emplace_back([&, t]() {
-        for (int r = t; r < batch; r += n_threads) {
-          volatile float sink =
-              pipeline.RunDenseStep(rb->batch.cache, rb->batch.requests[r]).output[0];
-          (void)sink;
-        }
-      });
-    }
-    for (auto& th : pool) th.join();
-  }
-  const auto t1 = std::chrono::steady_clock::now();
-  return std::chrono::duration<double, std::milli>(t1 - t0).count() / std::max(1, iterations);
+  return std::chrono::duration<double, std::milli>(t1 - t0).count();
 }
 
 }  // extern "C"

@@ -1,12 +1,15 @@
 """BASELINE config 3 at full size on one GPU (64 requests, 16k-32k context, k=64).
 
-The whole batch runs on the device; sampled requests are re-generated on the
-host with the oracle's restatement of the workload generator and decoded by
-the oracle: ids equal in order, scores bit for bit, outputs <= 1e-4.
-Size-independent properties cover the rest: every request selects exactly
-min(k, n) distinct pages of its own, and the outputs of the page-table step,
-the CSR step and the graph-replayed step agree bit for bit.  The same checks
-run on bf16- and fp8-page contexts against the oracle over the rounded values.
+The whole batch runs on the device.  With fp32 pages (the reference's
+format) EVERY one of the 64 requests is re-generated on the host with the
+oracle's restatement of the workload generator and decoded by the oracle:
+ids equal in order, scores bit for bit, outputs <= 1e-4.  The bf16- and
+fp8-page contexts run the same check, against the oracle over the rounded
+values, on 8 requests: both sides of the production step's two-range split
+(31, 32), the first and last request and four spread between.
+Size-independent properties cover every request in every format: each
+selects exactly min(k, n) distinct pages of its own, in (score desc, id asc)
+order of the device's scores.
 """
 import numpy as np
 import pytest
@@ -16,7 +19,8 @@ from oracle import oracle as o
 
 pytestmark = pytest.mark.gpu
 
-SAMPLED = [0, 37]
+# the step graph splits the 64 requests into ranges [0, 32) and [32, 64)
+SAMPLED = [0, 9, 20, 31, 32, 45, 54, 63]
 
 
 @pytest.fixture(scope="module", params=[0, 1, 2], ids=["f32", "bf16", "fp8"])
@@ -27,7 +31,7 @@ def cfg3(dsd, request):
     q = bench.queries_host(dsd)
     res = ctx.decode_step(np.arange(bench.BATCH), q, output_mode=dsd.OUTPUT_DEBUG)
     rnd = o.stored_round(fmt)
-    yield dict(ctx=ctx, ctx_lens=ctx_lens, cap=cap, ids=ids, counts=counts, q=q, res=res, rnd=rnd)
+    yield dict(fmt=fmt, ctx=ctx, ctx_lens=ctx_lens, cap=cap, ids=ids, counts=counts, q=q, res=res, rnd=rnd)
     ctx.close()
 
 
@@ -54,8 +58,13 @@ def test_selection_properties(cfg3):
         assert [int(own[i]) for i in order[:bench.K_TOP]] == s.tolist()
 
 
-@pytest.mark.parametrize("r", SAMPLED)
-def test_sampled_requests_match_oracle(cfg3, r):
+def test_requests_match_oracle(cfg3):
+    """fp32 pages: all 64 requests; bf16/fp8 pages: the sampled 8."""
+    for r in (range(bench.BATCH) if cfg3["fmt"] == 0 else SAMPLED):
+        check_request_against_oracle(cfg3, r)
+
+
+def check_request_against_oracle(cfg3, r):
     E, P = bench.E, bench.P
     ctx_lens, cap, res = cfg3["ctx_lens"], cfg3["cap"], cfg3["res"]
     n_tok = int(ctx_lens[r])
@@ -86,7 +95,9 @@ def test_sampled_requests_match_oracle(cfg3, r):
     sel, _, out, scores = o.sparse_decode(b)
     pages = (ctx_lens + P - 1) // P
     off = int(pages[:r].sum())
-    assert np.array_equal(res["scores"][off:off + n_pages].view(np.uint32), scores.view(np.uint32))
+    assert np.array_equal(res["scores"][off:off + n_pages].view(np.uint32),
+                          scores.view(np.uint32)), f"request {r}: scores differ"
     got = res["selected"][r * bench.K_TOP:(r + 1) * bench.K_TOP]
-    assert np.array_equal(got, sel + base)
-    assert float(np.abs(res["outputs"][r] - out[0]).max()) <= 1e-4
+    assert np.array_equal(got, sel + base), f"request {r}: selected pages differ"
+    diff = float(np.abs(res["outputs"][r] - out[0]).max())
+    assert diff <= 1e-4, f"request {r}: output max abs diff {diff}"
