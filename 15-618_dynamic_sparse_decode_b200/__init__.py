@@ -105,8 +105,8 @@ SIGNATURES = [
     ("dsd_kernels_per_step", ctypes.c_int, []),
     ("dsd_selftest_bounded_wait", ctypes.c_int, [_VP, ctypes.c_int64]),
     ("dsd_decode_batch_noalloc", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ModelConfig),
-                                                ctypes.c_int, _I32P, _VP, _VP, _VP, _VP, _VP,
-                                                _VP, _VP, _VP]),
+                                                ctypes.c_int, ctypes.c_int, _I32P, _VP, _VP,
+                                                _VP, _VP, _VP, _VP, _VP, _VP]),
 ]
 
 _lib = None

@@ -1851,9 +1851,24 @@ NaDevice& NaSetup(int device) {
   return d;
 }
 
+// Makes `device` current for the call and restores the caller's device on
+// every exit path (including a failure thrown by Fail/Check).
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int device) {
+    Check(cudaGetDevice(&prev), "cudaGetDevice");
+    if (prev != device) Check(cudaSetDevice(device), "cudaSetDevice");
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
 }  // namespace
 
-extern "C" int dsd_decode_batch_noalloc(int device, const dsd_model_config* config, int batch,
+extern "C" int dsd_decode_batch_noalloc(int device, const dsd_model_config* config,
+                                        int capacity_pages, int batch,
                                         const int32_t* cand_offsets, const int32_t* d_cand_ids,
                                         const float* d_queries, const float* d_summaries,
                                         const float* d_keys, const float* d_values,
@@ -1868,6 +1883,7 @@ extern "C" int dsd_decode_batch_noalloc(int device, const dsd_model_config* conf
       Fail(DSD_EINVAL, "unsupported model config");
     const int ept = cfg.num_heads * D;
     if (ept > kNaMaxEpt) Fail(DSD_EINVAL, "num_heads*head_dim exceeds the no-alloc limit 4096");
+    if (capacity_pages <= 0) Fail(DSD_EINVAL, "capacity_pages must be positive");
     if (batch < 0 || batch > kNaMaxBatch)
       Fail(DSD_EINVAL, "batch exceeds the no-alloc limit of 256 requests");
     if (batch == 0) return;
@@ -1889,7 +1905,7 @@ extern "C" int dsd_decode_batch_noalloc(int device, const dsd_model_config* conf
     if (!d_token_counts || (cand_offsets[batch] > 0 && !d_cand_ids))
       Fail(DSD_EINVAL, "null device array");
 
-    Check(cudaSetDevice(device), "cudaSetDevice");
+    DeviceGuard device_guard(device);
     NaDevice& nd = NaSetup(device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     int* base = nd.scratch;
@@ -1910,6 +1926,7 @@ extern "C" int dsd_decode_batch_noalloc(int device, const dsd_model_config* conf
     plan.unit_off = q; q += kNaMaxBatch + 1;
     plan.misc = q;
     plan.status = base + kNaHdr + 4;
+    plan.capacity = capacity_pages;   // the ids are checked on the device before use
     float* scores = reinterpret_cast<float*>(base + kNaScores);
     int* selected = base + kNaSelected;
     float* part_acc = reinterpret_cast<float*>(base + kNaPartAcc);
@@ -1937,6 +1954,6 @@ extern "C" int dsd_decode_batch_noalloc(int device, const dsd_model_config* conf
           "status read");
     Check(cudaStreamSynchronize(s), "stream synchronize");
     if (status & dsdk::kStatusTimeout) Fail(DSD_ETIMEOUT, "a device-side wait exceeded its budget");
-    if (status) Fail(DSD_EINVAL, "device kernels rejected the step input");
+    if (status) Fail(DSD_EINVAL, "a candidate page id is outside [0, capacity_pages)");
   });
 }

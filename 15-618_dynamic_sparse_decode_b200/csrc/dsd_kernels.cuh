@@ -152,6 +152,10 @@ struct StepPlan {
   int* unit_off;           // [B+1]
   int* misc;               // [0] pages per attention unit, [1] score tile size, [2] dense
   int* status;             // error bits
+  // > 0: the CSR candidate ids are range-checked on the device against this
+  // pool capacity before any page is read (callers whose ids never passed a
+  // host check); 0: the host validated them
+  int capacity;
 };
 
 // ------------------------------------------------------------------ PTX helpers
@@ -361,6 +365,21 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(StepPlan plan, int t
       n = plan.table_n[slot];
     }
     if (n < 0) { n = 0; atomicOr(plan.status, kStatusBadInput); }
+  }
+  if (plan.capacity > 0 && mode == 0) {
+    // ids straight from device memory: one out-of-range id rejects the step
+    // before any summary or page is loaded (every request then has no
+    // candidates, so the later kernels read nothing and write zero outputs)
+    const int total = B > 0 ? plan.req[B] : 0;
+    bool bad = false;
+    for (int i = threadIdx.x; i < total; i += blockDim.x) {
+      const int id = plan.cand_ids[i];
+      bad |= id < 0 || id >= plan.capacity;
+    }
+    if (__syncthreads_or(bad)) {
+      if (threadIdx.x == 0) atomicOr(plan.status, kStatusBadInput);
+      n = 0;
+    }
   }
   const int ksel = dense ? n : max(0, min(top_k, n));
   int v[2] = {n, ksel};

@@ -270,18 +270,25 @@ int dsd_selftest_bounded_wait(dsd_ctx* ctx, int64_t budget_cycles);
  * exits.  Limits: batch <= 256, total candidates <= 131072, total selected
  * pages (sum of min(k, n_r)) <= 8192, num_heads*head_dim <= 4096, top_k <= 4096;
  * larger sizes are rejected with DSD_EINVAL.
+ *   capacity_pages  pages in the pool the device arrays below describe
  *   cand_offsets  HOST array [batch+1] (validated here, copied to the device)
  *   d_cand_ids, d_queries [batch][H*D], d_summaries (pool summary layout),
  *   d_keys/d_values [cap][page_size][H*D], d_token_counts [cap], d_outputs
  *   [batch][H*D]: device pointers, float arrays 16-byte aligned; d_summaries in the
  *   pool's summary layout above (e.g. the pointer dsd_ctx_device_pointers returns).
- * Page ids are not range-checked (they live on the device).  Work is queued on
- * `stream` (a cudaStream_t, NULL = default stream) and the call waits for it.
+ * The page ids live on the device, so the first kernel checks every one
+ * against capacity_pages before any summary or page is read; an id outside
+ * [0, capacity_pages) makes the call return DSD_EINVAL with nothing loaded
+ * (d_outputs is then zero-filled).  Work is queued on `stream` (a
+ * cudaStream_t, NULL = default stream) and the call waits for it.  The call
+ * makes `device` current while it runs and restores the caller's current
+ * device before it returns.
  * The first call on a device looks up the array's device address and sets
  * kernel attributes; make that first call before any stream capture.  All
  * calls share the one array: calls that overlap on the GPU (other threads,
  * other streams) race and must be serialised by the caller. */
-int dsd_decode_batch_noalloc(int device, const dsd_model_config* config, int batch,
+int dsd_decode_batch_noalloc(int device, const dsd_model_config* config, int capacity_pages,
+                             int batch,
                              const int32_t* cand_offsets, const int32_t* d_cand_ids,
                              const float* d_queries, const float* d_summaries,
                              const float* d_keys, const float* d_values,
