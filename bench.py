@@ -15,8 +15,10 @@ every request: score all candidate pages, select the top 64, attend.
 --impl reference times the reference's own sparse_cpu code (oracle/_ref) on a
 bounded sample of the same workload shape on the host cores.
 
-Multi-GPU: torchrun, one process per GPU, each GPU owns its own 64 requests
-and page pool (request sharding, weak scaling, no collective on the data path).
+Multi-GPU: torchrun, one process per GPU.  Weak scaling (default): 64*N
+distinct requests, rank g owning the ids with id % N == g (64 per GPU) in its
+own page pool; --strong: 64 requests in total dealt the same way.  No
+collective on the data path.
 """
 from __future__ import annotations
 
@@ -266,15 +268,15 @@ def run_ours(args):
         raise RuntimeError("no sm_100 GPU visible")
     torch.cuda.set_device(local)
     global BATCH
-    gids = None
-    if args.strong:
-        # strong scaling: the --batch requests in total, rank g serving the
-        # requests with id % world == g (each with its single-GPU data)
-        gids = np.arange(args.batch)[rank::world]
-        ctx_lens = workload_contexts(args.batch)[gids]
-        BATCH = len(gids)
-    else:
-        ctx_lens = workload_contexts()
+    sharding = importlib.import_module("15-618_dynamic_sparse_decode_b200.sharding")
+    # Requests are dealt round-robin by global id (id % world == rank), each
+    # with the context length and data of that id in one global workload.
+    # strong: the --batch requests in total; weak: --batch per GPU, i.e.
+    # batch * world distinct requests (at N = 1 both are requests 0..63).
+    total = args.batch if args.strong else args.batch * world
+    gids = sharding.shard_round_robin(np.arange(total), world, rank)
+    ctx_lens = workload_contexts(total)[gids]
+    BATCH = len(gids)
     fmt = {"f32": dsd.KV_F32, "bf16": dsd.KV_BF16, "fp8": dsd.KV_FP8}[args.kv]
     bf16 = fmt != dsd.KV_F32          # a narrow (opt-in) page format
     ctx, cap, all_ids, all_counts = build_workload(dsd, ctx_lens, local, fmt, gids)
@@ -323,7 +325,6 @@ def run_ours(args):
             t = ctx.decode_bound_timed(dq.data_ptr(), do.data_ptr())
             for k_, v in t.items():
                 per_kernel[k_].append(v)
-    sharding = importlib.import_module("15-618_dynamic_sparse_decode_b200.sharding")
     ms_local = start.elapsed_time(stop)
     per_rank = sharding.gather_rank_stats({"ms_per_step": ms_local / args.steps},
                                           device=f"cuda:{local}")
@@ -380,7 +381,8 @@ def run_ours(args):
         "data": "synthetic (device-generated N(0,1) Irwin-Hall, seed 7)",
         "config": {"workload": ("config3: batch %d in total (strong), ctx U{16384..32768}, H32 D128 "
                                 "P16 k64" % args.batch) if args.strong else
-                               "config3: batch 64/GPU, ctx U{16384..32768}, H32 D128 P16 k64",
+                               "config3: batch 64/GPU (global request ids rank + world*r), "
+                               "ctx U{16384..32768}, H32 D128 P16 k64",
                    "kv_format": args.kv, "requests_per_gpu": BATCH, "candidate_pages_per_gpu": C,
                    "selected_pages_per_gpu": S, "selected_tokens_per_gpu": T_sel,
                    "step_bytes_per_gpu": step_bytes,
