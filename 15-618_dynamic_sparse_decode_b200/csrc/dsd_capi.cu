@@ -5,6 +5,7 @@
 // stream, pinned staging for the packed per-step H2D/D2H copies, the device
 // request page tables and a host mirror of those tables.
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
 #include <initializer_list>
@@ -25,6 +26,17 @@
 namespace {
 
 thread_local std::string g_last_error;
+
+// NVTX range over a host-side phase (entry points, and each stage of the step
+// while it is launched or captured), the counterpart of the reference's
+// ScopedStageTimer stages in a profiler timeline.  Header-only NVTX: without
+// an attached tool each push/pop is a no-op call.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 struct DsdError {
   int code;
@@ -542,10 +554,14 @@ void LaunchStep(dsd_ctx* c, const dsdk::StepPlan& plan, const float* d_q, float*
   const int comb_grid = std::max(1, std::min((pairs + 7) / 8, 8 * c->num_sms));
   const int nparts = timed ? 1 : kStepParts;
   if (timed) RecordEvent(c, 0, capturing);
+  NvtxRange nvtx_step("dsd.step");
   const int score_ctas =
       (c->kv_format != DSD_KV_F32 ? kScoreNarrowCtas : 2) * c->num_sms;
-  dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, c->stream>>>(plan, c->cfg.top_k_pages,
-                                                             target_units, score_ctas);
+  {
+    NvtxRange r("dsd.plan");
+    dsdk::plan_kernel<<<1, dsdk::kPlanThreads, 0, c->stream>>>(plan, c->cfg.top_k_pages,
+                                                               target_units, score_ctas);
+  }
   if (nparts > 1) {
     Check(cudaEventRecord(c->ev_fork, c->stream), "fork");
     Check(cudaStreamWaitEvent(c->stream2, c->ev_fork, 0), "fork wait");
@@ -555,6 +571,8 @@ void LaunchStep(dsd_ctx* c, const dsdk::StepPlan& plan, const float* d_q, float*
   }
   for (int part = 0; part < nparts; ++part) {
     cudaStream_t st = part == 0 ? c->stream : c->stream2;
+    NvtxRange nvtx_part(part == 0 ? "dsd.step.range0" : "dsd.step.range1");
+    nvtxRangePushA("dsd.score");
     if (c->kv_format == DSD_KV_F32) {
       dsdk::score_kernel<<<2 * c->num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, st>>>(
           plan, d_q, static_cast<const float*>(c->summaries), c->ept, c->scale, c->d_scores,
@@ -567,10 +585,14 @@ void LaunchStep(dsd_ctx* c, const dsdk::StepPlan& plan, const float* d_q, float*
                             c->ept, c->scale, c->d_scores, part, nparts);
       });
     }
+    nvtxRangePop();
     if (timed) RecordEvent(c, 1, capturing);
+    nvtxRangePushA("dsd.select");
     dsdk::select_kernel<<<sel_grid, dsdk::kSelectThreads, dsdk::kSelectSmem, st>>>(
         plan, c->d_scores, c->d_selected, part, nparts);
+    nvtxRangePop();
     if (timed) RecordEvent(c, 2, capturing);
+    nvtxRangePushA("dsd.attention");
     if (c->kv_format != DSD_KV_F32)
       WithKv(c, [&](auto tag) {
         using T = typename decltype(tag)::type;
@@ -583,8 +605,11 @@ void LaunchStep(dsd_ctx* c, const dsdk::StepPlan& plan, const float* d_q, float*
       LaunchAttn(c->attn, c->num_sms, st, plan, d_q, static_cast<const float*>(c->k_pool),
                  static_cast<const float*>(c->v_pool), c->token_counts, c->d_selected,
                  c->d_part_acc, c->d_part_ml, H, D, P, c->scale, part, nparts);
+    nvtxRangePop();
+    nvtxRangePushA("dsd.combine");
     dsdk::combine_kernel<<<comb_grid, 256, 0, st>>>(plan, c->d_part_acc, c->d_part_ml, H, D,
                                                     d_out, part, nparts);
+    nvtxRangePop();
     if (split_io && capturing && nparts > 1 && part == 0)
       Check(cudaEventRecordWithFlags(c->ev_out0, c->stream, cudaEventRecordExternal),
             "part output event");
@@ -1210,6 +1235,7 @@ int dsd_pool_reset(dsd_ctx* c) {
 int dsd_pool_upload_pages(dsd_ctx* c, const int32_t* page_ids, const int32_t* token_counts, int n,
                           const float* keys, const float* values, int compute_summary) {
   return Guard([&]() {
+    NvtxRange nvtx("dsd_pool_upload_pages");
     if (!c) Fail(DSD_EINVAL, "null context");
     if (n < 0) Fail(DSD_EINVAL, "negative page count");
     if (n == 0) return;
@@ -1278,6 +1304,7 @@ int dsd_pool_upload_pages(dsd_ctx* c, const int32_t* page_ids, const int32_t* to
 
 int dsd_pool_upload_summaries(dsd_ctx* c, const int32_t* page_ids, int n, const float* summaries) {
   return Guard([&]() {
+    NvtxRange nvtx("dsd_pool_upload_summaries");
     if (!c) Fail(DSD_EINVAL, "null context");
     if (n <= 0) return;
     SetDevice(c);
@@ -1301,6 +1328,7 @@ int dsd_pool_upload_summaries(dsd_ctx* c, const int32_t* page_ids, int n, const 
 int dsd_pool_prefill_synthetic(dsd_ctx* c, const int32_t* page_ids, const int32_t* token_counts,
                                int n, int request_id) {
   return Guard([&]() {
+    NvtxRange nvtx("dsd_pool_prefill_synthetic");
     if (!c) Fail(DSD_EINVAL, "null context");
     if (n <= 0) return;
     SetDevice(c);
@@ -1329,6 +1357,7 @@ int dsd_pool_generate_normal(dsd_ctx* c, const int32_t* page_ids, const int32_t*
                              const int32_t* request_ids, const int32_t* first_token, int n,
                              uint64_t seed) {
   return Guard([&]() {
+    NvtxRange nvtx("dsd_pool_generate_normal");
     if (!c) Fail(DSD_EINVAL, "null context");
     if (n <= 0) return;
     SetDevice(c);
@@ -1371,6 +1400,7 @@ void dsd_generate_normal_host(uint64_t seed, int kind, uint64_t first_index, int
 int dsd_append_tokens(dsd_ctx* c, const int32_t* page_ids, const int32_t* token_offsets,
                       const int32_t* request_ids, int n, const float* keys, const float* values) {
   return Guard([&]() {
+    NvtxRange nvtx("dsd_append_tokens");
     if (!c) Fail(DSD_EINVAL, "null context");
     if (n <= 0) return;
     if (!keys || !values) Fail(DSD_EINVAL, "token payload pointers must be non-null");
@@ -1433,6 +1463,7 @@ int dsd_append_tokens(dsd_ctx* c, const int32_t* page_ids, const int32_t* token_
 int dsd_append_tokens_synthetic(dsd_ctx* c, const int32_t* page_ids, const int32_t* token_offsets,
                                 const int32_t* request_ids, const int32_t* decode_steps, int n) {
   return Guard([&]() {
+    NvtxRange nvtx("dsd_append_tokens_synthetic");
     if (!c) Fail(DSD_EINVAL, "null context");
     if (n <= 0) return;
     SetDevice(c);
@@ -1470,6 +1501,7 @@ int dsd_append_tokens_synthetic(dsd_ctx* c, const int32_t* page_ids, const int32
 
 int dsd_pool_free_pages(dsd_ctx* c, const int32_t* page_ids, int n) {
   return Guard([&]() {
+    NvtxRange nvtx("dsd_pool_free_pages");
     if (!c) Fail(DSD_EINVAL, "null context");
     if (n <= 0) return;
     SetDevice(c);
@@ -1569,6 +1601,7 @@ int dsd_decode_batch(dsd_ctx* c, int batch, const float* queries, const int32_t*
                      const int32_t* cand_ids, int output_mode, int timing, float* outputs,
                      float* scores, int32_t* selected, dsd_step_timing* out_timing) {
   return Guard([&]() {
+    NvtxRange nvtx("dsd_decode_batch");
     if (!c) Fail(DSD_EINVAL, "null context");
     if (batch < 0) Fail(DSD_EINVAL, "negative batch");
     if (out_timing) *out_timing = dsd_step_timing{};
@@ -1606,6 +1639,7 @@ int dsd_decode_batch(dsd_ctx* c, int batch, const float* queries, const int32_t*
 
 int dsd_request_set_pages(dsd_ctx* c, int request_id, const int32_t* page_ids, int n) {
   return Guard([&]() {
+    NvtxRange nvtx("dsd_request_set_pages");
     if (!c) Fail(DSD_EINVAL, "null context");
     RequireTables(c);
     if (n < 0 || n > c->opt.max_pages_per_request)
@@ -1622,6 +1656,7 @@ int dsd_request_set_pages(dsd_ctx* c, int request_id, const int32_t* page_ids, i
 
 int dsd_request_append_pages(dsd_ctx* c, int request_id, const int32_t* page_ids, int n) {
   return Guard([&]() {
+    NvtxRange nvtx("dsd_request_append_pages");
     if (!c) Fail(DSD_EINVAL, "null context");
     RequireTables(c);
     for (int i = 0; i < n; ++i) ValidatePage(c, page_ids[i]);
@@ -1641,6 +1676,7 @@ int dsd_request_append_pages(dsd_ctx* c, int request_id, const int32_t* page_ids
 
 int dsd_request_release(dsd_ctx* c, int request_id, int free_pages) {
   return Guard([&]() {
+    NvtxRange nvtx("dsd_request_release");
     if (!c) Fail(DSD_EINVAL, "null context");
     RequireTables(c);
     auto it = c->slot_of.find(request_id);
@@ -1697,6 +1733,7 @@ int dsd_decode_step(dsd_ctx* c, const int32_t* request_ids, int batch, const flo
                     int output_mode, int timing, float* outputs, float* scores,
                     int32_t* selected, dsd_step_timing* out_timing) {
   return Guard([&]() {
+    NvtxRange nvtx("dsd_decode_step");
     if (!c) Fail(DSD_EINVAL, "null context");
     RequireTables(c);
     if (out_timing) *out_timing = dsd_step_timing{};
@@ -1715,6 +1752,7 @@ int dsd_decode_step(dsd_ctx* c, const int32_t* request_ids, int batch, const flo
 int dsd_decode_step_begin(dsd_ctx* c, const int32_t* request_ids, int batch,
                           const float* queries, int output_mode, int timing) {
   return Guard([&]() {
+    NvtxRange nvtx("dsd_decode_step_begin");
     if (!c) Fail(DSD_EINVAL, "null context");
     RequireTables(c);
     if (c->pend_count >= 2) Fail(DSD_EINVAL, "two decode steps are already pending");
@@ -1730,6 +1768,7 @@ int dsd_decode_step_begin(dsd_ctx* c, const int32_t* request_ids, int batch,
 int dsd_decode_step_end(dsd_ctx* c, float* outputs, float* scores, int32_t* selected,
                         dsd_step_timing* out_timing) {
   return Guard([&]() {
+    NvtxRange nvtx("dsd_decode_step_end");
     if (!c) Fail(DSD_EINVAL, "null context");
     if (out_timing) *out_timing = dsd_step_timing{};
     SetDevice(c);
@@ -1753,6 +1792,7 @@ int dsd_bind_requests(dsd_ctx* c, const int32_t* request_ids, int batch) {
 
 int dsd_decode_bound(dsd_ctx* c, const float* d_queries, float* d_outputs) {
   return Guard([&]() {
+    NvtxRange nvtx("dsd_decode_bound");
     if (!c) Fail(DSD_EINVAL, "null context");
     if (c->bound_batch <= 0) Fail(DSD_EINVAL, "no request set bound");
     SetDevice(c);
@@ -1763,6 +1803,7 @@ int dsd_decode_bound(dsd_ctx* c, const float* d_queries, float* d_outputs) {
 int dsd_decode_bound_timed(dsd_ctx* c, const float* d_queries, float* d_outputs,
                            dsd_step_timing* out_timing) {
   return Guard([&]() {
+    NvtxRange nvtx("dsd_decode_bound_timed");
     if (!c) Fail(DSD_EINVAL, "null context");
     if (c->bound_batch <= 0) Fail(DSD_EINVAL, "no request set bound");
     SetDevice(c);
@@ -1875,6 +1916,7 @@ extern "C" int dsd_decode_batch_noalloc(int device, const dsd_model_config* conf
                                         const int32_t* d_token_counts, float* d_outputs,
                                         void* stream) {
   return Guard([&]() {
+    NvtxRange nvtx("dsd_decode_batch_noalloc");
     if (!config || !cand_offsets) Fail(DSD_EINVAL, "null argument");
     const dsd_model_config cfg = *config;
     const int D = cfg.head_dim;

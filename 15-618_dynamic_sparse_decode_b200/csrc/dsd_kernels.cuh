@@ -1,7 +1,10 @@
 // dsd_kernels.cuh -- sm_100a kernels of the batched page-level sparse decode step.
 //
 // One decode step (SparseCudaContext::RunBatch in the reference,
-// src/cuda/sparse_batched_attention.cu:574-838) is five launches on one stream:
+// src/cuda/sparse_batched_attention.cu:574-838) is five kernels: plan, then
+// score -> select -> attention -> combine.  The production step is a CUDA
+// graph that splits the requests into two ranges whose four-kernel chains
+// run on two streams (fork/join inside the graph):
 //
 //   plan_kernel     per-request CSR offsets by a device prefix sum (replaces
 //                   the host PackSparseBatchInto, :24-96)
@@ -9,7 +12,7 @@
 //                   CPU's exact operation order (ScorePagesCpu,
 //                   src/reference_kernels.cpp:59-80) so page selection is
 //                   bit-identical to sparse_cpu; summaries stream HBM -> smem
-//                   through a 6-deep ring of coalesced 16 B cp.async copies
+//                   through a 3-stage ring of coalesced 16 B cp.async copies
 //   select_kernel   per-request top-min(k,n) by (score desc, page id asc)
 //                   (SelectTopKPagesCpu, :82-107) via a 64-bit radix select
 //   attn_kernel     split-K flash decode over the selected pages, all heads

@@ -4,11 +4,14 @@
 //             [iterations=5] [warmup=1] [num_heads=8] [head_dim=16] [page_size=16]
 // Sections and row names match, so the reference's experiment scripts parse
 // it.  Added keys: sparse_gpu_hbm_gbps, sparse_gpu_roofline_frac (against the
-// B200 HBM figure below), sparse_gpu_selection_exact.
+// HBM bandwidth HbmBytesPerSec finds), sparse_gpu_roofline_peak_gbps and
+// _peak_source, sparse_gpu_selection_exact.
 #include <algorithm>
 #include <chrono>
 #include <cstdint>
 #include <cstdlib>
+#include <fstream>
+#include <iterator>
 #include <iomanip>
 #include <iostream>
 #include <memory>
@@ -25,8 +28,39 @@
 namespace {
 
 using Clock = std::chrono::steady_clock;
-constexpr double kHbmBytesPerSec = 6.537e12;   // measured B200 copy bandwidth on this pool
 constexpr double kFp32FlopsPerSec = 75e12;      // B200 fp32 CUDA-core figure (context only)
+
+// HBM bandwidth the roofline fractions are quoted against, in bytes/s, and
+// where it came from: $DSD_HBM_GBS, else "hbm_gbs" of MEASURED_PEAKS.json
+// (the copy bandwidth measured on the machine, looked for in the working
+// directory and two levels above this executable), else a nominal 6.65 TB/s.
+std::string g_hbm_source = "fallback";
+double HbmBytesPerSec(const char* argv0) {
+  if (const char* env = std::getenv("DSD_HBM_GBS")) {
+    g_hbm_source = "DSD_HBM_GBS";
+    return std::atof(env) * 1e9;
+  }
+  std::string exe = argv0 ? argv0 : "";
+  const auto slash = exe.find_last_of('/');
+  const std::string dir = slash == std::string::npos ? "." : exe.substr(0, slash);
+  for (const std::string& path : {std::string("MEASURED_PEAKS.json"),
+                                 dir + "/../../MEASURED_PEAKS.json"}) {
+    std::ifstream f(path);
+    if (!f) continue;
+    const std::string text((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+    const auto key = text.find("\"hbm_gbs\"");
+    if (key == std::string::npos) continue;
+    const auto colon = text.find(':', key);
+    if (colon == std::string::npos) continue;
+    const double gbs = std::atof(text.c_str() + colon + 1);
+    if (gbs > 0) {
+      g_hbm_source = "measured";
+      return gbs * 1e9;
+    }
+  }
+  return 6650e9;
+}
+double kHbmBytesPerSec = 6650e9;
 
 int Arg(int argc, char** argv, int i, int dflt) { return argc > i ? std::atoi(argv[i]) : dflt; }
 
@@ -50,6 +84,7 @@ void AnalyticalRow(const std::string& name, double bytes, double flops) {
 }  // namespace
 
 int main(int argc, char** argv) {
+  kHbmBytesPerSec = HbmBytesPerSec(argc > 0 ? argv[0] : nullptr);
   dsd::ModelConfig config;
   config.top_k_pages = Arg(argc, argv, 1, 8);
   config.num_heads = Arg(argc, argv, 8, 8);
@@ -242,7 +277,9 @@ int main(int argc, char** argv) {
                               4.0 * (cand + 2.0 * total_sel + 3.0 * batch_size + 3.0);
     const double gbps = g_kernel > 0 ? step_bytes / (g_kernel * 1e-3) / 1e9 : 0.0;
     std::cout << std::fixed << std::setprecision(3) << "sparse_gpu_hbm_gbps=" << gbps << "\n"
-              << "sparse_gpu_roofline_frac=" << gbps * 1e9 / kHbmBytesPerSec << "\n";
+              << "sparse_gpu_roofline_frac=" << gbps * 1e9 / kHbmBytesPerSec << "\n"
+              << "sparse_gpu_roofline_peak_gbps=" << kHbmBytesPerSec / 1e9 << "\n"
+              << "sparse_gpu_roofline_peak_source=" << g_hbm_source << "\n";
   }
   std::cout << "\n== Reading Guide ==\n"
             << "End-to-End Total(ms) is the full wall time for that path.\n"
