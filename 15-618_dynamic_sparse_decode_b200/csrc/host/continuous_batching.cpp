@@ -326,8 +326,30 @@ ContinuousBatchStats RunContinuous(const ModelConfig& config,
   std::deque<Clock::time_point> step_starts;
   // Waits for the oldest queued step; its wall time runs from its BeginStep
   // to the moment its results are back on the host.
+  // step records awaiting their results (step_observer only)
+  std::deque<ContinuousStepRecord> records;
+  int step_index = 0;
+  auto record_step = [&]() {
+    if (!options.step_observer) return;
+    ContinuousStepRecord rec;
+    rec.step_index = step_index;
+    for (const auto& a : active) {
+      rec.request_ids.push_back(a.state.request_id);
+      rec.context_tokens.push_back(a.state.context_tokens);
+      rec.candidate_page_ids.push_back(a.state.candidate_page_ids);
+      rec.queries.push_back(a.state.query);
+    }
+    records.push_back(std::move(rec));
+  };
+  auto observe = [&](const SparseBatchCudaResult& out) {
+    if (!options.step_observer) return;
+    records.front().result = &out;
+    options.step_observer(records.front());
+    records.pop_front();
+  };
   auto finish_oldest = [&]() {
     const auto out = ctx.FinishStep();
+    observe(out);
     const double ms = Ms(step_starts.front(), Clock::now());
     step_starts.pop_front();
     stats.run_batch_wall_ms += ms;
@@ -384,12 +406,15 @@ ContinuousBatchStats RunContinuous(const ModelConfig& config,
     // are in flight: the host bookkeeping of this step's token appends, its
     // releases and the next step's admission overlap the GPU work (every
     // upload is ordered after the step on the context stream).
+    record_step();
+    ++step_index;
     if (tables) {
       step_starts.push_back(Clock::now());
       ctx.BeginStep(batch, run_opts);
     } else {
       const auto s0 = Clock::now();
       const auto out = ctx.RunBatch(batch, run_opts);
+      observe(out);
       const double ms = Ms(s0, Clock::now());
       stats.run_batch_wall_ms += ms;
       step_ms.push_back(ms);

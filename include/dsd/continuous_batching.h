@@ -6,6 +6,7 @@
 #pragma once
 
 #include <cstddef>
+#include <functional>
 #include <vector>
 
 #include "dsd/config.h"
@@ -33,6 +34,19 @@ struct ActiveDecodeRequest {
 
 enum class ContinuousPromptAdmissionMode { kCpuCache, kDirectGpuUpload, kSyntheticGpuPrefill };
 
+// This build: one decode step of the serving loop as the step observer sees
+// it -- the batch in launch order (request id, context tokens, the page list
+// the step selected from and the query the host handed over) and the step's
+// result (per_request outputs; selected ids and scores in kDebugTensors mode).
+struct ContinuousStepRecord {
+  int step_index = 0;
+  std::vector<int> request_ids;
+  std::vector<int> context_tokens;
+  std::vector<std::vector<PageId>> candidate_page_ids;
+  std::vector<std::vector<float>> queries;
+  const SparseBatchCudaResult* result = nullptr;
+};
+
 struct ContinuousDecodeOptions {
   int max_active_requests = 1;
   ContinuousPromptAdmissionMode prompt_admission_mode =
@@ -50,6 +64,10 @@ struct ContinuousDecodeOptions {
   // This build: page element format of the device pool (DSD_KV_F32, the
   // reference's, or DSD_KV_BF16: bf16 pages and summaries, fp32 arithmetic).
   int kv_format = 0;
+  // This build: called once per decode step, in step order, when the step's
+  // results are on the host (tracing and step-by-step checking).  Unset by
+  // default; the record and its result are valid during the call only.
+  std::function<void(const ContinuousStepRecord&)> step_observer;
 };
 
 struct ContinuousBatchStats {

@@ -17,6 +17,7 @@
 // build (no -march=native, no fast-math).
 
 #include <algorithm>
+#include <array>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -375,6 +376,38 @@ void orc_continuous_workload(int num_heads, int head_dim, int num_requests, int 
                   s.q.size() * sizeof(float));
       off += static_cast<long long>(s.k.size());
     }
+  }
+}
+
+// Spec draws without payloads: the lengths-only generator this build uses
+// where prompt payloads cannot be held on the host (BuildSyntheticContinuousSpecs
+// of the C++ API; no reference counterpart -- the reference always draws the
+// payloads, so its lengths at the same seed differ).  mt19937(seed), per
+// request arrival in [0, window], prompt and decode lengths, nothing else;
+// sorted by (arrival, id).
+void orc_continuous_specs_only(int num_requests, int arrival_window, int min_prompt,
+                               int max_prompt, int min_decode, int max_decode, int seed,
+                               int* request_ids, int* arrival_steps, int* prompt_tokens,
+                               int* decode_steps) {
+  std::mt19937 rng(static_cast<std::uint32_t>(seed));
+  std::uniform_int_distribution<int> arrival_dist(0, std::max(0, arrival_window));
+  std::uniform_int_distribution<int> prompt_dist(min_prompt, max_prompt);
+  std::uniform_int_distribution<int> decode_dist(min_decode, max_decode);
+  std::vector<std::array<int, 4>> specs;
+  for (int r = 0; r < num_requests; ++r) {
+    const int a = arrival_dist(rng);
+    const int p = prompt_dist(rng);
+    const int d = decode_dist(rng);
+    specs.push_back({a, r, p, d});
+  }
+  std::stable_sort(specs.begin(), specs.end(), [](const auto& x, const auto& y) {
+    return x[0] == y[0] ? x[1] < y[1] : x[0] < y[0];
+  });
+  for (int i = 0; i < num_requests; ++i) {
+    arrival_steps[i] = specs[static_cast<std::size_t>(i)][0];
+    request_ids[i] = specs[static_cast<std::size_t>(i)][1];
+    prompt_tokens[i] = specs[static_cast<std::size_t>(i)][2];
+    decode_steps[i] = specs[static_cast<std::size_t>(i)][3];
   }
 }
 

@@ -73,6 +73,7 @@ def lib():
         L.orc_synthetic_batch_fill.argtypes = [ctypes.c_int] * 7 + [_F, _F, _F, _I, _F, _I, _I]
         L.orc_deterministic_token_vector.argtypes = [ctypes.c_int] * 4 + [_F]
         L.orc_continuous_workload.argtypes = [ctypes.c_int] * 9 + [_I, _I, _I, _I, _F, _F, _F]
+        L.orc_continuous_specs_only.argtypes = [ctypes.c_int] * 7 + [_I, _I, _I, _I]
         L.orc_normal_value.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_uint64]
         L.orc_normal_value.restype = ctypes.c_float
         L.orc_normal_fill.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_uint64,
@@ -320,6 +321,15 @@ def continuous_workload(num_heads, head_dim, num_requests, arrival_window, min_p
     call(*args, fp(pk), fp(pv), fp(q))
     return dict(request_ids=ids, arrival_steps=arr, prompt_tokens=pt, decode_steps=ds,
                 prompt_keys=pk, prompt_values=pv, initial_queries=q)
+
+
+def continuous_specs_only(num_requests, arrival_window, min_prompt, max_prompt, min_decode,
+                          max_decode, seed):
+    """The lengths-only spec draws (this build's BuildSyntheticContinuousSpecs)."""
+    ids, arr, pt, ds = (np.zeros(num_requests, np.int32) for _ in range(4))
+    lib().orc_continuous_specs_only(num_requests, arrival_window, min_prompt, max_prompt,
+                                    min_decode, max_decode, seed, ip(ids), ip(arr), ip(pt), ip(ds))
+    return dict(request_ids=ids, arrival_steps=arr, prompt_tokens=pt, decode_steps=ds)
 
 
 def ref_continuous_workload(*args, **kw):

@@ -5,6 +5,8 @@
 //   dump_workload specs  H D N window min_prompt max_prompt min_decode max_decode seed OUT
 //       int32 ids[N], arrivals[N], prompt_tokens[N], decode_steps[N], then
 //       float32 prompt keys (packed), prompt values (packed), initial queries [N][E]
+//   dump_workload specs_only ...same arguments...
+//       the same layout from BuildSyntheticContinuousSpecs (no prompt payloads)
 //   dump_workload tokens COUNT REQUEST STEP STREAM OUT
 //       float32 DeterministicTokenVector(COUNT, REQUEST, STEP, STREAM)
 #include <cstdio>
@@ -26,14 +28,17 @@ void Write(std::FILE* f, const void* p, std::size_t bytes) {
 }  // namespace
 
 int main(int argc, char** argv) {
-  if (argc == 12 && std::strcmp(argv[1], "specs") == 0) {
+  const bool specs_only = argc == 12 && std::strcmp(argv[1], "specs_only") == 0;
+  if (argc == 12 && (specs_only || std::strcmp(argv[1], "specs") == 0)) {
     int a[9];
     for (int i = 0; i < 9; ++i) a[i] = std::atoi(argv[2 + i]);
     dsd::ModelConfig c;
     c.num_heads = a[0];
     c.head_dim = a[1];
-    const auto specs = dsd::BuildSyntheticContinuousWorkload(c, a[2], a[3], a[4], a[5], a[6],
-                                                             a[7], a[8]);
+    const auto specs =
+        specs_only
+            ? dsd::BuildSyntheticContinuousSpecs(c, a[2], a[3], a[4], a[5], a[6], a[7], a[8])
+            : dsd::BuildSyntheticContinuousWorkload(c, a[2], a[3], a[4], a[5], a[6], a[7], a[8]);
     std::FILE* f = std::fopen(argv[11], "wb");
     if (f == nullptr) return 1;
     std::vector<int> col(specs.size());

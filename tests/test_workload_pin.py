@@ -73,15 +73,15 @@ def dump_exe(tmp_path_factory):
     return exe
 
 
-def host_workload(exe, tmp_path, cfg):
+def host_workload(exe, tmp_path, cfg, mode="specs"):
     out = str(tmp_path / "w.bin")
-    subprocess.run([exe, "specs", *map(str, cfg), out], check=True)
+    subprocess.run([exe, mode, *map(str, cfg), out], check=True)
     raw = np.fromfile(out, np.uint8)
     n, e = cfg[2], cfg[0] * cfg[1]
     ints = raw[: 16 * n].view(np.int32).reshape(4, n)
     w = dict(zip(SPEC_FIELDS, ints))
     floats = raw[16 * n:].view(np.float32)
-    t = int(w["prompt_tokens"].sum())
+    t = int(w["prompt_tokens"].sum()) if mode == "specs" else 0
     w["prompt_keys"] = floats[: t * e].reshape(t, e)
     w["prompt_values"] = floats[t * e: 2 * t * e].reshape(t, e)
     w["initial_queries"] = floats[2 * t * e:].reshape(n, e)
@@ -114,3 +114,19 @@ def test_oracle_workload_matches_reference_library(cfg):
     for t in [(64, 0, 0, 0), (100, 9, 3, 2), (4096, 2047, 300, 1)]:
         assert np.array_equal(o.deterministic_token_vector(*t).view(np.uint32),
                               o.ref_deterministic_token_vector(*t).view(np.uint32))
+
+
+@pytest.mark.parametrize("cfg", [(32, 128, 96, 16, 256, 1536, 8, 24, 11),
+                                 (2, 4, 50, 0, 0, 7, 0, 3, 5)])
+def test_cpp_specs_without_payloads_match_oracle(dump_exe, tmp_path, cfg):
+    """This build's lengths-only generator (config 5's specs; no reference
+    counterpart) against the oracle's restatement, initial queries included."""
+    w = host_workload(dump_exe, tmp_path, cfg, mode="specs_only")
+    s = o.continuous_specs_only(*cfg[2:])
+    for f in SPEC_FIELDS:
+        assert np.array_equal(w[f], s[f]), f
+    assert w["prompt_keys"].size == 0 and w["prompt_values"].size == 0
+    e = cfg[0] * cfg[1]
+    for i, r in enumerate(s["request_ids"]):
+        q = o.deterministic_token_vector(e, int(r), 0, 0)
+        assert np.array_equal(w["initial_queries"][i].view(np.uint32), q.view(np.uint32))
