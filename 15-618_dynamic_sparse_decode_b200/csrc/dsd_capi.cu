@@ -261,9 +261,17 @@ struct KvTag { using type = T; };
 
 struct dsd_ctx {
   int device = 0;
-  dsd_model_config cfg{};
+  dsd_model_config cfg{};     // cfg.head_dim is the PHYSICAL head width (see padded)
   dsd_ctx_options opt{};
-  int ept = 0;
+  int ept = 0;                // physical elements per token row: num_heads * cfg.head_dim
+  // A head_dim that is not a power of two >= 4 is stored padded to one
+  // (user_head_dim 80 -> 128): every row the caller passes or receives has
+  // user_ept = num_heads * user_head_dim elements and is widened / narrowed
+  // at the boundary; the padding is zero, so dot products, softmax and the
+  // CPU's sequential score sums are unchanged.
+  int user_head_dim = 0;
+  int user_ept = 0;
+  bool padded = false;
   int num_sms = 0;
   AttnShape attn;     // attention launch shape
   float scale = 0.f;
@@ -529,6 +537,49 @@ void CheckStatus(dsd_ctx* c) {
   }
 }
 
+// ------------------------------------------------------------------ row layout
+
+// Caller rows ([rows][num_heads * user_head_dim]) into pool rows
+// ([rows][num_heads * head_dim]), zero padding; a plain copy when not padded.
+void PadRowsInto(const dsd_ctx* c, float* dst, const float* src, size_t rows) {
+  if (!c->padded) {
+    std::memcpy(dst, src, rows * size_t(c->ept) * sizeof(float));
+    return;
+  }
+  const int H = c->cfg.num_heads, d = c->user_head_dim, dp = c->cfg.head_dim;
+  for (size_t r = 0; r < rows; ++r)
+    for (int h = 0; h < H; ++h) {
+      float* o = dst + r * size_t(c->ept) + size_t(h) * dp;
+      std::memcpy(o, src + r * size_t(c->user_ept) + size_t(h) * d, size_t(d) * sizeof(float));
+      std::memset(o + d, 0, size_t(dp - d) * sizeof(float));
+    }
+}
+
+std::vector<float> PadRows(const dsd_ctx* c, const float* src, size_t rows) {
+  std::vector<float> out(rows * size_t(c->ept));
+  PadRowsInto(c, out.data(), src, rows);
+  return out;
+}
+
+// Pool rows back to caller rows (drops the padding).
+void UnpadRowsInto(const dsd_ctx* c, float* dst, const float* src, size_t rows) {
+  if (!c->padded) {
+    std::memcpy(dst, src, rows * size_t(c->ept) * sizeof(float));
+    return;
+  }
+  const int H = c->cfg.num_heads, d = c->user_head_dim, dp = c->cfg.head_dim;
+  for (size_t r = 0; r < rows; ++r)
+    for (int h = 0; h < H; ++h)
+      std::memcpy(dst + r * size_t(c->user_ept) + size_t(h) * d,
+                  src + r * size_t(c->ept) + size_t(h) * dp, size_t(d) * sizeof(float));
+}
+
+void RequireUnpadded(const dsd_ctx* c, const char* what) {
+  if (c->padded)
+    Fail(DSD_EINVAL, std::string(what) + " needs head_dim a power of two >= 4 (device rows "
+                     "are used as they are)");
+}
+
 // ------------------------------------------------------------------ step
 
 void RecordEvent(dsd_ctx* c, int i, bool capturing) {
@@ -684,11 +735,11 @@ int* IdsPtr(dsd_ctx* c) { return reinterpret_cast<int*>(c->h_in + c->in_ids_off)
 // go straight to the device; pageable ones through the pinned staging.
 void UploadQueries(dsd_ctx* c, const float* queries, int batch) {
   const size_t qbytes = size_t(batch) * c->ept * 4;
-  if (queries != QPtr(c) && IsPinnedHost(queries)) {
+  if (!c->padded && queries != QPtr(c) && IsPinnedHost(queries)) {
     H2D(c, c->d_in, c->h_in, c->in_q_off);
     H2D(c, c->d_in + c->in_q_off, queries, qbytes);
   } else {
-    if (queries != QPtr(c)) std::memcpy(QPtr(c), queries, qbytes);
+    if (queries != QPtr(c)) PadRowsInto(c, QPtr(c), queries, size_t(batch));
     H2D(c, c->d_in, c->h_in, c->in_q_off + qbytes);
   }
   Check(cudaEventRecord(c->ev_inputs, c->stream), "event record");
@@ -708,8 +759,8 @@ int SplitRow(int batch) { return int((long long)batch * 1 / kStepParts); }
 void UploadQueriesSplit(dsd_ctx* c, const float* queries, int batch) {
   const size_t row = size_t(c->ept) * 4;
   const int h0 = SplitRow(batch);
-  const bool direct = queries != QPtr(c) && IsPinnedHost(queries);
-  if (!direct && queries != QPtr(c)) std::memcpy(QPtr(c), queries, size_t(batch) * row);
+  const bool direct = !c->padded && queries != QPtr(c) && IsPinnedHost(queries);
+  if (!direct && queries != QPtr(c)) PadRowsInto(c, QPtr(c), queries, size_t(batch));
   const unsigned char* src1 =
       direct ? reinterpret_cast<const unsigned char*>(queries) + size_t(h0) * row
              : c->h_in + c->in_q_off + size_t(h0) * row;
@@ -756,7 +807,8 @@ void RunHostStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int outpu
   LaunchStepGraph(c, reinterpret_cast<const float*>(c->d_in + c->in_q_off), c->d_outputs,
                   timing != 0, split_io);
   const size_t out_bytes = size_t(batch) * c->ept * sizeof(float);
-  const bool direct_out = outputs && outputs != c->h_outputs && IsPinnedHost(outputs);
+  const bool direct_out =
+      !c->padded && outputs && outputs != c->h_outputs && IsPinnedHost(outputs);
   if (output_mode != DSD_OUTPUT_NONE && outputs) {
     if (split_io)
       CopyOutputsSplit(c, direct_out ? outputs : c->h_outputs, batch);
@@ -772,7 +824,7 @@ void RunHostStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int outpu
   CheckStatus(c);  // synchronises the stream
   if (timing) ReadTiming(c, out_timing);
   if (output_mode != DSD_OUTPUT_NONE && outputs && outputs != c->h_outputs && !direct_out)
-    std::memcpy(outputs, c->h_outputs, out_bytes);
+    UnpadRowsInto(c, outputs, c->h_outputs, size_t(batch));
   if (output_mode == DSD_OUTPUT_DEBUG) {
     if (scores && total_cand > 0)
       std::memcpy(scores, c->h_scores, size_t(total_cand) * sizeof(float));
@@ -800,8 +852,8 @@ void EnqueueStep(dsd_ctx* c, const float* queries, int batch, int total_cand, in
   const size_t qbytes = size_t(batch) * c->ept * 4;
   // input
   Check(cudaStreamWaitEvent(us, c->ev_graph_done[slot], 0), "slot wait");
-  const bool direct = queries != QPtr(c) && IsPinnedHost(queries);
-  if (!direct && queries != QPtr(c)) std::memcpy(QPtr(c), queries, qbytes);
+  const bool direct = !c->padded && queries != QPtr(c) && IsPinnedHost(queries);
+  if (!direct && queries != QPtr(c)) PadRowsInto(c, QPtr(c), queries, size_t(batch));
   Check(cudaMemcpyAsync(din, c->h_in, direct ? c->in_q_off : c->in_q_off + qbytes,
                         cudaMemcpyHostToDevice, us), "H2D copy");
   if (direct)
@@ -862,7 +914,7 @@ void FinishStep(dsd_ctx* c, float* outputs, float* scores, int32_t* selected,
   if (p.timing) ReadTiming(c, out_timing, slot);
   const float* h_out = slot ? c->h_outputs1 : c->h_outputs;
   if (p.output_mode != DSD_OUTPUT_NONE && outputs && outputs != h_out)
-    std::memcpy(outputs, h_out, size_t(p.batch) * c->ept * sizeof(float));
+    UnpadRowsInto(c, outputs, h_out, size_t(p.batch));
   if (p.output_mode == DSD_OUTPUT_DEBUG) {
     if (scores && p.total_cand > 0)
       std::memcpy(scores, slot ? c->h_scores1 : c->h_scores, size_t(p.total_cand) * sizeof(float));
@@ -986,16 +1038,20 @@ int dsd_ctx_create_ex(int device, const dsd_model_config* config, const dsd_ctx_
     if (!config || !options || !out) Fail(DSD_EINVAL, "null argument");
     if (kv_format != DSD_KV_F32 && kv_format != DSD_KV_BF16 && kv_format != DSD_KV_FP8)
       Fail(DSD_EINVAL, "unknown kv_format");
-    if (kv_format == DSD_KV_BF16 && config->head_dim < 8)
-      Fail(DSD_EINVAL, "bf16 pages need head_dim >= 8");
-    if (kv_format == DSD_KV_FP8 && config->head_dim < 16)
-      Fail(DSD_EINVAL, "fp8 pages need head_dim >= 16");
     *out = nullptr;
-    const dsd_model_config cfg = *config;
+    dsd_model_config cfg = *config;
     const dsd_ctx_options opt = *options;
-    const int D = cfg.head_dim;
-    if (cfg.num_heads <= 0 || D < 4 || D > 128 || (D & (D - 1)) != 0)
-      Fail(DSD_EINVAL, "head_dim must be a power of two in [4, 128] and num_heads positive");
+    const int user_d = cfg.head_dim;
+    if (cfg.num_heads <= 0 || user_d < 1 || user_d > 128)
+      Fail(DSD_EINVAL, "head_dim must be in [1, 128] and num_heads positive");
+    // physical head width: the next power of two, at least 4
+    int D = 4;
+    while (D < user_d) D *= 2;
+    cfg.head_dim = D;
+    if (kv_format == DSD_KV_BF16 && D < 8)
+      Fail(DSD_EINVAL, "bf16 pages need head_dim > 4");
+    if (kv_format == DSD_KV_FP8 && D < 16)
+      Fail(DSD_EINVAL, "fp8 pages need head_dim > 8");
     if (cfg.page_size <= 0) Fail(DSD_EINVAL, "page_size must be positive");
     if (cfg.top_k_pages < 0) Fail(DSD_EINVAL, "top_k_pages must be non-negative");
     if (cfg.top_k_pages > dsdk::kSelectMaxK)
@@ -1018,11 +1074,14 @@ int dsd_ctx_create_ex(int device, const dsd_model_config* config, const dsd_ctx_
       c->cfg = cfg;
       c->opt = opt;
       c->ept = ept;
+      c->user_head_dim = user_d;
+      c->user_ept = cfg.num_heads * user_d;
+      c->padded = user_d != D;
       c->num_sms = prop.multiProcessorCount;
       c->kv_format = kv_format;
       c->kv_elem = kv_format == DSD_KV_BF16 ? 2 : kv_format == DSD_KV_FP8 ? 1 : 4;
       c->attn = MakeAttnShape(cfg.num_heads, D, cfg.page_size, int(c->kv_elem));
-      c->scale = 1.0f / std::sqrt(static_cast<float>(D));
+      c->scale = 1.0f / std::sqrt(static_cast<float>(user_d));   // the caller's head_dim
       Check(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream");
       for (auto& e : c->ev) Check(cudaEventCreate(&e), "event");
       for (auto& e : c->ev_set1) Check(cudaEventCreate(&e), "event");
@@ -1206,6 +1265,7 @@ int dsd_step_staging_wait(dsd_ctx* c) {
 int dsd_step_host_buffers(dsd_ctx* c, float** queries, float** outputs) {
   return Guard([&]() {
     if (!c) Fail(DSD_EINVAL, "null context");
+    RequireUnpadded(c, "dsd_step_host_buffers");
     if (queries) *queries = QPtr(c);
     if (outputs) *outputs = c->h_outputs;
   });
@@ -1249,6 +1309,13 @@ int dsd_pool_upload_pages(dsd_ctx* c, const int32_t* page_ids, const int32_t* to
       total_tokens += token_counts[i];
     }
     if (!keys || !values) Fail(DSD_EINVAL, "host page payload pointers must be non-null");
+    std::vector<float> pad_k, pad_v;
+    if (c->padded) {
+      pad_k = PadRows(c, keys, size_t(total_tokens));
+      pad_v = PadRows(c, values, size_t(total_tokens));
+      keys = pad_k.data();
+      values = pad_v.data();
+    }
     const size_t row = size_t(c->ept) * sizeof(float);
     // process in groups whose payload fits a bounded staging buffer
     const size_t max_stage = size_t(256) << 20;
@@ -1309,6 +1376,11 @@ int dsd_pool_upload_summaries(dsd_ctx* c, const int32_t* page_ids, int n, const 
     if (n <= 0) return;
     SetDevice(c);
     for (int i = 0; i < n; ++i) ValidatePage(c, page_ids[i]);
+    std::vector<float> pad_s;
+    if (c->padded) {
+      pad_s = PadRows(c, summaries, size_t(n));
+      summaries = pad_s.data();
+    }
     const size_t sb = size_t(n) * c->ept * sizeof(float);
     const size_t ids_off = AlignUp(sb, 256);
     EnsureStage(c, ids_off + size_t(n) * 4);
@@ -1344,7 +1416,8 @@ int dsd_pool_prefill_synthetic(dsd_ctx* c, const int32_t* page_ids, const int32_
     WithKv(c, [&](auto tag) {
       using T = typename decltype(tag)::type;
       dsdk::prefill_synthetic_kernel<T><<<n, 256, 0, c->stream>>>(
-          d, d + n, request_id, c->ept, c->cfg.page_size, static_cast<T*>(c->k_pool),
+          d, d + n, request_id, c->ept, c->user_head_dim, c->cfg.head_dim, c->cfg.page_size,
+          static_cast<T*>(c->k_pool),
           static_cast<T*>(c->v_pool), static_cast<T*>(c->summaries), c->token_counts, c->live);
     });
     Check(cudaGetLastError(), "prefill kernel");
@@ -1379,8 +1452,8 @@ int dsd_pool_generate_normal(dsd_ctx* c, const int32_t* page_ids, const int32_t*
       WithKv(c, [&](auto tag) {
         using T = typename decltype(tag)::type;
         dsdk::generate_normal_kernel<T><<<grid, 256, 0, c->stream>>>(
-            d, d + m, d + 2 * m, d + 3 * m, c->ept, c->cfg.page_size,
-            dsdk::normal_seed_mix(seed, 1), dsdk::normal_seed_mix(seed, 2),
+            d, d + m, d + 2 * m, d + 3 * m, c->ept, c->user_head_dim, c->cfg.head_dim,
+            c->cfg.page_size, dsdk::normal_seed_mix(seed, 1), dsdk::normal_seed_mix(seed, 2),
             static_cast<T*>(c->k_pool), static_cast<T*>(c->v_pool),
             static_cast<T*>(c->summaries), c->token_counts, c->live);
       });
@@ -1436,8 +1509,8 @@ int dsd_append_tokens(dsd_ctx* c, const int32_t* page_ids, const int32_t* token_
     // payload in grouped order
     std::vector<float> sk(size_t(n) * c->ept), sv(size_t(n) * c->ept);
     for (int j = 0; j < n; ++j) {
-      std::memcpy(sk.data() + size_t(j) * c->ept, keys + size_t(order[j]) * c->ept, row);
-      std::memcpy(sv.data() + size_t(j) * c->ept, values + size_t(order[j]) * c->ept, row);
+      PadRowsInto(c, sk.data() + size_t(j) * c->ept, keys + size_t(order[j]) * c->user_ept, 1);
+      PadRowsInto(c, sv.data() + size_t(j) * c->ept, values + size_t(order[j]) * c->user_ept, 1);
     }
     H2D(c, c->d_stage, sk.data(), payload);
     H2D(c, c->d_stage + payload, sv.data(), payload);
@@ -1488,9 +1561,9 @@ int dsd_append_tokens_synthetic(dsd_ctx* c, const int32_t* page_ids, const int32
     WithKv(c, [&](auto tag) {
       using T = typename decltype(tag)::type;
       dsdk::append_synthetic_kernel<T><<<ng, 256, 0, c->stream>>>(
-          d, d + ng, toff, toff + n, toff + 2 * n, c->ept, c->cfg.page_size,
-          static_cast<T*>(c->k_pool), static_cast<T*>(c->v_pool), static_cast<T*>(c->summaries),
-          c->token_counts, c->live);
+          d, d + ng, toff, toff + n, toff + 2 * n, c->ept, c->user_head_dim, c->cfg.head_dim,
+          c->cfg.page_size, static_cast<T*>(c->k_pool), static_cast<T*>(c->v_pool),
+          static_cast<T*>(c->summaries), c->token_counts, c->live);
     });
     Check(cudaGetLastError(), "synthetic append kernel");
     // no wait: later users of the staging buffer are ordered on the same stream
@@ -1527,6 +1600,16 @@ int dsd_download_page(dsd_ctx* c, int page_id, float* keys, float* values, float
     ValidatePage(c, page_id);
     SetDevice(c);
     const size_t pf = size_t(c->cfg.page_size) * c->ept;
+    // padded head_dim: download pool rows, then drop the padding
+    float* const user_keys = keys;
+    float* const user_values = values;
+    float* const user_summary = summary;
+    std::vector<float> tk, tv, ts;
+    if (c->padded) {
+      if (keys) { tk.resize(pf); keys = tk.data(); }
+      if (values) { tv.resize(pf); values = tv.data(); }
+      if (summary) { ts.resize(size_t(c->ept)); summary = ts.data(); }
+    }
     const size_t el = c->kv_elem;
     const bool narrow = c->kv_format != DSD_KV_F32;
     // bf16 / fp8 pools land in host bytes and widen to fp32 after the sync
@@ -1568,6 +1651,12 @@ int dsd_download_page(dsd_ctx* c, int page_id, float* keys, float* values, float
       if (keys) widen(hk, keys);
       if (values) widen(hv, values);
       if (summary) widen(hs, summary);
+    }
+    if (c->padded) {
+      const size_t P = size_t(c->cfg.page_size);
+      if (user_keys) UnpadRowsInto(c, user_keys, tk.data(), P);
+      if (user_values) UnpadRowsInto(c, user_values, tv.data(), P);
+      if (user_summary) UnpadRowsInto(c, user_summary, ts.data(), 1);
     }
   });
 }
@@ -1794,6 +1883,7 @@ int dsd_decode_bound(dsd_ctx* c, const float* d_queries, float* d_outputs) {
   return Guard([&]() {
     NvtxRange nvtx("dsd_decode_bound");
     if (!c) Fail(DSD_EINVAL, "null context");
+    RequireUnpadded(c, "dsd_decode_bound");
     if (c->bound_batch <= 0) Fail(DSD_EINVAL, "no request set bound");
     SetDevice(c);
     LaunchStepGraph(c, d_queries, d_outputs, false);
@@ -1805,6 +1895,7 @@ int dsd_decode_bound_timed(dsd_ctx* c, const float* d_queries, float* d_outputs,
   return Guard([&]() {
     NvtxRange nvtx("dsd_decode_bound_timed");
     if (!c) Fail(DSD_EINVAL, "null context");
+    RequireUnpadded(c, "dsd_decode_bound_timed");
     if (c->bound_batch <= 0) Fail(DSD_EINVAL, "no request set bound");
     SetDevice(c);
     LaunchStepGraph(c, d_queries, d_outputs, true);

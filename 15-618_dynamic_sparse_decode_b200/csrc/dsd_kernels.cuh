@@ -1752,10 +1752,17 @@ __device__ __forceinline__ float decode_value(int request, int step, int element
 // Synthetic prefill: page i is page_idx i of `request`; summary by AppendPage's formula.
 // The key (stream 1) and value (stream 2) hashes share every combine step but
 // the last, so the shared prefix is computed once per element and token.
+// Element e of a pool row (physical head width hdp) -> its index in the
+// caller's row (head width hd <= hdp), or -1 for padding columns.
+__device__ __forceinline__ int logical_element(int e, int hd, int hdp) {
+  const int h = e / hdp, d = e - h * hdp;
+  return d < hd ? h * hd + d : -1;
+}
+
 template <typename T>
 __global__ void prefill_synthetic_kernel(const int* __restrict__ page_ids,
                                          const int* __restrict__ counts, int request, int ept,
-                                         int page_size, T* __restrict__ key_pool,
+                                         int hd, int hdp, int page_size, T* __restrict__ key_pool,
                                          T* __restrict__ value_pool,
                                          T* __restrict__ summaries,
                                          int* __restrict__ token_counts,
@@ -1770,11 +1777,17 @@ __global__ void prefill_synthetic_kernel(const int* __restrict__ page_ids,
   xr = combine_hash(xr, request, 0x85ebca6bu);
   xr = combine_hash(xr, i, 0xc2b2ae35u);
   for (int e = threadIdx.x; e < ept; e += blockDim.x) {
+    const int el = logical_element(e, hd, hdp);   // -1: padding
     float sum = 0.0f;
 #pragma unroll 4
     for (int t = 0; t < n; ++t) {
+      if (el < 0) {
+        Kv<T>::put(key_pool, (size_t(page) * page_size + t) * ept + e, 0.0f);
+        Kv<T>::put(value_pool, (size_t(page) * page_size + t) * ept + e, 0.0f);
+        continue;
+      }
       uint32_t x = combine_hash(xr, t, 0x27d4eb2fu);
-      x = combine_hash(x, e, 0x165667b1u);
+      x = combine_hash(x, el, 0x165667b1u);
       const float k = Kv<T>::round(hash_to_unit_lut(combine_hash(x, 1, 0xd3a2646cu), lut));
       const float v = hash_to_unit_lut(combine_hash(x, 2, 0xd3a2646cu), lut);
       Kv<T>::put(key_pool, (size_t(page) * page_size + t) * ept + e, k);
@@ -1796,7 +1809,8 @@ __global__ void append_synthetic_kernel(const int* __restrict__ group_page,
                                         const int* __restrict__ token_first,
                                         const int* __restrict__ token_offset,
                                         const int* __restrict__ reqs, const int* __restrict__ steps,
-                                        int ept, int page_size, T* __restrict__ key_pool,
+                                        int ept, int hd, int hdp, int page_size,
+                                        T* __restrict__ key_pool,
                                         T* __restrict__ value_pool,
                                         T* __restrict__ summaries,
                                         int* __restrict__ token_counts,
@@ -1811,10 +1825,11 @@ __global__ void append_synthetic_kernel(const int* __restrict__ group_page,
     const float old_c = static_cast<float>(off);
     const float new_c = __fadd_rn(old_c, 1.0f);
     for (int e = threadIdx.x; e < ept; e += blockDim.x) {
-      const float k = Kv<T>::round(decode_value(reqs[i], steps[i], e, 1));
+      const int el = logical_element(e, hd, hdp);   // -1: padding (stays zero)
+      const float k = el < 0 ? 0.0f : Kv<T>::round(decode_value(reqs[i], steps[i], el, 1));
       Kv<T>::put(key_pool, (size_t(page) * page_size + off) * ept + e, k);
       Kv<T>::put(value_pool, (size_t(page) * page_size + off) * ept + e,
-                 decode_value(reqs[i], steps[i], e, 2));
+                 el < 0 ? 0.0f : decode_value(reqs[i], steps[i], el, 2));
       const size_t so = sbase + size_t(e / scw) * 128 * scw + (e % scw);
       const float s = off == 0 ? 0.0f : Kv<T>::get(summaries, so);
       Kv<T>::put(summaries, so, __fdiv_rn(__fadd_rn(__fmul_rn(s, old_c), k), new_c));
@@ -1859,8 +1874,8 @@ template <typename T>
 __global__ void generate_normal_kernel(const int* __restrict__ page_ids,
                                        const int* __restrict__ counts,
                                        const int* __restrict__ reqs,
-                                       const int* __restrict__ first_token, int ept,
-                                       int page_size, uint64_t kmix, uint64_t vmix,
+                                       const int* __restrict__ first_token, int ept, int hd,
+                                       int hdp, int page_size, uint64_t kmix, uint64_t vmix,
                                        T* __restrict__ key_pool,
                                        T* __restrict__ value_pool,
                                        T* __restrict__ summaries,
@@ -1871,12 +1886,15 @@ __global__ void generate_normal_kernel(const int* __restrict__ page_ids,
   const int page = page_ids[i];
   const int n = counts[i];
   if (e < ept) {
+    const int el = logical_element(e, hd, hdp);   // -1: padding
+    const int lept = ept / hdp * hd;               // the caller's row length
     float sum = 0.0f;
     for (int t = 0; t < n; ++t) {
-      const uint64_t idx = normal_index(reqs[i], first_token[i] + t, ept, e);
-      const float k = Kv<T>::round(normal_value(kmix, idx));
+      const uint64_t idx = normal_index(reqs[i], first_token[i] + t, lept, max(el, 0));
+      const float k = el < 0 ? 0.0f : Kv<T>::round(normal_value(kmix, idx));
       Kv<T>::put(key_pool, (size_t(page) * page_size + t) * ept + e, k);
-      Kv<T>::put(value_pool, (size_t(page) * page_size + t) * ept + e, normal_value(vmix, idx));
+      Kv<T>::put(value_pool, (size_t(page) * page_size + t) * ept + e,
+                 el < 0 ? 0.0f : normal_value(vmix, idx));
       sum = __fadd_rn(sum, k);
     }
     Kv<T>::put(summaries, summary_off(page, e, ept),

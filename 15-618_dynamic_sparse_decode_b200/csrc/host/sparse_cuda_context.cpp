@@ -48,8 +48,16 @@ SparseCudaContext::SparseCudaContext(const PagedKvCache& cache, const ModelConfi
     throw;
   }
   // queries are packed straight into the context's pinned staging and
-  // outputs read from it: no extra host copy per step
-  ThrowIf(dsd_step_host_buffers(ctx_, &host_queries_, &host_outputs_));
+  // outputs read from it: no extra host copy per step.  A head_dim the
+  // device pads (not a power of two >= 4) has no such buffers: rows then go
+  // through host vectors that the C ABI widens and narrows.
+  if (dsd_step_host_buffers(ctx_, &host_queries_, &host_outputs_) != DSD_OK) {
+    const std::size_t rows = static_cast<std::size_t>(std::max(1, max_batch_size));
+    own_queries_.assign(rows * static_cast<std::size_t>(elements_per_token_), 0.0f);
+    own_outputs_.assign(rows * static_cast<std::size_t>(elements_per_token_), 0.0f);
+    host_queries_ = own_queries_.data();
+    host_outputs_ = own_outputs_.data();
+  }
   const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
   pack_pool_.reset(new detail::WorkerPool(static_cast<int>(std::min(4u, hw) - 1)));
 }

@@ -134,6 +134,7 @@ class SparseCudaContext {
   std::vector<const RequestState*> ptr_scratch_;
   float* host_queries_ = nullptr;   // pinned step staging owned by the context
   float* host_outputs_ = nullptr;
+  std::vector<float> own_queries_, own_outputs_;   // used when the device pads head_dim
   std::vector<int> offsets_, ids_, request_ids_, selected_;
   std::vector<float> scores_;
   std::vector<float> finish_outputs_;

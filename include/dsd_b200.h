@@ -12,7 +12,11 @@
  * The C++ drop-in classes in the package (csrc/host) are thin wrappers over
  * this ABI; a C, cgo, JNI or ctypes caller binds it directly.
  *
- * Data layout in HBM (one context = one GPU):
+ * Data layout in HBM (one context = one GPU).  D below is the stored head
+ * width: the caller's head_dim when it is a power of two >= 4, otherwise the
+ * next power of two (at least 4), the extra columns zero.  Every host row an
+ * entry point takes or returns (queries, outputs, keys, values, summaries)
+ * has the caller's num_heads*head_dim elements; the widening is internal.
  *   keys, values  float [capacity_pages][page_size][H*D]   page-major, 16 B aligned rows
  *   summaries     mean key of each page, chunk-major in groups of 128 pages:
  *                 element e of page p at ((p/128*NC + e/CW)*128 + p%128)*CW + e%CW,
@@ -49,7 +53,7 @@ enum { DSD_OUTPUT_NONE = 0, DSD_OUTPUT_OUTPUTS = 1, DSD_OUTPUT_DEBUG = 2 };
 /* ModelConfig (include/dsd/config.h:5-10). */
 typedef struct dsd_model_config {
   int32_t num_heads;
-  int32_t head_dim;     /* power of two in [4, 128] */
+  int32_t head_dim;     /* 1..128 (the reference's range); stored padded to a power of two */
   int32_t page_size;
   int32_t top_k_pages;
 } dsd_model_config;
@@ -106,8 +110,8 @@ int dsd_ctx_destroy(dsd_ctx* ctx);
 #define DSD_KV_F32 0
 #define DSD_KV_BF16 1
 #define DSD_KV_FP8 2   /* fp8 e4m3 (saturating, round to nearest even); head_dim >= 16 */
-/* dsd_ctx_create with an explicit page format (bf16 needs head_dim >= 8,
- * fp8 head_dim >= 16).
+/* dsd_ctx_create with an explicit page format (bf16 needs head_dim > 4,
+ * fp8 head_dim > 8).
  * dsd_ctx_device_pointers then returns the pools as raw storage of that
  * format (cast the float pointers to __nv_bfloat16* for DSD_KV_BF16). */
 int dsd_ctx_create_ex(int device, const dsd_model_config* config, const dsd_ctx_options* options,
@@ -115,7 +119,8 @@ int dsd_ctx_create_ex(int device, const dsd_model_config* config, const dsd_ctx_
 /* The context's DSD_KV_* format, -1 for a null context. */
 int dsd_ctx_kv_format(dsd_ctx* ctx);
 
-/* Device pointers for callers that keep their own data in HBM (bench, tests). */
+/* Device pointers for callers that keep their own data in HBM (bench, tests).
+ * The arrays are in the stored layout above (padded head width D). */
 int dsd_ctx_device_pointers(dsd_ctx* ctx, float** keys, float** values, float** summaries,
                             int32_t** token_counts);
 /* The CUDA stream every call of this context is ordered on (cudaStream_t). */
@@ -123,7 +128,9 @@ void* dsd_ctx_stream(dsd_ctx* ctx);
 /* The context's pinned per-step staging: queries [max_batch][H*D] and outputs
  * [max_batch][H*D].  Passing these pointers as `queries` / `outputs` to
  * dsd_decode_batch / dsd_decode_step skips one host copy each way.  Valid
- * until the context is destroyed; the next step overwrites them. */
+ * until the context is destroyed; the next step overwrites them.  Rows are in
+ * the stored layout, so a context whose head_dim is padded returns DSD_EINVAL
+ * (pass ordinary host rows instead). */
 int dsd_step_host_buffers(dsd_ctx* ctx, float** queries, float** outputs);
 /* Waits until the previous step's upload of the pinned query staging has
  * completed; call before writing the staging while a step is in flight. */
@@ -233,7 +240,9 @@ int dsd_decode_step_end(dsd_ctx* ctx, float* outputs, float* scores, int32_t* se
 
 /* Device-resident variant: bind a request set once, then run steps whose
  * queries and outputs already live in HBM ([batch][H*D] each).  The step is
- * replayed from a CUDA graph; nothing crosses PCIe. */
+ * replayed from a CUDA graph; nothing crosses PCIe.  Device rows are used as
+ * they are, so these two need head_dim a power of two >= 4 (DSD_EINVAL
+ * otherwise). */
 int dsd_bind_requests(dsd_ctx* ctx, const int32_t* request_ids, int batch);
 int dsd_decode_bound(dsd_ctx* ctx, const float* d_queries, float* d_outputs);
 /* Same step from a second graph that also records a CUDA event between the
@@ -268,7 +277,8 @@ int dsd_selftest_bounded_wait(dsd_ctx* ctx, int64_t budget_cycles);
  * selected ids, split-K partials) lives in one static device array of about
  * 20 MiB that every GPU which loads this library keeps until the process
  * exits.  Limits: batch <= 256, total candidates <= 131072, total selected
- * pages (sum of min(k, n_r)) <= 8192, num_heads*head_dim <= 4096, top_k <= 4096;
+ * pages (sum of min(k, n_r)) <= 8192, num_heads*head_dim <= 4096, head_dim a
+ * power of two in [4, 128] (device rows are used as they are), top_k <= 4096;
  * larger sizes are rejected with DSD_EINVAL.
  *   capacity_pages  pages in the pool the device arrays below describe
  *   cand_offsets  HOST array [batch+1] (validated here, copied to the device)

@@ -16,9 +16,15 @@ from oracle import oracle as o
 pytestmark = pytest.mark.gpu
 
 
-def small_ctx(dsd, cap=16, tables=True):
-    return dsd.SparseDecodeContext(4, 16, 8, 3, cap, 4, cap, 12,
+def small_ctx(dsd, cap=16, tables=True, H=4, D=16):
+    return dsd.SparseDecodeContext(H, D, 8, 3, cap, 4, cap, 12,
                                    max_requests=4 if tables else 0, max_pages_per_request=cap)
+
+
+# (H, D): the stored layout; a head_dim that is not a power of two >= 4 is
+# stored padded (5 -> 8, 80 -> 128, 3 -> 4) and must read back unchanged
+HEAD_SHAPES = pytest.mark.parametrize("H,D", [(4, 16), (3, 5), (2, 80), (5, 3)],
+                                      ids=["h4d16", "h3d5_padded", "h2d80_padded", "h5d3_padded"])
 
 
 def decode_checks(dsd, ctx):
@@ -65,9 +71,10 @@ def test_bad_inputs_rejected_before_launch(dsd):
         decode_checks(dsd, ctx)
 
 
-def test_synthetic_prefill_and_append_match_reference_hash(dsd):
-    E, P = 64, 8
-    with small_ctx(dsd) as ctx:
+@HEAD_SHAPES
+def test_synthetic_prefill_and_append_match_reference_hash(dsd, H, D):
+    E, P = H * D, 8
+    with small_ctx(dsd, H=H, D=D) as ctx:
         ctx.prefill_synthetic([5, 6, 7], [8, 8, 3], request_id=11)
         for i, (pid, n) in enumerate([(5, 8), (6, 8), (7, 3)]):
             k, v, s, cnt = ctx.download_page(pid)
@@ -91,9 +98,10 @@ def test_synthetic_prefill_and_append_match_reference_hash(dsd):
         assert cnt8 == 1 and np.array_equal(s8, o.synthetic_decode(11, 2, E, 1))
 
 
-def test_normal_generator_pages_match_oracle(dsd):
-    E, P = 64, 8
-    with small_ctx(dsd) as ctx:
+@HEAD_SHAPES
+def test_normal_generator_pages_match_oracle(dsd, H, D):
+    E, P = H * D, 8
+    with small_ctx(dsd, H=H, D=D) as ctx:
         ctx.generate_normal([3, 4], [8, 5], [2, 2], [0, 8], seed=9)
         for pid, first, n in ((3, 0, 8), (4, 8, 5)):
             k, v, s, cnt = ctx.download_page(pid)
@@ -112,3 +120,27 @@ def test_free_pages_clear_metadata(dsd):
         assert tc[0] == 8 and tc[1] == 0 and live[0] == 1 and live[1] == 0
         _, _, s, _ = ctx.download_page(1)
         assert not s.any()
+
+
+@HEAD_SHAPES
+def test_upload_append_download_round_trip(dsd, H, D):
+    """Rows go in and come back in the caller's layout whatever the stored
+    head width; summaries follow the CPU formulas bit for bit."""
+    E, P = H * D, 8
+    rng = np.random.default_rng(H * 100 + D)
+    k = rng.standard_normal((P + 3, E)).astype(np.float32)
+    v = rng.standard_normal((P + 3, E)).astype(np.float32)
+    with small_ctx(dsd, H=H, D=D) as ctx:
+        ctx.upload_pages([2, 9], [P, 3], k, v)
+        k9, v9, s9, n9 = ctx.download_page(9)
+        assert n9 == 3 and np.array_equal(k9[:3], k[P:]) and np.array_equal(v9[:3], v[P:])
+        assert np.array_equal(s9.view(np.uint32), o.page_summary(k[P:]).view(np.uint32))
+        nk = rng.standard_normal((2, E)).astype(np.float32)
+        nv = rng.standard_normal((2, E)).astype(np.float32)
+        ctx.append_tokens([9, 9], [3, 4], nk, nv)
+        k9, v9, s9, n9 = ctx.download_page(9)
+        assert n9 == 5 and np.array_equal(k9[3:5], nk) and np.array_equal(v9[3:5], nv)
+        summ = o.page_summary(k[P:])
+        for off in (3, 4):
+            summ = o.running_mean_append(summ, nk[off - 3], off)
+        assert np.array_equal(s9.view(np.uint32), summ.view(np.uint32))

@@ -1,8 +1,9 @@
 """Shape and size edges of the CUDA path vs the oracle (GPU).
 
 Covers the kernel variants the config tests do not reach: head_dim 4 and 8
-(1 and 2 float4 per lane), H*D = 8192 (two register slots), page sizes 1, 32
-and 64, a request with more than 8192 candidates (select reads the keys from
+(1 and 2 float4 per lane), H*D = 8192 (two register slots), head_dim that is
+not a power of two (1, 3, 5, 80, 100, 127: stored padded to the next power of
+two, the reference accepts any head_dim in (0, 128]), page sizes 1, 32 and 64, a request with more than 8192 candidates (select reads the keys from
 global memory), k large enough for long bitonic sorts, and batches at the
 1024-request limit.
 """
@@ -32,10 +33,11 @@ def random_batch(rng, H, D, P, k, n_per_req, cap_extra=0, zero_frac=0.0):
     return o.Batch(H, D, P, k, kp, vp, summ, tc, q, offs, ids)
 
 
-def run_and_check(dsd, b, tol=1e-4):
+def run_and_check(dsd, b, tol=1e-4, kv_format=0):
     n = np.diff(b.cand_offsets)
     with dsd.SparseDecodeContext(b.num_heads, b.head_dim, b.page_size, b.top_k, b.capacity,
-                                 b.batch, int(n.sum()), max(1, int(np.minimum(n, b.top_k).sum()))) as ctx:
+                                 b.batch, int(n.sum()), max(1, int(np.minimum(n, b.top_k).sum())),
+                                 kv_format=kv_format) as ctx:
         ctx.upload_pool(b.key_pool, b.value_pool, b.token_counts)
         res = ctx.decode_batch(b.queries, b.cand_offsets, b.cand_ids)
     sel, so, out, scores = o.sparse_decode(b)
@@ -45,8 +47,11 @@ def run_and_check(dsd, b, tol=1e-4):
 
 
 @pytest.mark.parametrize("H,D,P", [(2, 4, 4), (16, 4, 8), (4, 8, 16), (64, 128, 2),
-                                   (8, 64, 32), (4, 32, 64), (3, 16, 1)],
-                         ids=["d4", "d4_h16", "d8", "e8192", "p32", "p64", "p1_h3"])
+                                   (8, 64, 32), (4, 32, 64), (3, 16, 1),
+                                   (3, 1, 4), (5, 3, 8), (4, 5, 4), (2, 80, 8), (4, 100, 16),
+                                   (2, 127, 4), (48, 96, 16)],
+                         ids=["d4", "d4_h16", "d8", "e8192", "p32", "p64", "p1_h3",
+                              "d1", "d3", "d5", "d80", "d100", "d127", "h48_d96"])
 def test_head_and_page_shapes(dsd, H, D, P):
     rng = np.random.default_rng(H * 1000 + D * 10 + P)
     run_and_check(dsd, random_batch(rng, H, D, P, 5, [3, 17, 40, 9]))
@@ -67,3 +72,13 @@ def test_batch_at_the_limit(dsd):
     rng = np.random.default_rng(5)
     n = rng.integers(0, 6, 1024)
     run_and_check(dsd, random_batch(rng, 2, 16, 4, 3, list(n)))
+
+
+@pytest.mark.parametrize("kv_format,H,D", [(1, 4, 5), (1, 2, 80), (2, 3, 12), (2, 2, 100)],
+                         ids=["bf16_d5", "bf16_d80", "fp8_d12", "fp8_d100"])
+def test_padded_head_dim_narrow_pages(dsd, kv_format, H, D):
+    """bf16 / fp8 pages with a padded head width, against the oracle on the
+    rounded values."""
+    rng = np.random.default_rng(kv_format * 1000 + D)
+    b = o.stored_batch(random_batch(rng, H, D, 8, 4, [6, 20, 11]), o.stored_round(kv_format))
+    run_and_check(dsd, b, kv_format=kv_format)
