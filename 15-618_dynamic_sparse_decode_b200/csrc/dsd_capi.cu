@@ -1042,8 +1042,11 @@ int dsd_ctx_create_ex(int device, const dsd_model_config* config, const dsd_ctx_
     dsd_model_config cfg = *config;
     const dsd_ctx_options opt = *options;
     const int user_d = cfg.head_dim;
-    if (cfg.num_heads <= 0 || user_d < 1 || user_d > 128)
-      Fail(DSD_EINVAL, "head_dim must be in [1, 128] and num_heads positive");
+    // the reference accepts head_dim in (0, 128] for the sparse path and
+    // (0, 256] for its dense baseline (src/cuda/kernels.cu:42-43); both use
+    // this context
+    if (cfg.num_heads <= 0 || user_d < 1 || user_d > 256)
+      Fail(DSD_EINVAL, "head_dim must be in [1, 256] and num_heads positive");
     // physical head width: the next power of two, at least 4
     int D = 4;
     while (D < user_d) D *= 2;

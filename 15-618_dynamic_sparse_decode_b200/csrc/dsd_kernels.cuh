@@ -1526,9 +1526,10 @@ __global__ void __launch_bounds__(256) combine_kernel(StepPlan plan,
       for (int d = lane; d < g4; d += 32) out[d] = make_float4(0.f, 0.f, 0.f, 0.f);
       continue;
     }
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    // float4 columns lane and lane + 32 (head_dim <= 256)
+    float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
     float L = 0.f;
-    const bool col = lane < g4;   // head_dim <= 128: one float4 column per lane
+    const bool col[2] = {lane < g4, lane + 32 < g4};
     for (int c0 = u0; c0 < u1; c0 += 32) {
       float w = 0.f;
       if (c0 == u0) {
@@ -1542,32 +1543,42 @@ __global__ void __launch_bounds__(256) combine_kernel(StepPlan plan,
       }
       const int nu = min(32, u1 - c0);
       const float* base = part_acc + size_t(c0) * ept + size_t(h) * head_dim + 4 * lane;
-      int i = 0;
-      for (; i + 4 <= nu; i += 4) {
-        float4 a[4];
+      for (int cc = 0; cc < 2; ++cc) {
+        if (!__any_sync(0xffffffffu, col[cc])) break;   // the same g4 on every lane
+        const float* cb = base + 128 * cc;
+        int i = 0;
+        for (; i + 4 <= nu; i += 4) {
+          float4 a[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          a[k] = col ? *reinterpret_cast<const float4*>(base + size_t(i + k) * ept)
-                     : make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int k = 0; k < 4; ++k)
+            a[k] = col[cc] ? *reinterpret_cast<const float4*>(cb + size_t(i + k) * ept)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float wk = __shfl_sync(0xffffffffu, w, i + k);
-          acc.x += wk * a[k].x; acc.y += wk * a[k].y; acc.z += wk * a[k].z; acc.w += wk * a[k].w;
+          for (int k = 0; k < 4; ++k) {
+            const float wk = __shfl_sync(0xffffffffu, w, i + k);
+            acc[cc].x += wk * a[k].x; acc[cc].y += wk * a[k].y;
+            acc[cc].z += wk * a[k].z; acc[cc].w += wk * a[k].w;
+          }
         }
-      }
-      for (; i < nu; ++i) {
-        const float4 a = col ? *reinterpret_cast<const float4*>(base + size_t(i) * ept)
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
-        const float wk = __shfl_sync(0xffffffffu, w, i);
-        acc.x += wk * a.x; acc.y += wk * a.y; acc.z += wk * a.z; acc.w += wk * a.w;
+        for (; i < nu; ++i) {
+          const float4 a = col[cc] ? *reinterpret_cast<const float4*>(cb + size_t(i) * ept)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float wk = __shfl_sync(0xffffffffu, w, i);
+          acc[cc].x += wk * a.x; acc[cc].y += wk * a.y; acc[cc].z += wk * a.z;
+          acc[cc].w += wk * a.w;
+        }
       }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
     const float inv = L > 0.f ? 1.0f / L : 0.0f;
-    if (col)
-      out[lane] = L > 0.f ? make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv)
-                          : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc)
+      if (col[cc])
+        out[lane + 32 * cc] =
+            L > 0.f ? make_float4(acc[cc].x * inv, acc[cc].y * inv, acc[cc].z * inv,
+                                  acc[cc].w * inv)
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
   }
 }
 

@@ -53,7 +53,8 @@ enum { DSD_OUTPUT_NONE = 0, DSD_OUTPUT_OUTPUTS = 1, DSD_OUTPUT_DEBUG = 2 };
 /* ModelConfig (include/dsd/config.h:5-10). */
 typedef struct dsd_model_config {
   int32_t num_heads;
-  int32_t head_dim;     /* 1..128 (the reference's range); stored padded to a power of two */
+  int32_t head_dim;     /* 1..256 (the reference: sparse 1..128, dense 1..256); stored
+                           padded to a power of two */
   int32_t page_size;
   int32_t top_k_pages;
 } dsd_model_config;

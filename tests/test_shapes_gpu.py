@@ -2,8 +2,9 @@
 
 Covers the kernel variants the config tests do not reach: head_dim 4 and 8
 (1 and 2 float4 per lane), H*D = 8192 (two register slots), head_dim that is
-not a power of two (1, 3, 5, 80, 100, 127: stored padded to the next power of
-two, the reference accepts any head_dim in (0, 128]), page sizes 1, 32 and 64, a request with more than 8192 candidates (select reads the keys from
+not a power of two (1, 3, 5, 80, 100, 127, 200: stored padded to the next
+power of two; the reference accepts any head_dim in (0, 128], and up to 256 on
+its dense path), head_dim 256, page sizes 1, 32 and 64, a request with more than 8192 candidates (select reads the keys from
 global memory), k large enough for long bitonic sorts, and batches at the
 1024-request limit.
 """
@@ -49,9 +50,11 @@ def run_and_check(dsd, b, tol=1e-4, kv_format=0):
 @pytest.mark.parametrize("H,D,P", [(2, 4, 4), (16, 4, 8), (4, 8, 16), (64, 128, 2),
                                    (8, 64, 32), (4, 32, 64), (3, 16, 1),
                                    (3, 1, 4), (5, 3, 8), (4, 5, 4), (2, 80, 8), (4, 100, 16),
-                                   (2, 127, 4), (48, 96, 16)],
+                                   (2, 127, 4), (48, 96, 16), (4, 256, 8), (3, 200, 4),
+                                   (32, 256, 2)],
                          ids=["d4", "d4_h16", "d8", "e8192", "p32", "p64", "p1_h3",
-                              "d1", "d3", "d5", "d80", "d100", "d127", "h48_d96"])
+                              "d1", "d3", "d5", "d80", "d100", "d127", "h48_d96", "d256",
+                              "d200", "d256_e8192"])
 def test_head_and_page_shapes(dsd, H, D, P):
     rng = np.random.default_rng(H * 1000 + D * 10 + P)
     run_and_check(dsd, random_batch(rng, H, D, P, 5, [3, 17, 40, 9]))
@@ -74,8 +77,10 @@ def test_batch_at_the_limit(dsd):
     run_and_check(dsd, random_batch(rng, 2, 16, 4, 3, list(n)))
 
 
-@pytest.mark.parametrize("kv_format,H,D", [(1, 4, 5), (1, 2, 80), (2, 3, 12), (2, 2, 100)],
-                         ids=["bf16_d5", "bf16_d80", "fp8_d12", "fp8_d100"])
+@pytest.mark.parametrize("kv_format,H,D", [(1, 4, 5), (1, 2, 80), (2, 3, 12), (2, 2, 100),
+                                           (1, 4, 256), (2, 2, 256)],
+                         ids=["bf16_d5", "bf16_d80", "fp8_d12", "fp8_d100", "bf16_d256",
+                              "fp8_d256"])
 def test_padded_head_dim_narrow_pages(dsd, kv_format, H, D):
     """bf16 / fp8 pages with a padded head width, against the oracle on the
     rounded values."""

@@ -240,10 +240,13 @@ def test_pinned_host_buffers_match_pageable(dsd, orc):
         check_against_oracle(orc, b, res, 1e-4)
 
 
-# tests/test_dense_cuda.cpp:21-156: dense_gpu vs dense_cpu on five shapes
-DENSE_CASES = [((2, 8, 4, 4, 3, 5, 19, 11), 1e-5), ((4, 16, 16, 4, 4, 33, 97, 7), 2e-5),
-               ((2, 64, 8, 4, 2, 17, 45, 17), 5e-5), ((8, 32, 16, 4, 3, 100, 300, 5), 5e-5),
-               ((32, 128, 16, 8, 4, 256, 1024, 7), 1e-4)]
+# tests/test_dense_cuda.cpp:96-156: dense_gpu vs dense_cpu on the reference's
+# five shapes (head_dim 80 is stored padded to 128), plus config-3 width and
+# head_dim 256 (the top of the reference dense path's range)
+DENSE_CASES = [((2, 8, 4, 8, 3, 5, 19, 11), 1e-5), ((4, 16, 16, 8, 5, 33, 97, 7), 2e-5),
+               ((2, 64, 8, 16, 4, 17, 45, 17), 5e-5), ((2, 80, 8, 16, 4, 17, 45, 19), 5e-5),
+               ((2, 128, 8, 16, 2, 9, 25, 29), 1e-4), ((32, 128, 16, 8, 4, 256, 1024, 7), 1e-4),
+               ((2, 256, 8, 16, 2, 9, 25, 3), 1e-4)]
 
 
 @pytest.mark.parametrize("cfg,tol", DENSE_CASES, ids=[f"dense{i}" for i in range(len(DENSE_CASES))])
