@@ -642,19 +642,28 @@ __device__ __forceinline__ void widen16(const uint4 raw, const __nv_bfloat16*, f
   }
 }
 
-// two fp8 e4m3 (low byte first) -> float2, exact (through half)
-__device__ __forceinline__ float2 fp8x2_to_float2(uint32_t pair) {
-  const __half2_raw hr =
-      __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(pair & 0xffffu), __NV_E4M3);
-  return __half22float2(*reinterpret_cast<const __half2*>(&hr));
+// fp8 e4m3 widening by integer bit moves (no conversion instructions: the
+// hardware fp8/half conversions issue on the narrow transcendental/conversion
+// pipe, which bounded both fp8 kernels).  An e4m3 byte is s eeee mmm with
+// exponent bias 7; fp32 has bias 127.  Moving the sign to bit 31 and the
+// seven eeee mmm bits to bits 26..20 gives the fp32 whose value is exactly
+// 2^-120 times the e4m3 value, for every code: normals (exponent e + 120 in
+// fp32) as well as zero and the e4m3 subnormals (0.mmm * 2^-6, which land
+// on fp32 subnormals 0.mmm * 2^-126).  Callers apply the 2^120 once: the
+// score kernel per element with an exact multiply, the attention kernel in
+// its logit scale and its output write.  Codes 0x7f / 0xff (NaN in e4m3fn)
+// are never stored: the pools saturate to +-448.
+constexpr float kE4m3Unscale = 1.329227995784916e36f;   // 2^120
+__device__ __forceinline__ float e4m3_scaled(uint32_t w, int i) {
+  const int32_t top = static_cast<int32_t>(w << (24 - 8 * i));   // byte i in bits 31..24
+  return __int_as_float((top >> 4) & static_cast<int32_t>(0x87F00000u));
 }
 __device__ __forceinline__ void widen16(const uint4 raw, const __nv_fp8_e4m3*, float (&f)[16]) {
   const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-  for (int h = 0; h < 4; ++h) {
-    const float2 lo = fp8x2_to_float2(w[h]), hi = fp8x2_to_float2(w[h] >> 16);
-    f[4 * h] = lo.x; f[4 * h + 1] = lo.y; f[4 * h + 2] = hi.x; f[4 * h + 3] = hi.y;
-  }
+  for (int h = 0; h < 4; ++h)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) f[4 * h + i] = __fmul_rn(e4m3_scaled(w[h], i), kE4m3Unscale);
 }
 
 template <typename T, int STAGES, int MINB>
@@ -1219,13 +1228,20 @@ __device__ __forceinline__ void unpack16(const uint4 raw, const __nv_bfloat16*, 
   for (int h = 0; h < 4; ++h)
     f[h] = make_float2(__uint_as_float(w[h] << 16), __uint_as_float(w[h] & 0xffff0000u));
 }
+// fp8: the pairs come out scaled by 2^-120 (e4m3_scaled); the attention
+// kernel folds the 2^120 into its logit scale and its partial outputs.
 __device__ __forceinline__ void unpack16(const uint4 raw, const __nv_fp8_e4m3*, float2 (&f)[8]) {
   const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
   for (int h = 0; h < 4; ++h) {
-    f[2 * h] = fp8x2_to_float2(w[h]);
-    f[2 * h + 1] = fp8x2_to_float2(w[h] >> 16);
+    f[2 * h] = make_float2(e4m3_scaled(w[h], 0), e4m3_scaled(w[h], 1));
+    f[2 * h + 1] = make_float2(e4m3_scaled(w[h], 2), e4m3_scaled(w[h], 3));
   }
+}
+// the factor unpack16 leaves on its values (1 for bf16)
+template <typename T>
+__device__ __forceinline__ constexpr float unpack_unscale() {
+  return sizeof(T) == 1 ? kE4m3Unscale : 1.0f;
 }
 
 // The narrow-page attention keeps its softmax in base 2: logits are scaled by
@@ -1267,7 +1283,7 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_narrow(
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
-  const float scale_log2 = scale * kLog2e;
+  const float scale_log2 = scale * kLog2e * unpack_unscale<T>();   // K values come scaled
   if (tid == 0) {
     for (int s = 0; s < nstages; ++s) {
       mbar_init(&full[s], 1);
@@ -1465,13 +1481,14 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_narrow(
     for (int m = 0; m < SLOTS; ++m) {
       if (!ok[m]) continue;
       float4* pa = reinterpret_cast<float4*>(part_acc + size_t(u) * ept);
+      constexpr float us = unpack_unscale<T>();   // V values came scaled
 #pragma unroll
       for (int j = 0; j < NV; ++j) {
 #pragma unroll
         for (int h = 0; h < VE / 4; ++h)
-          pa[(VE / 4) * colv[m][j] + h] = make_float4(acc[m][j][2 * h].x, acc[m][j][2 * h].y,
-                                                      acc[m][j][2 * h + 1].x,
-                                                      acc[m][j][2 * h + 1].y);
+          pa[(VE / 4) * colv[m][j] + h] =
+              make_float4(acc[m][j][2 * h].x * us, acc[m][j][2 * h].y * us,
+                          acc[m][j][2 * h + 1].x * us, acc[m][j][2 * h + 1].y * us);
       }
       const int item = tid + kAttnThreads * m;
       if (item % LP == 0) {

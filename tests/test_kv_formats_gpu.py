@@ -163,3 +163,32 @@ def test_continuous_cli_serves_the_same_tokens(admission):
         assert r["kv_format"] == name
         assert int(r["total_generated_tokens"]) == int(f32["total_generated_tokens"])
         assert float(r["continuous_sparse_tokens_per_second"]) > 0
+
+
+def test_fp8_every_code_widens_exactly(dsd):
+    """Every finite e4m3 code (the 126 positive and 126 negative normals and
+    subnormals, and +-0) appears in the keys and values of a page set; the
+    device widens them by integer bit moves (no conversion instructions), so
+    scores must equal the oracle's bit for bit and outputs within 1e-4."""
+    import torch
+    codes = np.array([c for c in range(256) if c & 0x7F != 0x7F], np.uint8)
+    vals = torch.from_numpy(codes).view(torch.float8_e4m3fn).float().numpy()
+    H, D, P = 2, 16, 8
+    E = H * D
+    rng = np.random.default_rng(8)
+    cap = 12
+    flat_k = np.resize(rng.permutation(vals), cap * P * E).astype(np.float32)
+    flat_v = np.resize(rng.permutation(vals), cap * P * E).astype(np.float32)
+    kp = flat_k.reshape(cap, P, E)
+    vp = flat_v.reshape(cap, P, E) / np.float32(64.0)   # keep the softmax outputs moderate
+    tc = np.full(cap, P, np.int32)
+    summ = np.stack([o.page_summary(kp[p]) for p in range(cap)])
+    q = rng.standard_normal((3, E)).astype(np.float32) * np.float32(0.05)
+    offs = np.array([0, 4, 9, 12], np.int32)
+    ids = rng.permutation(cap).astype(np.int32)
+    b = o.Batch(H, D, P, 3, kp, vp, summ, tc, q, offs, ids)
+    ref = o.stored_batch(b, o.stored_round(2))
+    assert np.array_equal(ref.key_pool, kp)          # every key is an exact e4m3 value
+    with narrow_ctx(dsd, b, 2) as ctx:
+        ctx.upload_pool(kp, vp, tc)
+        check(ctx.decode_batch(q, offs, ids), ref)
