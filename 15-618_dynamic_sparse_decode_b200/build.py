@@ -32,17 +32,19 @@ def _newer(target: str, deps: list[str]) -> bool:
     return all(os.path.getmtime(d) <= t for d in deps)
 
 
-def build_library(force: bool = False, verbose: bool = False) -> str:
+def build_library(force: bool = False, verbose: bool = False, out: str = LIB,
+                  defines: tuple = ()) -> str:
     deps = [os.path.join(CSRC, s) for s in SOURCES + HEADERS] + [os.path.join(INCLUDE, "dsd_b200.h")]
-    if not force and _newer(LIB, deps):
-        return LIB
+    if not force and _newer(out, deps):
+        return out
     cmd = [NVCC, *ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
-           f"-I{INCLUDE}", f"-I{CSRC}", "-o", LIB, *[os.path.join(CSRC, s) for s in SOURCES]]
+           *[f"-D{d}" for d in defines],
+           f"-I{INCLUDE}", f"-I{CSRC}", "-o", out, *[os.path.join(CSRC, s) for s in SOURCES]]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)
-    return LIB
+    return out
 
 
 HOST_DIR = os.path.join(CSRC, "host")
