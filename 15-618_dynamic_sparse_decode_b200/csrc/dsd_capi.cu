@@ -289,7 +289,6 @@ struct dsd_ctx {
   // the graph)
   cudaStream_t copy_stream = nullptr;
   cudaEvent_t ev_part0_up = nullptr, ev_q1 = nullptr, ev_out0 = nullptr, ev_out0_done = nullptr;
-  cudaEvent_t ev_q2 = nullptr, ev_out1 = nullptr;   // third range of a split-I/O step
   // steps queued with dsd_decode_step_begin use per-slot device input/output
   // buffers (slot 0: d_in / d_outputs / plan, slot 1: d_in1 / d_outputs1 /
   // plan1): a slot's upload and result copies run on copy_stream, so they
@@ -593,14 +592,9 @@ void RecordEvent(dsd_ctx* c, int i, bool capturing) {
 // One decode step.  Untimed steps split the requests into kStepParts ranges
 // whose kernel chains run on two streams (fork/join inside the captured
 // graph), so one part's small kernels and kernel tails overlap the other
-// part's bandwidth-bound kernels.  Host-facing steps whose copies are split
-// (split_io) use three ranges -- B/8, the middle, B/8 (part_range) -- with
-// the outer two on the context stream: only the first range's queries and the
-// last range's outputs cross PCIe outside the kernels; the middle range's
-// copies overlap the outer ranges' kernels.  Timed steps run one chain with an
-// event between the stages.
+// part's bandwidth-bound kernels.  Timed steps run one chain with an event
+// between the stages.
 constexpr int kStepParts = 2;
-constexpr int kSplitIoParts = 3;
 
 void LaunchStep(dsd_ctx* c, const dsdk::StepPlan& plan, const float* d_q, float* d_out,
                 bool timed, bool capturing = false, bool split_io = false) {
@@ -609,7 +603,7 @@ void LaunchStep(dsd_ctx* c, const dsdk::StepPlan& plan, const float* d_q, float*
   const int sel_grid = std::max(1, std::min(c->opt.max_batch, 2 * c->num_sms));
   const int pairs = c->opt.max_batch * H;
   const int comb_grid = std::max(1, std::min((pairs + 7) / 8, 8 * c->num_sms));
-  const int nparts = timed ? 1 : split_io ? kSplitIoParts : kStepParts;
+  const int nparts = timed ? 1 : kStepParts;
   if (timed) RecordEvent(c, 0, capturing);
   NvtxRange nvtx_step("dsd.step");
   const int score_ctas =
@@ -627,12 +621,8 @@ void LaunchStep(dsd_ctx* c, const dsdk::StepPlan& plan, const float* d_q, float*
       Check(cudaStreamWaitEvent(c->stream2, c->ev_q1, cudaEventWaitExternal), "query wait");
   }
   for (int part = 0; part < nparts; ++part) {
-    cudaStream_t st = part == 1 ? c->stream2 : c->stream;
-    NvtxRange nvtx_part(part == 0 ? "dsd.step.range0" : part == 1 ? "dsd.step.range1"
-                                                                   : "dsd.step.range2");
-    // the third range's queries arrive on copy_stream after the second's
-    if (split_io && capturing && part == 2)
-      Check(cudaStreamWaitEvent(c->stream, c->ev_q2, cudaEventWaitExternal), "query wait");
+    cudaStream_t st = part == 0 ? c->stream : c->stream2;
+    NvtxRange nvtx_part(part == 0 ? "dsd.step.range0" : "dsd.step.range1");
     nvtxRangePushA("dsd.score");
     if (c->kv_format == DSD_KV_F32) {
       dsdk::score_kernel<<<2 * c->num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, st>>>(
@@ -671,9 +661,9 @@ void LaunchStep(dsd_ctx* c, const dsdk::StepPlan& plan, const float* d_q, float*
     dsdk::combine_kernel<<<comb_grid, 256, 0, st>>>(plan, c->d_part_acc, c->d_part_ml, H, D,
                                                     d_out, part, nparts);
     nvtxRangePop();
-    if (split_io && capturing && part < 2)
-      Check(cudaEventRecordWithFlags(part == 0 ? c->ev_out0 : c->ev_out1, st,
-                                     cudaEventRecordExternal), "part output event");
+    if (split_io && capturing && nparts > 1 && part == 0)
+      Check(cudaEventRecordWithFlags(c->ev_out0, c->stream, cudaEventRecordExternal),
+            "part output event");
   }
   if (nparts > 1) {
     Check(cudaEventRecord(c->ev_join, c->stream2), "join");
@@ -756,14 +746,10 @@ void UploadQueries(dsd_ctx* c, const float* queries, int batch) {
 }
 
 // Untimed page-table steps of at least two requests split their host I/O.
-bool SplitIo(int batch, int timing) { return timing == 0 && batch >= 2; }
+bool SplitIo(int batch, int timing) { return timing == 0 && batch >= kStepParts; }
 
-// First request of range `part` of a split-I/O step (part_range, as the kernels see it).
-int SplitRow(int batch, int part) {
-  int r0 = 0, r1 = 0;
-  dsdk::part_range(batch, part, kSplitIoParts, &r0, &r1);
-  return r0;
-}
+// First request of the second range of a split step (part_range on the device).
+int SplitRow(int batch) { return int((long long)batch * 1 / kStepParts); }
 
 // UploadQueries for a page-table step whose host I/O is split: the header,
 // request list and the first range's queries go up on the context stream,
@@ -772,31 +758,26 @@ int SplitRow(int batch, int part) {
 // waits for before the second range's kernels.
 void UploadQueriesSplit(dsd_ctx* c, const float* queries, int batch) {
   const size_t row = size_t(c->ept) * 4;
-  const int h1 = SplitRow(batch, 1), h2 = SplitRow(batch, 2);
+  const int h0 = SplitRow(batch);
   const bool direct = !c->padded && queries != QPtr(c) && IsPinnedHost(queries);
   if (!direct && queries != QPtr(c)) PadRowsInto(c, QPtr(c), queries, size_t(batch));
-  const unsigned char* src =
-      direct ? reinterpret_cast<const unsigned char*>(queries) : c->h_in + c->in_q_off;
+  const unsigned char* src1 =
+      direct ? reinterpret_cast<const unsigned char*>(queries) + size_t(h0) * row
+             : c->h_in + c->in_q_off + size_t(h0) * row;
   if (direct) {
     H2D(c, c->d_in, c->h_in, c->in_q_off);
-    H2D(c, c->d_in + c->in_q_off, queries, size_t(h1) * row);
+    H2D(c, c->d_in + c->in_q_off, queries, size_t(h0) * row);
   } else {
-    H2D(c, c->d_in, c->h_in, c->in_q_off + size_t(h1) * row);
+    H2D(c, c->d_in, c->h_in, c->in_q_off + size_t(h0) * row);
   }
   Check(cudaEventRecord(c->ev_part0_up, c->stream), "event record");
   Check(cudaStreamWaitEvent(c->copy_stream, c->ev_part0_up, 0), "copy stream wait");
-  // the middle range, then the last, each completing the event its chain waits for
-  const int rows[2][2] = {{h1, h2}, {h2, batch}};
-  for (int k = 0; k < 2; ++k) {
-    const size_t off = size_t(rows[k][0]) * row, bytes = size_t(rows[k][1] - rows[k][0]) * row;
-    if (bytes) {
-      Check(cudaMemcpyAsync(c->d_in + c->in_q_off + off, src + off, bytes,
-                            cudaMemcpyHostToDevice, c->copy_stream), "H2D copy");
-      CountH2D(c, bytes);
-    }
-    Check(cudaEventRecord(k == 0 ? c->ev_q1 : c->ev_q2, c->copy_stream), "event record");
-  }
-  // the pinned staging is free again once every upload is done
+  Check(cudaMemcpyAsync(c->d_in + c->in_q_off + size_t(h0) * row, src1,
+                        size_t(batch - h0) * row, cudaMemcpyHostToDevice, c->copy_stream),
+        "H2D copy");
+  CountH2D(c, size_t(batch - h0) * row);
+  Check(cudaEventRecord(c->ev_q1, c->copy_stream), "event record");
+  // the pinned staging is free again once both uploads are done
   Check(cudaEventRecord(c->ev_inputs, c->copy_stream), "event record");
 }
 
@@ -805,24 +786,15 @@ void UploadQueriesSplit(dsd_ctx* c, const float* queries, int batch) {
 // second range's on the context stream, which then waits for the first.
 void CopyOutputsSplit(dsd_ctx* c, float* h_out, int batch) {
   const size_t row = size_t(c->ept) * 4;
-  const int h1 = SplitRow(batch, 1), h2 = SplitRow(batch, 2);
-  auto* dst = reinterpret_cast<unsigned char*>(h_out);
-  const auto* src = reinterpret_cast<const unsigned char*>(c->d_outputs);
-  // the first and the middle range come back on copy_stream as their chains finish
-  const int rows[2][2] = {{0, h1}, {h1, h2}};
-  for (int k = 0; k < 2; ++k) {
-    const size_t off = size_t(rows[k][0]) * row, bytes = size_t(rows[k][1] - rows[k][0]) * row;
-    Check(cudaStreamWaitEvent(c->copy_stream, k == 0 ? c->ev_out0 : c->ev_out1, 0),
-          "copy stream wait");
-    if (bytes) {
-      Check(cudaMemcpyAsync(dst + off, src + off, bytes, cudaMemcpyDeviceToHost,
-                            c->copy_stream), "D2H copy");
-      CountD2H(c, bytes);
-    }
-  }
+  const int h0 = SplitRow(batch);
+  Check(cudaStreamWaitEvent(c->copy_stream, c->ev_out0, 0), "copy stream wait");
+  Check(cudaMemcpyAsync(h_out, c->d_outputs, size_t(h0) * row, cudaMemcpyDeviceToHost,
+                        c->copy_stream), "D2H copy");
   Check(cudaEventRecord(c->ev_out0_done, c->copy_stream), "event record");
-  // the last range on the context stream, after the graph
-  D2H(c, dst + size_t(h2) * row, src + size_t(h2) * row, size_t(batch - h2) * row);
+  D2H(c, reinterpret_cast<unsigned char*>(h_out) + size_t(h0) * row,
+      reinterpret_cast<const unsigned char*>(c->d_outputs) + size_t(h0) * row,
+      size_t(batch - h0) * row);
+  CountD2H(c, size_t(h0) * row);
   Check(cudaStreamWaitEvent(c->stream, c->ev_out0_done, 0), "output join");
 }
 
@@ -1123,7 +1095,6 @@ int dsd_ctx_create_ex(int device, const dsd_model_config* config, const dsd_ctx_
       Check(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking), "stream");
       Check(cudaStreamCreateWithFlags(&c->up_stream, cudaStreamNonBlocking), "stream");
       for (cudaEvent_t* e : {&c->ev_part0_up, &c->ev_q1, &c->ev_out0, &c->ev_out0_done,
-                             &c->ev_q2, &c->ev_out1,
                              &c->ev_in_ready[0], &c->ev_in_ready[1], &c->ev_graph_done[0],
                              &c->ev_graph_done[1], &c->ev_out_read[0], &c->ev_out_read[1]})
         Check(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "event");
@@ -1261,8 +1232,7 @@ int dsd_ctx_destroy(dsd_ctx* c) {
   if (c->ev_inputs) cudaEventDestroy(c->ev_inputs);
   if (c->ev_fork) cudaEventDestroy(c->ev_fork);
   if (c->ev_join) cudaEventDestroy(c->ev_join);
-  for (cudaEvent_t e : {c->ev_part0_up, c->ev_q1, c->ev_out0, c->ev_out0_done, c->ev_q2,
-                        c->ev_out1, c->ev_in_ready[0],
+  for (cudaEvent_t e : {c->ev_part0_up, c->ev_q1, c->ev_out0, c->ev_out0_done, c->ev_in_ready[0],
                         c->ev_in_ready[1], c->ev_graph_done[0], c->ev_graph_done[1],
                         c->ev_out_read[0], c->ev_out_read[1]})
     if (e) cudaEventDestroy(e);

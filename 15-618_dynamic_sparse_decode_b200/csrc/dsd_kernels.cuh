@@ -300,19 +300,7 @@ __host__ __device__ __forceinline__ size_t summary_off(int page, int e, int ept)
 
 // Requests [r0, r1) of part `part` of `nparts` (a step may be split into
 // request ranges that run on different streams).
-// Request range [r0, r1) of part `part` of a step split into nparts chains.
-// nparts 1 and 2: equal ranges.  nparts 3 (host-facing steps whose copies
-// are split): B/8, B - 2*(B/8), B/8 -- only the first range's queries and the
-// last range's outputs cross PCIe outside the kernels, so those two are small.
-// Used by the kernels and by the host code that splits the copies.
-__host__ __device__ __forceinline__ void part_range(int B, int part, int nparts, int* r0,
-                                                    int* r1) {
-  if (nparts == 3) {
-    const int e = B / 8;
-    *r0 = part == 0 ? 0 : part == 1 ? e : B - e;
-    *r1 = part == 0 ? e : part == 1 ? B - e : B;
-    return;
-  }
+__device__ __forceinline__ void part_range(int B, int part, int nparts, int* r0, int* r1) {
   *r0 = static_cast<int>(static_cast<long long>(B) * part / nparts);
   *r1 = static_cast<int>(static_cast<long long>(B) * (part + 1) / nparts);
 }
