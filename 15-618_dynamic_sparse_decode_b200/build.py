@@ -34,6 +34,7 @@ def _newer(target: str, deps: list[str]) -> bool:
 
 def build_library(force: bool = False, verbose: bool = False, out: str = LIB,
                   defines: tuple = ()) -> str:
+    """nvcc the C ABI + kernels into `out` (extra -D `defines` for experiments)."""
     deps = [os.path.join(CSRC, s) for s in SOURCES + HEADERS] + [os.path.join(INCLUDE, "dsd_b200.h")]
     if not force and _newer(out, deps):
         return out

@@ -642,36 +642,11 @@ __device__ __forceinline__ void widen16(const uint4 raw, const __nv_bfloat16*, f
   }
 }
 
-// fp8 e4m3 widening by integer bit moves (no conversion instructions: the
-// hardware fp8/half conversions issue on the narrow transcendental/conversion
-// pipe, which bounded both fp8 kernels).  An e4m3 byte is s eeee mmm with
-// exponent bias 7; fp32 has bias 127.  Moving the sign to bit 31 and the
-// seven eeee mmm bits to bits 26..20 gives the fp32 whose value is exactly
-// 2^-120 times the e4m3 value, for every code: normals (exponent e + 120 in
-// fp32) as well as zero and the e4m3 subnormals (0.mmm * 2^-6, which land
-// on fp32 subnormals 0.mmm * 2^-126).  Callers apply the 2^120 once: the
-// score kernel per element with an exact multiply, the attention kernel in
-// its logit scale and its output write.  Codes 0x7f / 0xff (NaN in e4m3fn)
-// are never stored: the pools saturate to +-448.
-constexpr float kE4m3Unscale = 1.329227995784916e36f;   // 2^120
-__device__ __forceinline__ float e4m3_scaled(uint32_t w, int i) {
-  const int32_t top = static_cast<int32_t>(w << (24 - 8 * i));   // byte i in bits 31..24
-  return __int_as_float((top >> 4) & static_cast<int32_t>(0x87F00000u));
-}
-// Which fp8 widening each consumer uses: 0 = the hardware conversion
-// (fp8x2 -> half2 -> float2), 1 = the integer bit moves above.  The two load
-// different pipes (conversion pipe vs integer ALU); K and V of the attention
-// kernel and the score kernel choose separately so the load can be split.
-#ifndef DSD_FP8_WIDEN_SCORE
-#define DSD_FP8_WIDEN_SCORE 1
-#endif
-#ifndef DSD_FP8_WIDEN_K
-#define DSD_FP8_WIDEN_K 1
-#endif
-#ifndef DSD_FP8_WIDEN_V
-#define DSD_FP8_WIDEN_V 1
-#endif
-// two fp8 e4m3 (low byte first) -> float2, exact, by the hardware conversion
+// two fp8 e4m3 (low byte first) -> float2, exact (through half).  The
+// conversions issue on the conversion pipe, which bounds both fp8 kernels; an
+// integer widening (bit moves into fp32 position plus a power-of-two rescale)
+// was measured slower on every consumer split (more integer-ALU issue than
+// the conversion pipe saves), so the hardware conversion stays.
 __device__ __forceinline__ float2 fp8x2_to_float2(uint32_t pair) {
   const __half2_raw hr =
       __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(pair & 0xffffu), __NV_E4M3);
@@ -681,13 +656,8 @@ __device__ __forceinline__ void widen16(const uint4 raw, const __nv_fp8_e4m3*, f
   const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
   for (int h = 0; h < 4; ++h) {
-#if DSD_FP8_WIDEN_SCORE
-#pragma unroll
-    for (int i = 0; i < 4; ++i) f[4 * h + i] = __fmul_rn(e4m3_scaled(w[h], i), kE4m3Unscale);
-#else
     const float2 lo = fp8x2_to_float2(w[h]), hi = fp8x2_to_float2(w[h] >> 16);
     f[4 * h] = lo.x; f[4 * h + 1] = lo.y; f[4 * h + 2] = hi.x; f[4 * h + 3] = hi.y;
-#endif
   }
 }
 
@@ -1247,33 +1217,19 @@ __host__ __device__ constexpr int attn_narrow_reg_tokens(int slots) {
 
 // 16 bytes of page elements -> float2 pairs (elements 2h, 2h+1); widening is
 // exact.  bf16: a 16-bit shift / mask; fp8 e4m3: via half (exact).
-template <int INT_WIDEN>
 __device__ __forceinline__ void unpack16(const uint4 raw, const __nv_bfloat16*, float2 (&f)[4]) {
   const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
   for (int h = 0; h < 4; ++h)
     f[h] = make_float2(__uint_as_float(w[h] << 16), __uint_as_float(w[h] & 0xffff0000u));
 }
-// fp8: the pairs come out scaled by 2^-120 (e4m3_scaled); the attention
-// kernel folds the 2^120 into its logit scale and its partial outputs.
-template <int INT_WIDEN>
 __device__ __forceinline__ void unpack16(const uint4 raw, const __nv_fp8_e4m3*, float2 (&f)[8]) {
   const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
   for (int h = 0; h < 4; ++h) {
-    if (INT_WIDEN) {
-      f[2 * h] = make_float2(e4m3_scaled(w[h], 0), e4m3_scaled(w[h], 1));
-      f[2 * h + 1] = make_float2(e4m3_scaled(w[h], 2), e4m3_scaled(w[h], 3));
-    } else {
-      f[2 * h] = fp8x2_to_float2(w[h]);
-      f[2 * h + 1] = fp8x2_to_float2(w[h] >> 16);
-    }
+    f[2 * h] = fp8x2_to_float2(w[h]);
+    f[2 * h + 1] = fp8x2_to_float2(w[h] >> 16);
   }
-}
-// the factor unpack16<INT_WIDEN> leaves on its values (1 for bf16)
-template <typename T, int INT_WIDEN>
-__device__ __forceinline__ constexpr float unpack_unscale() {
-  return sizeof(T) == 1 && INT_WIDEN ? kE4m3Unscale : 1.0f;
 }
 
 // The narrow-page attention keeps its softmax in base 2: logits are scaled by
@@ -1315,8 +1271,7 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_narrow(
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
-  // K values may come scaled (integer widening)
-  const float scale_log2 = scale * kLog2e * unpack_unscale<T, DSD_FP8_WIDEN_K>();
+  const float scale_log2 = scale * kLog2e;
   if (tid == 0) {
     for (int s = 0; s < nstages; ++s) {
       mbar_init(&full[s], 1);
@@ -1456,8 +1411,7 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_narrow(
               for (int j = 0; j < NV; ++j) {
                 vreg[m][t][j] = vst[size_t(t) * vec + colv[m][j]];
                 float2 kk[VP];
-                unpack16<DSD_FP8_WIDEN_K>(kst[size_t(t) * vec + colv[m][j]],
-                                          static_cast<const T*>(nullptr), kk);
+                unpack16(kst[size_t(t) * vec + colv[m][j]], static_cast<const T*>(nullptr), kk);
 #pragma unroll
                 for (int x = 0; x < VP; ++x) d2 = __ffma2_rn(q[m][j][x], kk[x], d2);
               }
@@ -1500,7 +1454,7 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_narrow(
 #pragma unroll
               for (int j = 0; j < NV; ++j) {
                 float2 vv[VP];
-                unpack16<DSD_FP8_WIDEN_V>(vreg[m][t][j], static_cast<const T*>(nullptr), vv);
+                unpack16(vreg[m][t][j], static_cast<const T*>(nullptr), vv);
 #pragma unroll
                 for (int x = 0; x < VP; ++x) acc[m][j][x] = __ffma2_rn(beta2, vv[x], acc[m][j][x]);
               }
@@ -1515,14 +1469,13 @@ __global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_narrow(
     for (int m = 0; m < SLOTS; ++m) {
       if (!ok[m]) continue;
       float4* pa = reinterpret_cast<float4*>(part_acc + size_t(u) * ept);
-      constexpr float us = unpack_unscale<T, DSD_FP8_WIDEN_V>();   // V values may come scaled
 #pragma unroll
       for (int j = 0; j < NV; ++j) {
 #pragma unroll
         for (int h = 0; h < VE / 4; ++h)
-          pa[(VE / 4) * colv[m][j] + h] =
-              make_float4(acc[m][j][2 * h].x * us, acc[m][j][2 * h].y * us,
-                          acc[m][j][2 * h + 1].x * us, acc[m][j][2 * h + 1].y * us);
+          pa[(VE / 4) * colv[m][j] + h] = make_float4(acc[m][j][2 * h].x, acc[m][j][2 * h].y,
+                                                      acc[m][j][2 * h + 1].x,
+                                                      acc[m][j][2 * h + 1].y);
       }
       const int item = tid + kAttnThreads * m;
       if (item % LP == 0) {

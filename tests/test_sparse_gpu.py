@@ -264,7 +264,7 @@ def test_dense_baseline_matches_dense_cpu(dsd, orc, cfg, tol):
         check_against_oracle(orc, b, ctx.decode_batch(b.queries, b.cand_offsets, b.cand_ids), 1e-4)
 
 
-@pytest.mark.parametrize("batch", [1, 2, 3, 7])
+@pytest.mark.parametrize("batch", [1, 2, 3, 7, 8, 17, 64])
 def test_step_io_split_by_request_range(dsd, orc, batch):
     """Untimed page-table steps upload the second request range's queries and
     download the first range's outputs on a copy stream; every batch size,
