@@ -289,6 +289,7 @@ struct dsd_ctx {
   // the graph)
   cudaStream_t copy_stream = nullptr;
   cudaEvent_t ev_part0_up = nullptr, ev_q1 = nullptr, ev_out0 = nullptr, ev_out0_done = nullptr;
+  cudaEvent_t ev_q0 = nullptr;   // first range's queries landed (plan runs meanwhile)
   // steps queued with dsd_decode_step_begin use per-slot device input/output
   // buffers (slot 0: d_in / d_outputs / plan, slot 1: d_in1 / d_outputs1 /
   // plan1): a slot's upload and result copies run on copy_stream, so they
@@ -623,6 +624,9 @@ void LaunchStep(dsd_ctx* c, const dsdk::StepPlan& plan, const float* d_q, float*
   for (int part = 0; part < nparts; ++part) {
     cudaStream_t st = part == 0 ? c->stream : c->stream2;
     NvtxRange nvtx_part(part == 0 ? "dsd.step.range0" : "dsd.step.range1");
+    // the first range's queries arrive on copy_stream while the plan kernel runs
+    if (split_io && capturing && part == 0)
+      Check(cudaStreamWaitEvent(c->stream, c->ev_q0, cudaEventWaitExternal), "query wait");
     nvtxRangePushA("dsd.score");
     if (c->kv_format == DSD_KV_F32) {
       dsdk::score_kernel<<<2 * c->num_sms, dsdk::kScoreThreads, dsdk::kScoreSmem, st>>>(
@@ -761,21 +765,22 @@ void UploadQueriesSplit(dsd_ctx* c, const float* queries, int batch) {
   const int h0 = SplitRow(batch);
   const bool direct = !c->padded && queries != QPtr(c) && IsPinnedHost(queries);
   if (!direct && queries != QPtr(c)) PadRowsInto(c, QPtr(c), queries, size_t(batch));
-  const unsigned char* src1 =
-      direct ? reinterpret_cast<const unsigned char*>(queries) + size_t(h0) * row
-             : c->h_in + c->in_q_off + size_t(h0) * row;
-  if (direct) {
-    H2D(c, c->d_in, c->h_in, c->in_q_off);
-    H2D(c, c->d_in + c->in_q_off, queries, size_t(h0) * row);
-  } else {
-    H2D(c, c->d_in, c->h_in, c->in_q_off + size_t(h0) * row);
-  }
+  const unsigned char* src =
+      direct ? reinterpret_cast<const unsigned char*>(queries) : c->h_in + c->in_q_off;
+  // header and request list on the context stream (the plan kernel needs only
+  // them), then both query ranges on copy_stream, each completing the event
+  // its range's chain waits for inside the step graph
+  H2D(c, c->d_in, c->h_in, c->in_q_off);
   Check(cudaEventRecord(c->ev_part0_up, c->stream), "event record");
   Check(cudaStreamWaitEvent(c->copy_stream, c->ev_part0_up, 0), "copy stream wait");
-  Check(cudaMemcpyAsync(c->d_in + c->in_q_off + size_t(h0) * row, src1,
-                        size_t(batch - h0) * row, cudaMemcpyHostToDevice, c->copy_stream),
-        "H2D copy");
-  CountH2D(c, size_t(batch - h0) * row);
+  const size_t split = size_t(h0) * row, total = size_t(batch) * row;
+  if (split)
+    Check(cudaMemcpyAsync(c->d_in + c->in_q_off, src, split, cudaMemcpyHostToDevice,
+                          c->copy_stream), "H2D copy");
+  Check(cudaEventRecord(c->ev_q0, c->copy_stream), "event record");
+  Check(cudaMemcpyAsync(c->d_in + c->in_q_off + split, src + split, total - split,
+                        cudaMemcpyHostToDevice, c->copy_stream), "H2D copy");
+  CountH2D(c, total);
   Check(cudaEventRecord(c->ev_q1, c->copy_stream), "event record");
   // the pinned staging is free again once both uploads are done
   Check(cudaEventRecord(c->ev_inputs, c->copy_stream), "event record");
@@ -1094,7 +1099,7 @@ int dsd_ctx_create_ex(int device, const dsd_model_config* config, const dsd_ctx_
       Check(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming), "event");
       Check(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking), "stream");
       Check(cudaStreamCreateWithFlags(&c->up_stream, cudaStreamNonBlocking), "stream");
-      for (cudaEvent_t* e : {&c->ev_part0_up, &c->ev_q1, &c->ev_out0, &c->ev_out0_done,
+      for (cudaEvent_t* e : {&c->ev_part0_up, &c->ev_q1, &c->ev_out0, &c->ev_out0_done, &c->ev_q0,
                              &c->ev_in_ready[0], &c->ev_in_ready[1], &c->ev_graph_done[0],
                              &c->ev_graph_done[1], &c->ev_out_read[0], &c->ev_out_read[1]})
         Check(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "event");
@@ -1232,7 +1237,8 @@ int dsd_ctx_destroy(dsd_ctx* c) {
   if (c->ev_inputs) cudaEventDestroy(c->ev_inputs);
   if (c->ev_fork) cudaEventDestroy(c->ev_fork);
   if (c->ev_join) cudaEventDestroy(c->ev_join);
-  for (cudaEvent_t e : {c->ev_part0_up, c->ev_q1, c->ev_out0, c->ev_out0_done, c->ev_in_ready[0],
+  for (cudaEvent_t e : {c->ev_part0_up, c->ev_q1, c->ev_out0, c->ev_out0_done, c->ev_q0,
+                        c->ev_in_ready[0],
                         c->ev_in_ready[1], c->ev_graph_done[0], c->ev_graph_done[1],
                         c->ev_out_read[0], c->ev_out_read[1]})
     if (e) cudaEventDestroy(e);
