@@ -701,6 +701,16 @@ void LaunchStepGraph(dsd_ctx* c, const float* d_q, float* d_out, bool timed,
   }
   Check(cudaStreamEndCapture(c->stream, &g.graph), "end capture");
   Check(cudaGraphInstantiate(&g.exec, g.graph, 0), "graph instantiate");
+  // one graph per (plan, query, output) pointer set; a caller cycling through
+  // many result buffers keeps at most kMaxGraphs of them (oldest evicted,
+  // after the stream has drained)
+  constexpr size_t kMaxGraphs = 16;
+  if (c->graphs.size() >= kMaxGraphs) {
+    Sync(c);
+    cudaGraphExecDestroy(c->graphs.front().exec);
+    cudaGraphDestroy(c->graphs.front().graph);
+    c->graphs.erase(c->graphs.begin());
+  }
   c->graphs.push_back(g);
   Check(cudaGraphLaunch(g.exec, c->stream), "graph launch");
 }
@@ -724,6 +734,17 @@ bool IsPinnedHost(const void* p) {
     return false;
   }
   return a.type == cudaMemoryTypeHost;
+}
+
+// The device-side address of page-locked, mapped host memory (kernels write
+// it over PCIe), or nullptr when `p` is not such memory.
+float* MappedHostOutput(float* p) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return a.type == cudaMemoryTypeHost ? static_cast<float*>(a.devicePointer) : nullptr;
 }
 
 // The pinned input staging may be rewritten once the previous step's upload
@@ -809,12 +830,17 @@ void RunHostStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int outpu
                  dsd_step_timing* out_timing, bool split_io = false) {
   // queued (begin/end) steps may still be copying results out of d_outputs
   for (cudaEvent_t e : c->ev_out_read) Check(cudaStreamWaitEvent(c->stream, e, 0), "wait");
-  LaunchStepGraph(c, reinterpret_cast<const float*>(c->d_in + c->in_q_off), c->d_outputs,
-                  timing != 0, split_io);
   const size_t out_bytes = size_t(batch) * c->ept * sizeof(float);
+  const bool want_out = output_mode != DSD_OUTPUT_NONE && outputs;
   const bool direct_out =
-      !c->padded && outputs && outputs != c->h_outputs && IsPinnedHost(outputs);
-  if (output_mode != DSD_OUTPUT_NONE && outputs) {
+      !c->padded && want_out && outputs != c->h_outputs && IsPinnedHost(outputs);
+  // A split-I/O step with a mapped, page-locked result buffer has its combine
+  // kernels write the outputs straight into it over PCIe: no output copy,
+  // each range's rows leave as they are computed.
+  float* zero_copy = split_io && direct_out ? MappedHostOutput(outputs) : nullptr;
+  LaunchStepGraph(c, reinterpret_cast<const float*>(c->d_in + c->in_q_off),
+                  zero_copy ? zero_copy : c->d_outputs, timing != 0, split_io);
+  if (want_out && !zero_copy) {
     if (split_io)
       CopyOutputsSplit(c, direct_out ? outputs : c->h_outputs, batch);
     else

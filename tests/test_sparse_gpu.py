@@ -283,6 +283,14 @@ def test_step_io_split_by_request_range(dsd, orc, batch):
         o_pin = torch.zeros(b.queries.shape, dtype=torch.float32, pin_memory=True).numpy()
         ctx.decode_step(reqs, q_pin, output_mode=dsd.OUTPUT_OUTPUTS, out=o_pin)
         assert float(np.abs(o_pin - out).max()) <= 1e-4
+        if batch == 17:
+            # page-locked result buffers are written by the kernels directly (one
+            # step graph per buffer, at most 16 kept): cycle through more than that
+            for i in range(18):
+                o_i = torch.full(b.queries.shape, float("nan"), dtype=torch.float32,
+                                 pin_memory=True).numpy()
+                ctx.decode_step(reqs, q_pin, output_mode=dsd.OUTPUT_OUTPUTS, out=o_i)
+                assert float(np.abs(o_i - out).max()) <= 1e-4, i
         ctx.decode_step_begin(reqs, q_pin)
         ctx.decode_step_begin(reqs, b.queries)
         for _ in range(2):
