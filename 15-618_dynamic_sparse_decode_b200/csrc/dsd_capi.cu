@@ -112,6 +112,7 @@ float Fp8E4m3ToFloat(unsigned char b) {
 // SLOTS items per thread, tokens per stage and dynamic shared memory.
 struct AttnShape {
   int nv = 1, slots = 1, tps = 1, nstages = 0;
+  int ctas = 1;       // narrow attention CTAs per SM
   size_t smem = 0;
 };
 
@@ -128,11 +129,13 @@ AttnShape MakeAttnShape(int num_heads, int head_dim, int page_size, int elem_byt
     const int slots = (items + dsdk::kAttnThreads - 1) / dsdk::kAttnThreads;
     if (slots > 4) Fail(DSD_EINVAL, "num_heads*head_dim is too large for the attention kernel");
     a.slots = slots <= 1 ? 1 : slots <= 2 ? 2 : 4;
-    // 32 KiB stages, as many as fit in ~200 KiB (at most 8)
+    a.ctas = dsdk::attn_narrow_ctas(elem_bytes, a.slots);
+    // 32 KiB stages, as many as fit in ~200 KiB per SM (at most 8), shared by
+    // the format's CTAs per SM
     a.tps = std::max(1, std::min({page_size, 65536 / (2 * ept * elem_bytes),
                                   dsdk::attn_narrow_reg_tokens(a.slots)}));
     const size_t stage = size_t(2) * a.tps * ept * elem_bytes;
-    a.nstages = int(std::max<size_t>(2, std::min<size_t>(8, (200u << 10) / stage)));
+    a.nstages = int(std::max<size_t>(2, std::min<size_t>(8, (size_t(200u / a.ctas) << 10) / stage)));
     a.smem = size_t(a.nstages) * (stage + 16);
     return a;
   }
@@ -652,7 +655,7 @@ void LaunchStep(dsd_ctx* c, const dsdk::StepPlan& plan, const float* d_q, float*
       WithKv(c, [&](auto tag) {
         using T = typename decltype(tag)::type;
         if constexpr (!std::is_same<T, float>::value)
-          LaunchAttnNarrow(c->attn, c->num_sms, st, plan, d_q, static_cast<const T*>(c->k_pool),
+          LaunchAttnNarrow(c->attn, c->attn.ctas * c->num_sms, st, plan, d_q, static_cast<const T*>(c->k_pool),
                            static_cast<const T*>(c->v_pool), c->token_counts, c->d_selected,
                            c->d_part_acc, c->d_part_ml, H, D, P, c->scale, part, nparts);
       });

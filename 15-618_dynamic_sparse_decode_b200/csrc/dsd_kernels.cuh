@@ -1244,8 +1244,19 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// CTAs per SM of the narrow attention kernel: fp8 consumers are bound by
+// their per-element dependent chains (conversions, FMAs, softmax), so two
+// CTAs with half-size rings (18 warps per SM) beat one with a full ring
+// (config 3: attention 0.189 -> 0.148 ms); bf16 keeps one CTA, whose longer
+// stage hold needs the deeper ring (two CTAs measured 0.183 -> 0.219 ms).
+// Threads that serve two heads (SLOTS 2) need more registers than two CTAs
+// leave, so they keep one CTA per SM.
+__host__ __device__ constexpr int attn_narrow_ctas(int elem_bytes, int slots) {
+  return elem_bytes == 1 && slots == 1 ? 2 : 1;
+}
 template <typename T, int NV, int SLOTS>
-__global__ void __launch_bounds__(kAttnBfThreads, 1) attn_kernel_narrow(
+__global__ void __launch_bounds__(kAttnBfThreads, attn_narrow_ctas(int(sizeof(T)), SLOTS))
+    attn_kernel_narrow(
     StepPlan plan, const float* __restrict__ queries, const T* __restrict__ key_pool,
     const T* __restrict__ value_pool, const int* __restrict__ token_counts,
     const int* __restrict__ selected, float* __restrict__ part_acc, float* __restrict__ part_ml,

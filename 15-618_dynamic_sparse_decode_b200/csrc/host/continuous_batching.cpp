@@ -302,6 +302,7 @@ ContinuousBatchStats RunContinuous(const ModelConfig& config,
   std::vector<ActiveDecodeRequest> active;
   active.reserve(static_cast<std::size_t>(options.max_active_requests));
   std::vector<const RequestState*> batch;
+  std::vector<const float*> query_rows;
   std::vector<std::uint8_t> admitted(specs.size(), 0);
 
   if (options.preadmit_prompts) {
@@ -337,7 +338,8 @@ ContinuousBatchStats RunContinuous(const ModelConfig& config,
       rec.request_ids.push_back(a.state.request_id);
       rec.context_tokens.push_back(a.state.context_tokens);
       rec.candidate_page_ids.push_back(a.state.candidate_page_ids);
-      rec.queries.push_back(a.state.query);
+      rec.queries.push_back(a.query_row ? std::vector<float>(a.query_row, a.query_row + ept)
+                                        : a.state.query);
     }
     records.push_back(std::move(rec));
   };
@@ -348,7 +350,8 @@ ContinuousBatchStats RunContinuous(const ModelConfig& config,
     records.pop_front();
   };
   auto finish_oldest = [&]() {
-    const auto out = ctx.FinishStep();
+    // the loop reads only the timings: outputs are copied out for an observer only
+    const auto out = ctx.FinishStep(static_cast<bool>(options.step_observer));
     observe(out);
     const double ms = Ms(step_starts.front(), Clock::now());
     step_starts.pop_front();
@@ -401,7 +404,11 @@ ContinuousBatchStats RunContinuous(const ModelConfig& config,
     }
 
     batch.clear();
-    for (const auto& a : active) batch.push_back(&a.state);
+    query_rows.clear();
+    for (const auto& a : active) {
+      batch.push_back(&a.state);
+      query_rows.push_back(a.query_row);
+    }
     // With device page tables steps are queued asynchronously and up to two
     // are in flight: the host bookkeeping of this step's token appends, its
     // releases and the next step's admission overlap the GPU work (every
@@ -410,7 +417,7 @@ ContinuousBatchStats RunContinuous(const ModelConfig& config,
     ++step_index;
     if (tables) {
       step_starts.push_back(Clock::now());
-      ctx.BeginStep(batch, run_opts);
+      ctx.BeginStep(batch, run_opts, &query_rows);
     } else {
       const auto s0 = Clock::now();
       const auto out = ctx.RunBatch(batch, run_opts);
@@ -446,7 +453,8 @@ ContinuousBatchStats RunContinuous(const ModelConfig& config,
       }
       if (options.precompute_decode_payloads) {
         const float* q = pre_q[a.spec_index].data() + static_cast<std::size_t>(d) * ept;
-        a.state.query.assign(q, q + ept);
+        // queued steps pack it straight from the payload store
+        if (tables) a.query_row = q; else a.state.query.assign(q, q + ept);
       } else {
         a.state.query = DeterministicTokenVector(ept, rid, d + 1, 0);
       }

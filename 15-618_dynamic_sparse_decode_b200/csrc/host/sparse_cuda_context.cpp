@@ -64,12 +64,14 @@ SparseCudaContext::SparseCudaContext(const PagedKvCache& cache, const ModelConfi
 
 // Copies every request's query into the pinned step staging; large batches
 // are split over the pack pool (the host copy is memory-bound).
-void SparseCudaContext::PackQueries(const std::vector<const RequestState*>& requests) {
+void SparseCudaContext::PackQueries(const std::vector<const RequestState*>& requests,
+                                    const std::vector<const float*>* query_rows) {
   const int B = static_cast<int>(requests.size());
   const int ept = elements_per_token_;
   auto copy_one = [&](int r) {
-    const auto& q = requests[static_cast<std::size_t>(r)]->query;
-    std::copy(q.begin(), q.end(), host_queries_ + static_cast<std::size_t>(r) * ept);
+    const float* row = query_rows ? (*query_rows)[static_cast<std::size_t>(r)] : nullptr;
+    if (row == nullptr) row = requests[static_cast<std::size_t>(r)]->query.data();
+    std::copy(row, row + ept, host_queries_ + static_cast<std::size_t>(r) * ept);
   };
   if (static_cast<std::size_t>(B) * ept < (std::size_t(1) << 17)) {
     for (int r = 0; r < B; ++r) copy_one(r);
@@ -217,6 +219,14 @@ SparseBatchCudaResult SparseCudaContext::Run(const std::vector<const RequestStat
 
 void SparseCudaContext::BeginStep(const std::vector<const RequestState*>& requests,
                                   SparseRunBatchOptions options) {
+  BeginStep(requests, options, nullptr);
+}
+
+void SparseCudaContext::BeginStep(const std::vector<const RequestState*>& requests,
+                                  SparseRunBatchOptions options,
+                                  const std::vector<const float*>* query_rows) {
+  if (query_rows && query_rows->size() != requests.size())
+    throw std::invalid_argument("one query row per request");
   if (!HasRequestTables())
     throw std::invalid_argument("context was created without device request page tables");
   if (pending_.size() >= 2) throw std::invalid_argument("two steps are already pending");
@@ -234,7 +244,8 @@ void SparseCudaContext::BeginStep(const std::vector<const RequestState*>& reques
   for (int r = 0; r < B; ++r) {
     const RequestState* q = requests[static_cast<std::size_t>(r)];
     if (!q) throw std::invalid_argument("request pointer must be non-null");
-    if (static_cast<int>(q->query.size()) != ept)
+    const bool row = query_rows && (*query_rows)[static_cast<std::size_t>(r)] != nullptr;
+    if (!row && static_cast<int>(q->query.size()) != ept)
       throw std::invalid_argument("query length does not match model config");
     ps.request_ids.push_back(q->request_id);
     if (debug) ps.candidates.push_back(q->candidate_page_ids);
@@ -248,7 +259,7 @@ void SparseCudaContext::BeginStep(const std::vector<const RequestState*>& reques
   if (ps.sel_off.back() > max_total_selected_pages_)
     throw std::invalid_argument("selected page count exceeds sparse CUDA context capacity");
   ThrowIf(dsd_step_staging_wait(ctx_));   // the staging may still feed the previous step
-  PackQueries(requests);
+  PackQueries(requests, query_rows);
   ps.prep_ms =
       std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   const int mode = options.output_mode == SparseBatchOutputMode::kNoOutputs ? DSD_OUTPUT_NONE
@@ -259,7 +270,9 @@ void SparseCudaContext::BeginStep(const std::vector<const RequestState*>& reques
   pending_.push_back(std::move(ps));
 }
 
-SparseBatchCudaResult SparseCudaContext::FinishStep() {
+SparseBatchCudaResult SparseCudaContext::FinishStep() { return FinishStep(true); }
+
+SparseBatchCudaResult SparseCudaContext::FinishStep(bool copy_outputs) {
   if (pending_.empty()) throw std::invalid_argument("no step is pending");
   PendingStep ps = std::move(pending_.front());
   pending_.erase(pending_.begin());
@@ -272,7 +285,8 @@ SparseBatchCudaResult SparseCudaContext::FinishStep() {
   finish_outputs_.resize(static_cast<std::size_t>(B) * ept);
   dsd_step_timing st{};
   const auto t0 = std::chrono::steady_clock::now();
-  ThrowIf(dsd_decode_step_end(ctx_, finish_outputs_.data(), scores_.data(), selected_.data(), &st));
+  ThrowIf(dsd_decode_step_end(ctx_, copy_outputs ? finish_outputs_.data() : nullptr,
+                              scores_.data(), selected_.data(), &st));
   SparseBatchCudaResult result;
   if (timed) {
     result.aggregate_timings.page_scoring_ms = st.score_ms;
@@ -299,8 +313,9 @@ SparseBatchCudaResult SparseCudaContext::FinishStep() {
       one.selected_page_ids.assign(selected_.begin() + ps.sel_off[static_cast<std::size_t>(r)],
                                    selected_.begin() + ps.sel_off[static_cast<std::size_t>(r) + 1]);
     }
-    one.output.output.assign(finish_outputs_.begin() + static_cast<std::ptrdiff_t>(r) * ept,
-                             finish_outputs_.begin() + static_cast<std::ptrdiff_t>(r + 1) * ept);
+    if (copy_outputs)
+      one.output.output.assign(finish_outputs_.begin() + static_cast<std::ptrdiff_t>(r) * ept,
+                               finish_outputs_.begin() + static_cast<std::ptrdiff_t>(r + 1) * ept);
     result.per_request.push_back(std::move(one));
   }
   return result;

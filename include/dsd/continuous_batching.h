@@ -30,6 +30,9 @@ struct ActiveDecodeRequest {
   int remaining_decode_steps = 0;
   int decode_step_index = 0;
   std::size_t spec_index = 0;
+  // This build: when non-null, the step's query (a precomputed payload row)
+  // used in place of state.query
+  const float* query_row = nullptr;
 };
 
 enum class ContinuousPromptAdmissionMode { kCpuCache, kDirectGpuUpload, kSyntheticGpuPrefill };

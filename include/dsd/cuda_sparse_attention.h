@@ -87,6 +87,15 @@ class SparseCudaContext {
   // as needed, so they may change after BeginStep returns.
   void BeginStep(const std::vector<const RequestState*>& requests, SparseRunBatchOptions options);
   SparseBatchCudaResult FinishStep();
+  // This build: BeginStep whose request r takes its query from query_rows[r]
+  // when that is non-null (num_heads*head_dim floats, read before the call
+  // returns) instead of requests[r]->query -- the serving loop's precomputed
+  // queries go straight into the pinned staging.  FinishStep(false) leaves
+  // per_request[r].output empty: the outputs still come back to the host
+  // staging, but are not copied out for a caller that does not read them.
+  void BeginStep(const std::vector<const RequestState*>& requests, SparseRunBatchOptions options,
+                 const std::vector<const float*>* query_rows);
+  SparseBatchCudaResult FinishStep(bool copy_outputs);
 
   void SyncPageFromCache(const PagedKvCache& cache, PageId page_id);
   void SyncPagesFromCache(const PagedKvCache& cache, const std::vector<PageId>& page_ids);
@@ -148,7 +157,8 @@ class SparseCudaContext {
   };
   std::vector<PendingStep> pending_;
   std::unique_ptr<detail::WorkerPool> pack_pool_;   // parallel query packing
-  void PackQueries(const std::vector<const RequestState*>& requests);
+  void PackQueries(const std::vector<const RequestState*>& requests,
+                   const std::vector<const float*>* query_rows = nullptr);
 };
 
 SparseDecodeResult SparseDecodeCuda(const PagedKvCache& cache, const RequestState& request,
