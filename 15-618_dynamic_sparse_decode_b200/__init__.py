@@ -89,6 +89,7 @@ SIGNATURES = [
                                         ctypes.POINTER(StepTiming)]),
     ("dsd_request_set_pages", ctypes.c_int, [_VP, ctypes.c_int, _I32P, ctypes.c_int]),
     ("dsd_request_append_pages", ctypes.c_int, [_VP, ctypes.c_int, _I32P, ctypes.c_int]),
+    ("dsd_request_append_pages_multi", ctypes.c_int, [_VP, _I32P, _I32P, ctypes.c_int]),
     ("dsd_request_release", ctypes.c_int, [_VP, ctypes.c_int, ctypes.c_int]),
     ("dsd_request_num_pages", ctypes.c_int, [_VP, ctypes.c_int]),
     ("dsd_decode_step", ctypes.c_int, [_VP, _I32P, ctypes.c_int, _F32P, ctypes.c_int,
@@ -352,6 +353,13 @@ class SparseDecodeContext:
     def append_request_pages(self, request_id, page_ids):
         ids = _i32(page_ids)
         _check(self.lib.dsd_request_append_pages(self.h, request_id, _ip(ids), len(ids)))
+
+    def append_request_pages_multi(self, request_ids, page_ids):
+        """page_ids[i] joins request_ids[i]'s page table, in order, one upload."""
+        reqs, ids = _i32(request_ids), _i32(page_ids)
+        if len(reqs) != len(ids):
+            raise InvalidArgument(int(DSD_EINVAL), "one request id per page")
+        _check(self.lib.dsd_request_append_pages_multi(self.h, _ip(reqs), _ip(ids), len(ids)))
 
     def release_request(self, request_id, free_pages=True):
         _check(self.lib.dsd_request_release(self.h, request_id, int(free_pages)))

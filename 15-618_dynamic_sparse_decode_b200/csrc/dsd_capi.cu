@@ -1781,6 +1781,34 @@ int dsd_request_set_pages(dsd_ctx* c, int request_id, const int32_t* page_ids, i
   });
 }
 
+int dsd_request_append_pages_multi(dsd_ctx* c, const int32_t* request_ids,
+                                   const int32_t* page_ids, int n) {
+  return Guard([&]() {
+    NvtxRange nvtx("dsd_request_append_pages_multi");
+    if (!c) Fail(DSD_EINVAL, "null context");
+    RequireTables(c);
+    if (n <= 0) return;
+    if (!request_ids || !page_ids) Fail(DSD_EINVAL, "null argument");
+    for (int i = 0; i < n; ++i) ValidatePage(c, page_ids[i]);
+    SetDevice(c);
+    // check every request's room first, so a refused call changes nothing
+    std::unordered_map<int, int> added;
+    for (int i = 0; i < n; ++i) {
+      const int slot = SlotOf(c, request_ids[i], true);
+      if (int(c->slot_pages[slot].size()) + ++added[slot] > c->opt.max_pages_per_request)
+        Fail(DSD_EINVAL, "page count exceeds the request page table");
+    }
+    std::vector<int> triples;
+    for (int i = 0; i < n; ++i) {
+      const int slot = SlotOf(c, request_ids[i], false);
+      auto& pages = c->slot_pages[slot];
+      triples.insert(triples.end(), {slot, int(pages.size()), page_ids[i]});
+      pages.push_back(page_ids[i]);
+    }
+    UploadTableEntries(c, triples, {});
+  });
+}
+
 int dsd_request_append_pages(dsd_ctx* c, int request_id, const int32_t* page_ids, int n) {
   return Guard([&]() {
     NvtxRange nvtx("dsd_request_append_pages");

@@ -369,6 +369,8 @@ ContinuousBatchStats RunContinuous(const ModelConfig& config,
       std::min<unsigned>(8, std::max(1u, std::thread::hardware_concurrency())) - 1);
   detail::WorkerPool pool(pool_threads);
   std::vector<std::pair<int, PageId>> new_pages;
+  std::vector<int> np_reqs;
+  std::vector<PageId> np_pages;
   while (next < specs.size() || !pending.empty() || !active.empty()) {
     if (active.empty() && pending.empty() && next < specs.size() &&
         step < specs[next].arrival_step)
@@ -443,7 +445,7 @@ ContinuousBatchStats RunContinuous(const ModelConfig& config,
       gen_k.resize(active.size());
       gen_v.resize(active.size());
     }
-    pool.ParallelFor(static_cast<int>(active.size()), [&](int i) {
+    auto next_payload = [&](int i) {
       auto& a = active[static_cast<std::size_t>(i)];
       const int rid = a.state.request_id;
       const int d = a.decode_step_index;
@@ -458,7 +460,13 @@ ContinuousBatchStats RunContinuous(const ModelConfig& config,
       } else {
         a.state.query = DeterministicTokenVector(ept, rid, d + 1, 0);
       }
-    });
+    };
+    // generation is spread over the worker pool; pointing at precomputed rows
+    // is not worth a dispatch
+    if (gen_kv || !options.precompute_decode_payloads)
+      pool.ParallelFor(static_cast<int>(active.size()), next_payload);
+    else
+      for (int i = 0; i < static_cast<int>(active.size()); ++i) next_payload(i);
     for (std::size_t ai = 0; ai < active.size(); ++ai) {
       auto& a = active[ai];
       const int rid = a.state.request_id;
@@ -520,8 +528,15 @@ ContinuousBatchStats RunContinuous(const ModelConfig& config,
       } else {
         ctx.SyncAppendedTokens(cache, results);
       }
-      if (tables)
-        for (const auto& np : new_pages) ctx.AppendRequestPages(np.first, {np.second});
+      if (tables && !new_pages.empty()) {
+        np_reqs.clear();
+        np_pages.clear();
+        for (const auto& np : new_pages) {
+          np_reqs.push_back(np.first);
+          np_pages.push_back(np.second);
+        }
+        ctx.AppendRequestPages(np_reqs, np_pages);   // one upload for all of them
+      }
     }
     stats.append_sync_ms += Ms(a0, Clock::now());
     if (tables && ctx.PendingSteps() == 2) finish_oldest();

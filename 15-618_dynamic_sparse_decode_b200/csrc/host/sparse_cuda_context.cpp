@@ -380,6 +380,13 @@ void SparseCudaContext::AppendRequestPages(int request_id, const std::vector<Pag
   ThrowIf(dsd_request_append_pages(ctx_, request_id, page_ids.data(),
                                    static_cast<int>(page_ids.size())));
 }
+void SparseCudaContext::AppendRequestPages(const std::vector<int>& request_ids,
+                                           const std::vector<PageId>& page_ids) {
+  if (request_ids.size() != page_ids.size())
+    throw std::invalid_argument("one request id per page");
+  ThrowIf(dsd_request_append_pages_multi(ctx_, request_ids.data(), page_ids.data(),
+                                         static_cast<int>(page_ids.size())));
+}
 void SparseCudaContext::ReleaseRequestPages(int request_id, bool free_pages) {
   ThrowIf(dsd_request_release(ctx_, request_id, free_pages ? 1 : 0));
 }

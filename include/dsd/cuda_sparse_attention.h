@@ -121,6 +121,8 @@ class SparseCudaContext {
   // device request page tables
   void SetRequestPages(int request_id, const std::vector<PageId>& page_ids);
   void AppendRequestPages(int request_id, const std::vector<PageId>& page_ids);
+  // one upload for new pages of several requests (request_ids[i] gets page_ids[i])
+  void AppendRequestPages(const std::vector<int>& request_ids, const std::vector<PageId>& page_ids);
   void ReleaseRequestPages(int request_id, bool free_pages);
   bool HasRequestTables() const { return max_requests_ > 0; }
   int PendingSteps() const { return static_cast<int>(pending_.size()); }

@@ -215,6 +215,11 @@ int dsd_decode_batch(dsd_ctx* ctx, int batch, const float* queries, const int32_
  * (and frees its pages on the device when free_pages != 0). */
 int dsd_request_set_pages(dsd_ctx* ctx, int request_id, const int32_t* page_ids, int n);
 int dsd_request_append_pages(dsd_ctx* ctx, int request_id, const int32_t* page_ids, int n);
+/* Appends page_ids[i] to the page table of request_ids[i], i = 0..n-1 in
+ * order, with one upload for all of them (the continuous step's new pages of
+ * many requests; per-request equivalent: dsd_request_append_pages). */
+int dsd_request_append_pages_multi(dsd_ctx* ctx, const int32_t* request_ids,
+                                   const int32_t* page_ids, int n);
 int dsd_request_release(dsd_ctx* ctx, int request_id, int free_pages);
 int dsd_request_num_pages(dsd_ctx* ctx, int request_id);
 
