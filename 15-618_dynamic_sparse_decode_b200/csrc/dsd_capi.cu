@@ -1791,16 +1791,23 @@ int dsd_request_append_pages_multi(dsd_ctx* c, const int32_t* request_ids,
     if (!request_ids || !page_ids) Fail(DSD_EINVAL, "null argument");
     for (int i = 0; i < n; ++i) ValidatePage(c, page_ids[i]);
     SetDevice(c);
-    // check every request's room first, so a refused call changes nothing
+    // check every request's room (and free slots for new requests) first, so a
+    // refused call changes nothing
     std::unordered_map<int, int> added;
+    int new_requests = 0;
     for (int i = 0; i < n; ++i) {
-      const int slot = SlotOf(c, request_ids[i], true);
-      if (int(c->slot_pages[slot].size()) + ++added[slot] > c->opt.max_pages_per_request)
+      const auto it = c->slot_of.find(request_ids[i]);
+      const int have = it == c->slot_of.end() ? 0 : int(c->slot_pages[it->second].size());
+      int& a = added[request_ids[i]];
+      if (it == c->slot_of.end() && a == 0) ++new_requests;
+      if (have + ++a > c->opt.max_pages_per_request)
         Fail(DSD_EINVAL, "page count exceeds the request page table");
     }
+    if (new_requests > int(c->free_slots.size()))
+      Fail(DSD_ENOMEM, "no free request page-table slot");
     std::vector<int> triples;
     for (int i = 0; i < n; ++i) {
-      const int slot = SlotOf(c, request_ids[i], false);
+      const int slot = SlotOf(c, request_ids[i], true);
       auto& pages = c->slot_pages[slot];
       triples.insert(triples.end(), {slot, int(pages.size()), page_ids[i]});
       pages.push_back(page_ids[i]);

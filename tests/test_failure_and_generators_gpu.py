@@ -144,3 +144,20 @@ def test_upload_append_download_round_trip(dsd, H, D):
         for off in (3, 4):
             summ = o.running_mean_append(summ, nk[off - 3], off)
         assert np.array_equal(s9.view(np.uint32), summ.view(np.uint32))
+
+
+def test_append_pages_multi_is_all_or_nothing(dsd):
+    """dsd_request_append_pages_multi: pages join their requests' tables in
+    order; a call that would overflow one table is refused before any change."""
+    with small_ctx(dsd, cap=16) as ctx:   # 4 page-table slots of 16 pages
+        ctx.set_request_pages(7, [0, 1])
+        ctx.append_request_pages_multi([7, 9, 7], [2, 3, 4])
+        assert ctx.request_num_pages(7) == 4 and ctx.request_num_pages(9) == 1
+        with pytest.raises(dsd.InvalidArgument):
+            ctx.append_request_pages_multi([9] * 15 + [11], list(range(16)))
+        assert ctx.request_num_pages(9) == 1 and ctx.request_num_pages(11) == 0
+        # no slot was taken by the refused call: two of the four are still free
+        ctx.set_request_pages(12, [5])
+        ctx.set_request_pages(13, [6])
+        with pytest.raises(dsd.DsdError):
+            ctx.set_request_pages(14, [8])
