@@ -154,7 +154,8 @@ def test_append_pages_multi_is_all_or_nothing(dsd):
         ctx.append_request_pages_multi([7, 9, 7], [2, 3, 4])
         assert ctx.request_num_pages(7) == 4 and ctx.request_num_pages(9) == 1
         with pytest.raises(dsd.InvalidArgument):
-            ctx.append_request_pages_multi([9] * 15 + [11], list(range(16)))
+            # request 9 holds 1 page: 16 more would exceed its 16-entry table
+            ctx.append_request_pages_multi([11] + [9] * 16, [0] + list(range(16)))
         assert ctx.request_num_pages(9) == 1 and ctx.request_num_pages(11) == 0
         # no slot was taken by the refused call: two of the four are still free
         ctx.set_request_pages(12, [5])
