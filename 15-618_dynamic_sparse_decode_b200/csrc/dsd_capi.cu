@@ -843,6 +843,7 @@ void RunHostStep(dsd_ctx* c, int batch, int total_cand, int total_sel, int outpu
   float* zero_copy = split_io && direct_out ? MappedHostOutput(outputs) : nullptr;
   LaunchStepGraph(c, reinterpret_cast<const float*>(c->d_in + c->in_q_off),
                   zero_copy ? zero_copy : c->d_outputs, timing != 0, split_io);
+  if (zero_copy) CountD2H(c, out_bytes);   // written over PCIe by the kernels themselves
   if (want_out && !zero_copy) {
     if (split_io)
       CopyOutputsSplit(c, direct_out ? outputs : c->h_outputs, batch);

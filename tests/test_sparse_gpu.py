@@ -281,8 +281,12 @@ def test_step_io_split_by_request_range(dsd, orc, batch):
         q_pin = torch.empty(b.queries.shape, dtype=torch.float32, pin_memory=True).numpy()
         q_pin[:] = b.queries
         o_pin = torch.zeros(b.queries.shape, dtype=torch.float32, pin_memory=True).numpy()
+        ctx.reset_transfer_stats()
         ctx.decode_step(reqs, q_pin, output_mode=dsd.OUTPUT_OUTPUTS, out=o_pin)
         assert float(np.abs(o_pin - out).max()) <= 1e-4
+        # the outputs reach the host whether copied or written by the kernels
+        st = ctx.transfer_stats()
+        assert st["d2h_bytes"] >= o_pin.nbytes and st["h2d_bytes"] >= q_pin.nbytes
         if batch == 17:
             # page-locked result buffers are written by the kernels directly (one
             # step graph per buffer, at most 16 kept): cycle through more than that
