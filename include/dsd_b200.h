@@ -225,7 +225,11 @@ int dsd_request_num_pages(dsd_ctx* ctx, int request_id);
 
 /* One decode step over requests whose candidates are their device page
  * tables (the continuous-batching step).  The CSR offsets are a device prefix
- * sum; only the queries cross H2D and the outputs D2H. */
+ * sum; only the queries cross H2D and the outputs D2H.  With at least two
+ * requests, a page-locked `outputs` buffer (cudaHostAlloc / pinned memory) is
+ * written by the kernels directly over PCIe; any other buffer is filled from
+ * the context's staging.  Either way the call returns with the outputs in
+ * place.  A context keeps a step graph per such buffer (at most 16). */
 int dsd_decode_step(dsd_ctx* ctx, const int32_t* request_ids, int batch, const float* queries,
                     int output_mode, int timing, float* outputs, float* scores,
                     int32_t* selected, dsd_step_timing* out_timing);
